@@ -1,0 +1,617 @@
+// C ABI of the FlashHead decode-step head (declared in include/flashhead.h).
+//
+// Host code only validates arguments, lays out the caller's workspace and
+// launches kernels on the caller's stream: it never allocates, synchronises
+// or reads device memory, so every entry point can be captured in a CUDA
+// graph. Kernels after the first of a call are launched with programmatic
+// dependent launch so that their CTAs are resident before their predecessor
+// finishes.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "../../include/flashhead.h"
+#include "fh_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(FH_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define FH_CHECK_LAUNCH(expr, what)           \
+  do {                                        \
+    cudaError_t _e = (expr);                  \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+template <typename Kern, typename... Args>
+cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// k_select keeps every key of a row in dynamic shared memory; raise its
+// limit once per device.
+std::mutex g_attr_mutex;
+bool g_select_attr_done[128];
+
+cudaError_t prepare_select() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!g_select_attr_done[dev]) {
+    e = cudaFuncSetAttribute(fh::k_select, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(fh::kSelMaxItems * sizeof(unsigned long long)));
+    if (e != cudaSuccess) return e;
+    g_select_attr_done[dev] = true;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace
+
+struct fh_head {
+  fh_head_desc d;
+};
+
+// ---------------------------------------------------------------------------
+// Workspace layout for `rows` hidden states.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct Workspace {
+  float *scores;                // [rows, score_stride]
+  int score_stride;
+  int32_t *probes;              // [rows, p]
+  unsigned long long *packed;   // [rows]
+  unsigned *counter;            // [1]
+  size_t bytes;
+};
+
+Workspace layout(const fh_head_desc &d, int rows, void *base) {
+  Workspace w;
+  char *p = reinterpret_cast<char *>(base);
+  size_t off = 0;
+  w.score_stride = (int)round_up((size_t)d.n_clusters, 64);
+  w.scores = reinterpret_cast<float *>(p + off);
+  off = round_up(off + (size_t)rows * w.score_stride * sizeof(float), 256);
+  w.probes = reinterpret_cast<int32_t *>(p + off);
+  off = round_up(off + (size_t)rows * d.n_probes * sizeof(int32_t), 256);
+  w.packed = reinterpret_cast<unsigned long long *>(p + off);
+  off = round_up(off + (size_t)rows * sizeof(unsigned long long), 256);
+  w.counter = reinterpret_cast<unsigned *>(p + off);
+  off = round_up(off + 256, 256);
+  w.bytes = off;
+  return w;
+}
+
+int check_call(const fh_head *h, const void *hidden, int rows, const void *out, void *ws,
+               size_t ws_bytes) {
+  if (!h) return fail(FH_ERR_INVALID_ARGUMENT, "null head");
+  if (rows < 0) return fail(FH_ERR_INVALID_ARGUMENT, "rows=%d < 0", rows);
+  if (rows == 0) return FH_OK;
+  if (!hidden || !out) return fail(FH_ERR_INVALID_ARGUMENT, "null hidden/output pointer");
+  if (!aligned16(hidden))
+    return fail(FH_ERR_INVALID_ARGUMENT, "hidden states must be 16-byte aligned");
+  if (!ws) return fail(FH_ERR_WORKSPACE, "null workspace");
+  const size_t need = layout(h->d, rows, nullptr).bytes;
+  if (ws_bytes < need)
+    return fail(FH_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed for %d rows", ws_bytes,
+                need, rows);
+  if (!aligned16(ws)) return fail(FH_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  return FH_OK;
+}
+
+fh::RngKey rng_key(uint64_t seed, uint64_t offset) {
+  fh::RngKey k;
+  k.k0 = (uint32_t)seed;
+  k.k1 = (uint32_t)(seed >> 32);
+  k.off_lo = (uint32_t)offset;
+  k.off_hi = (uint32_t)(offset >> 32);
+  return k;
+}
+
+// ---------------------------------------------------------------------------
+// Stage-1 scores launch: picks rows per CTA and clusters per warp.
+// ---------------------------------------------------------------------------
+template <typename HT, typename WT>
+cudaError_t launch_scores_t(const fh::ScoresArgs &a, cudaStream_t s) {
+  const int rows = a.rows;
+  auto go = [&](auto kern, int rows_per, int cpw) {
+    const int warps = (a.K + cpw - 1) / cpw;
+    const int ctas = (warps + 7) / 8;
+    dim3 grid(ctas, (rows + rows_per - 1) / rows_per);
+    return launch(kern, grid, dim3(256), 0, s, false, a);
+  };
+  if (rows == 1) return go(fh::k_scores<HT, WT, 1, 1, 4>, 1, 1);
+  if (rows == 2) return go(fh::k_scores<HT, WT, 2, 2, 2>, 2, 2);
+  if (rows <= 4) return go(fh::k_scores<HT, WT, 4, 2, 2>, 4, 2);
+  return go(fh::k_scores<HT, WT, 8, 4, 1>, 8, 4);
+}
+
+cudaError_t launch_scores(int hdt, int wdt, const fh::ScoresArgs &a, cudaStream_t s) {
+  if (hdt == FH_BF16) {
+    if (wdt == FH_FP8_E4M3) return launch_scores_t<__nv_bfloat16, __nv_fp8_e4m3>(a, s);
+    return launch_scores_t<__nv_bfloat16, __nv_bfloat16>(a, s);
+  }
+  if (wdt == FH_FP8_E4M3) return launch_scores_t<__half, __nv_fp8_e4m3>(a, s);
+  return launch_scores_t<__half, __half>(a, s);
+}
+
+template <typename HT, typename IdxT, int MODE>
+cudaError_t launch_stage2_t(const fh::Stage2Args &a, int items, cudaStream_t s, bool pdl) {
+  constexpr int U = 8;
+  return launch(fh::k_stage2<HT, IdxT, MODE, U>, dim3(items), dim3(32 * a.cap), 0, s, pdl, a);
+}
+
+template <typename IdxT, int MODE>
+cudaError_t launch_stage2(int hdt, const fh::Stage2Args &a, int items, cudaStream_t s, bool pdl) {
+  if (hdt == FH_BF16) return launch_stage2_t<__nv_bfloat16, IdxT, MODE>(a, items, s, pdl);
+  return launch_stage2_t<__half, IdxT, MODE>(a, items, s, pdl);
+}
+
+fh::Stage2Args stage2_args(const fh_head_desc &d, const void *hidden, int rows) {
+  fh::Stage2Args a;
+  memset(&a, 0, sizeof(a));
+  a.hidden = hidden;
+  a.rows = rows;
+  a.D = d.hidden;
+  a.w_perm = d.w_perm;
+  a.K = d.n_clusters;
+  a.cap = d.cluster_size;
+  a.vocab_map = d.vocab_map;
+  a.special_slots = d.special_slots;
+  a.n_special = d.n_special;
+  a.cluster_base = d.cluster_base;
+  a.temperature = 1.f;
+  return a;
+}
+
+fh::ScoresArgs scores_args(const fh_head_desc &d, const void *hidden, int rows, bool sample,
+                           float temperature, uint64_t seed, uint64_t offset) {
+  fh::ScoresArgs a;
+  memset(&a, 0, sizeof(a));
+  a.hidden = hidden;
+  a.rows = rows;
+  a.D = d.hidden;
+  a.w = sample ? d.centroid_w : d.cluster_w;
+  a.scale = sample ? d.centroid_scale : d.cluster_scale;
+  a.K = d.n_clusters;
+  a.do_sample = sample ? 1 : 0;
+  a.temperature = temperature;
+  a.rng = rng_key(seed, offset);
+  a.cluster_base = d.cluster_base;
+  return a;
+}
+
+fh::SelectArgs select_dense_args(const fh_head_desc &d, const float *scores, int stride,
+                                 int rows) {
+  fh::SelectArgs a;
+  memset(&a, 0, sizeof(a));
+  a.scores = scores;
+  a.score_stride = stride;
+  a.rows = rows;
+  a.n_items = d.n_clusters;
+  a.p = d.n_probes;
+  a.wait_prior = 1;
+  return a;
+}
+
+int check_sampling(const fh_head *h, float temperature) {
+  if (!h->d.centroid_w)
+    return fail(FH_ERR_UNSUPPORTED, "sampling needs the raw centroid matrix (centroid_w)");
+  if (!(temperature > 0.f) || !std::isfinite(temperature))
+    return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite (got %g)",
+                (double)temperature);
+  return FH_OK;
+}
+
+// Stage 1 + selection for the local head. Writes probes (local or global
+// ids) and/or signed candidate words; zeroes packed/counter for stage 2.
+int run_stage1(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+               uint64_t seed, uint64_t offset, const Workspace &w, float *scores_out,
+               int32_t *probes_out, long long *cand_out, int id_base, cudaStream_t s) {
+  const fh_head_desc &d = h->d;
+  fh::ScoresArgs sa = scores_args(d, hidden, rows, sample, temperature, seed, offset);
+  sa.scores = scores_out ? scores_out : w.scores;
+  sa.score_stride = scores_out ? d.n_clusters : w.score_stride;
+  sa.packed = w.packed;
+  sa.counter = w.counter;
+  sa.n_packed = rows;
+  const int wdt = sample ? d.sample_dtype : d.score_dtype;
+  FH_CHECK_LAUNCH(launch_scores(d.weight_dtype, wdt, sa, s), "stage-1 scores launch");
+  FH_CHECK_LAUNCH(prepare_select(), "select kernel attribute");
+  fh::SelectArgs se = select_dense_args(d, sa.scores, sa.score_stride, rows);
+  se.probes = probes_out;
+  se.cand_out = cand_out;
+  se.id_base = id_base;
+  const size_t smem = (size_t)d.n_clusters * sizeof(unsigned long long);
+  FH_CHECK_LAUNCH(launch(fh::k_select, dim3(rows), dim3(fh::kSelThreads), smem, s, true, se),
+                  "probe selection launch");
+  return FH_OK;
+}
+
+int validate_desc(const fh_head_desc *d) {
+  if (!d) return fail(FH_ERR_INVALID_ARGUMENT, "null descriptor");
+  if (d->hidden <= 0 || d->hidden % 16 != 0)
+    return fail(FH_ERR_INVALID_ARGUMENT, "hidden=%d must be a positive multiple of 16", d->hidden);
+  if (d->n_clusters <= 0 || d->n_clusters > fh::kSelMaxItems)
+    return fail(FH_ERR_INVALID_ARGUMENT, "n_clusters=%d outside 1..%d", d->n_clusters,
+                fh::kSelMaxItems);
+  if (d->cluster_size < 1 || d->cluster_size > 32)
+    return fail(FH_ERR_INVALID_ARGUMENT, "cluster_size=%d outside 1..32", d->cluster_size);
+  if (d->n_probes < 1 || d->n_probes > d->n_clusters)
+    return fail(FH_ERR_INVALID_ARGUMENT, "n_probes=%d outside 1..n_clusters=%d", d->n_probes,
+                d->n_clusters);
+  if (d->weight_dtype != FH_BF16 && d->weight_dtype != FH_FP16)
+    return fail(FH_ERR_INVALID_ARGUMENT, "weight_dtype must be FH_BF16 or FH_FP16");
+  if (d->score_dtype != FH_FP8_E4M3 && d->score_dtype != d->weight_dtype)
+    return fail(FH_ERR_INVALID_ARGUMENT, "score_dtype must be FH_FP8_E4M3 or weight_dtype");
+  if (d->centroid_w && d->sample_dtype != FH_FP8_E4M3 && d->sample_dtype != d->weight_dtype)
+    return fail(FH_ERR_INVALID_ARGUMENT, "sample_dtype must be FH_FP8_E4M3 or weight_dtype");
+  if (!d->w_perm || !d->vocab_map || !d->cluster_w)
+    return fail(FH_ERR_INVALID_ARGUMENT, "w_perm, vocab_map and cluster_w are required");
+  if (!aligned16(d->w_perm) || !aligned16(d->cluster_w) ||
+      (d->centroid_w && !aligned16(d->centroid_w)))
+    return fail(FH_ERR_INVALID_ARGUMENT, "weight matrices must be 16-byte aligned");
+  if ((d->score_dtype == FH_FP8_E4M3) != (d->cluster_scale != nullptr))
+    return fail(FH_ERR_INVALID_ARGUMENT, "cluster_scale is required exactly for fp8 cluster_w");
+  if (d->centroid_w && (d->sample_dtype == FH_FP8_E4M3) != (d->centroid_scale != nullptr))
+    return fail(FH_ERR_INVALID_ARGUMENT, "centroid_scale is required exactly for fp8 centroid_w");
+  if (d->n_special < 0 || (d->n_special > 0 && !d->special_slots))
+    return fail(FH_ERR_INVALID_ARGUMENT, "n_special=%d with null special_slots", d->n_special);
+  if (d->cluster_base < 0) return fail(FH_ERR_INVALID_ARGUMENT, "cluster_base < 0");
+  return FH_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// Exported functions
+// ===========================================================================
+extern "C" {
+
+FH_API int fh_version(void) { return 1; }
+
+FH_API const char *fh_last_error(void) { return g_last_error.c_str(); }
+
+FH_API int fh_head_create(const fh_head_desc *desc, fh_head **out) {
+  if (!out) return fail(FH_ERR_INVALID_ARGUMENT, "null output handle pointer");
+  *out = nullptr;
+  const int st = validate_desc(desc);
+  if (st != FH_OK) return st;
+  fh_head *h = new (std::nothrow) fh_head;
+  if (!h) return fail(FH_ERR_INVALID_ARGUMENT, "out of host memory");
+  h->d = *desc;
+  *out = h;
+  return FH_OK;
+}
+
+FH_API int fh_head_destroy(fh_head *head) {
+  delete head;
+  return FH_OK;
+}
+
+FH_API size_t fh_workspace_bytes(const fh_head *head, int rows) {
+  if (!head || rows < 0) return 0;
+  return layout(head->d, rows, nullptr).bytes;
+}
+
+FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
+                             int64_t *out_ids, void *workspace, size_t workspace_bytes,
+                             fh_stream_t stream) {
+  int st = check_call(head, hidden, rows, out_ids, workspace, workspace_bytes);
+  if (st != FH_OK || rows == 0) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = layout(head->d, rows, workspace);
+  st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
+  if (st != FH_OK) return st;
+  fh::Stage2Args a = stage2_args(head->d, hidden, rows);
+  a.probes = w.probes;
+  a.probe_stride = head->d.n_probes;
+  a.P = head->d.n_probes;
+  a.cluster_base = 0;
+  a.packed = w.packed;
+  a.counter = w.counter;
+  a.out_ids = out_ids;
+  a.wait_prior = 1;
+  const int items = rows * (a.P + a.n_special);
+  FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kGreedy>(head->d.weight_dtype, a, items, s, true)),
+                  "stage-2 launch");
+  return FH_OK;
+}
+
+FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int rows,
+                                    float temperature, uint64_t seed, uint64_t offset,
+                                    int64_t *out_ids, void *workspace, size_t workspace_bytes,
+                                    fh_stream_t stream) {
+  int st = check_call(head, hidden, rows, out_ids, workspace, workspace_bytes);
+  if (st != FH_OK || rows == 0) return st;
+  st = check_sampling(head, temperature);
+  if (st != FH_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = layout(head->d, rows, workspace);
+  st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
+                  nullptr, 0, s);
+  if (st != FH_OK) return st;
+  fh::Stage2Args a = stage2_args(head->d, hidden, rows);
+  a.probes = w.probes;
+  a.probe_stride = head->d.n_probes;
+  a.P = head->d.n_probes;
+  a.cluster_base = 0;
+  a.packed = w.packed;
+  a.counter = w.counter;
+  a.out_ids = out_ids;
+  a.temperature = temperature;
+  a.rng = rng_key(seed, offset);
+  a.wait_prior = 1;
+  const int items = rows * (a.P + a.n_special);
+  FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kSample>(head->d.weight_dtype, a, items, s, true)),
+                  "stage-2 launch");
+  return FH_OK;
+}
+
+FH_API int fh_top_clusters(const fh_head *head, const void *hidden, int rows, int do_sample,
+                           float temperature, uint64_t seed, uint64_t offset,
+                           int32_t *out_probes, float *out_scores, void *workspace,
+                           size_t workspace_bytes, fh_stream_t stream) {
+  int st = check_call(head, hidden, rows, out_probes, workspace, workspace_bytes);
+  if (st != FH_OK || rows == 0) return st;
+  if (do_sample) {
+    st = check_sampling(head, temperature);
+    if (st != FH_OK) return st;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = layout(head->d, rows, workspace);
+  return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, out_scores,
+                    out_probes, nullptr, 0, s);
+}
+
+FH_API int fh_dense_next_token(const fh_head *head, const void *hidden, int rows, int do_sample,
+                               float temperature, uint64_t seed, uint64_t offset,
+                               int64_t *out_ids, void *workspace, size_t workspace_bytes,
+                               fh_stream_t stream) {
+  int st = check_call(head, hidden, rows, out_ids, workspace, workspace_bytes);
+  if (st != FH_OK || rows == 0) return st;
+  if (do_sample && (!(temperature > 0.f) || !std::isfinite(temperature)))
+    return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = layout(head->d, rows, workspace);
+  FH_CHECK_LAUNCH(launch(fh::k_fill_u64, dim3((rows + 255) / 256), dim3(256), 0, s, false,
+                         w.packed, rows, 0ull),
+                  "fill launch");
+  FH_CHECK_LAUNCH(launch(fh::k_fill_u64, dim3(1), dim3(32), 0, s, false,
+                         reinterpret_cast<unsigned long long *>(w.counter), 1, 0ull),
+                  "fill launch");
+  fh::Stage2Args a = stage2_args(head->d, hidden, rows);
+  a.dense = 1;
+  a.P = head->d.n_clusters;
+  a.n_special = 0;
+  a.cluster_base = 0;
+  a.packed = w.packed;
+  a.counter = w.counter;
+  a.out_ids = out_ids;
+  a.temperature = temperature;
+  a.rng = rng_key(seed, offset);
+  const int items = rows * a.P;
+  if (do_sample)
+    FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kSample>(head->d.weight_dtype, a, items, s, false)),
+                    "dense launch");
+  else
+    FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kGreedy>(head->d.weight_dtype, a, items, s, false)),
+                    "dense launch");
+  return FH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Stateless kernels with the reference's layout (fused.py)
+// ---------------------------------------------------------------------------
+static int check_stateless(const void *hs, int T, int D, const void *w_perm, const int64_t *ci,
+                           int P, int K, int cap, int dtype, const void *out) {
+  if (T < 0 || P < 0) return fail(FH_ERR_INVALID_ARGUMENT, "negative T or P");
+  if (T == 0 || P == 0) return FH_OK;
+  if (!hs || !w_perm || !ci || !out)
+    return fail(FH_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (D <= 0 || D % 8 != 0)
+    return fail(FH_ERR_INVALID_ARGUMENT, "D=%d must be a positive multiple of 8", D);
+  if (K <= 0 || cap < 1 || cap > 32)
+    return fail(FH_ERR_INVALID_ARGUMENT, "n_clusters=%d / cluster_size=%d invalid", K, cap);
+  if (dtype != FH_BF16 && dtype != FH_FP16)
+    return fail(FH_ERR_INVALID_ARGUMENT, "dtype must be FH_BF16 or FH_FP16");
+  if (!aligned16(hs) || !aligned16(w_perm))
+    return fail(FH_ERR_INVALID_ARGUMENT, "hs and w_perm must be 16-byte aligned");
+  if ((long long)T * P > 0x7FFFFFFFll) return fail(FH_ERR_INVALID_ARGUMENT, "T*P too large");
+  return FH_OK;
+}
+
+static fh::Stage2Args stateless_args(const void *hs, int T, int D, const void *w_perm,
+                                     const int64_t *ci, int P, const int64_t *vocab_maps, int K,
+                                     int cap) {
+  fh::Stage2Args a;
+  memset(&a, 0, sizeof(a));
+  a.hidden = hs;
+  a.rows = T;
+  a.D = D;
+  a.w_perm = w_perm;
+  a.K = K;
+  a.cap = cap;
+  a.probes = ci;
+  a.probe_stride = P;
+  a.P = P;
+  a.vocab_map = vocab_maps;
+  a.temperature = 1.f;
+  return a;
+}
+
+FH_API int fh_block_sparse_logits(const void *hs, int T, int D, const void *w_perm,
+                                  const int64_t *ci, int P, int n_clusters, int cluster_size,
+                                  int dtype, void *out, fh_stream_t stream) {
+  int st = check_stateless(hs, T, D, w_perm, ci, P, n_clusters, cluster_size, dtype, out);
+  if (st != FH_OK || T == 0 || P == 0) return st;
+  fh::Stage2Args a = stateless_args(hs, T, D, w_perm, ci, P, nullptr, n_clusters, cluster_size);
+  a.out_logits = out;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  FH_CHECK_LAUNCH((launch_stage2<int64_t, fh::kLogits>(dtype, a, T * P, s, false)),
+                  "block_sparse_logits launch");
+  return FH_OK;
+}
+
+FH_API int fh_block_sparse_logits_argmax(const void *hs, int T, int D, const void *w_perm,
+                                         const int64_t *ci, int P, const int64_t *vocab_maps,
+                                         int n_clusters, int cluster_size, int dtype,
+                                         void *out_max, int64_t *out_vocab, fh_stream_t stream) {
+  int st = check_stateless(hs, T, D, w_perm, ci, P, n_clusters, cluster_size, dtype, out_max);
+  if (st != FH_OK || T == 0 || P == 0) return st;
+  if (!vocab_maps || !out_vocab) return fail(FH_ERR_INVALID_ARGUMENT, "null pointer argument");
+  fh::Stage2Args a =
+      stateless_args(hs, T, D, w_perm, ci, P, vocab_maps, n_clusters, cluster_size);
+  a.out_max = out_max;
+  a.out_vocab = out_vocab;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  FH_CHECK_LAUNCH((launch_stage2<int64_t, fh::kProbeMax>(dtype, a, T * P, s, false)),
+                  "block_sparse_logits_argmax launch");
+  return FH_OK;
+}
+
+FH_API int fh_block_sparse_argmax_atomic(const void *hs, int T, int D, const void *w_perm,
+                                         const int64_t *ci, int P, const int64_t *vocab_maps,
+                                         int n_clusters, int cluster_size, int dtype,
+                                         int64_t *out, fh_stream_t stream) {
+  int st = check_stateless(hs, T, D, w_perm, ci, P, n_clusters, cluster_size, dtype, out);
+  if (st != FH_OK || T == 0) return st;
+  if (!vocab_maps && P > 0) return fail(FH_ERR_INVALID_ARGUMENT, "null vocab_maps");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  unsigned long long *acc = reinterpret_cast<unsigned long long *>(out);
+  FH_CHECK_LAUNCH(launch(fh::k_fill_u64, dim3((T + 255) / 256), dim3(256), 0, s, false, acc, T,
+                         0ull),
+                  "fill launch");
+  if (P > 0) {
+    fh::Stage2Args a =
+        stateless_args(hs, T, D, w_perm, ci, P, vocab_maps, n_clusters, cluster_size);
+    a.packed = acc;
+    FH_CHECK_LAUNCH((launch_stage2<int64_t, fh::kGreedy>(dtype, a, T * P, s, false)),
+                    "block_sparse_argmax_atomic launch");
+  }
+  FH_CHECK_LAUNCH(launch(fh::k_unpack_ids, dim3((T + 255) / 256), dim3(256), 0, s, false, acc, T),
+                  "unpack launch");
+  return FH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor parallel
+// ---------------------------------------------------------------------------
+FH_API int fh_tp_local_candidates(const fh_head *head, const void *hidden, int rows,
+                                  int do_sample, float temperature, uint64_t seed,
+                                  uint64_t offset, int64_t *cand, void *workspace,
+                                  size_t workspace_bytes, fh_stream_t stream) {
+  int st = check_call(head, hidden, rows, cand, workspace, workspace_bytes);
+  if (st != FH_OK || rows == 0) return st;
+  if (do_sample) {
+    st = check_sampling(head, temperature);
+    if (st != FH_OK) return st;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = layout(head->d, rows, workspace);
+  return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, nullptr,
+                    nullptr, reinterpret_cast<long long *>(cand), head->d.cluster_base, s);
+}
+
+FH_API int fh_tp_select_and_score(const fh_head *head, const void *hidden, int rows, int n_ranks,
+                                  const int64_t *all_cand, int do_sample, float temperature,
+                                  uint64_t seed, uint64_t offset, int64_t *best, void *workspace,
+                                  size_t workspace_bytes, fh_stream_t stream) {
+  int st = check_call(head, hidden, rows, best, workspace, workspace_bytes);
+  if (st != FH_OK || rows == 0) return st;
+  if (!all_cand) return fail(FH_ERR_INVALID_ARGUMENT, "null candidate list");
+  if (n_ranks < 1 || (long long)n_ranks * head->d.n_probes > fh::kSelMaxItems)
+    return fail(FH_ERR_INVALID_ARGUMENT, "n_ranks=%d x n_probes=%d exceeds %d candidates",
+                n_ranks, head->d.n_probes, fh::kSelMaxItems);
+  if (do_sample && (!(temperature > 0.f) || !std::isfinite(temperature)))
+    return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const Workspace w = layout(head->d, rows, workspace);
+  FH_CHECK_LAUNCH(prepare_select(), "select kernel attribute");
+  fh::SelectArgs se;
+  memset(&se, 0, sizeof(se));
+  se.cand = reinterpret_cast<const long long *>(all_cand);
+  se.p_in = head->d.n_probes;
+  se.n_ranks = n_ranks;
+  se.rows = rows;
+  se.n_items = n_ranks * head->d.n_probes;
+  se.p = head->d.n_probes;
+  se.probes = w.probes;
+  se.packed = w.packed;
+  se.counter = w.counter;
+  se.n_packed = rows;
+  se.wait_prior = 0;
+  const size_t smem = (size_t)se.n_items * sizeof(unsigned long long);
+  FH_CHECK_LAUNCH(launch(fh::k_select, dim3(rows), dim3(fh::kSelThreads), smem, s, false, se),
+                  "global probe selection launch");
+  fh::Stage2Args a = stage2_args(head->d, hidden, rows);
+  a.probes = w.probes;
+  a.probe_stride = head->d.n_probes;
+  a.P = head->d.n_probes;
+  a.packed = w.packed;
+  a.counter = w.counter;
+  a.out_signed = reinterpret_cast<long long *>(best);
+  a.temperature = do_sample ? temperature : 1.f;
+  a.rng = rng_key(seed, offset);
+  a.wait_prior = 1;
+  const int items = rows * (a.P + a.n_special);
+  if (do_sample)
+    FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kSample>(head->d.weight_dtype, a, items, s, true)),
+                    "stage-2 launch");
+  else
+    FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kGreedy>(head->d.weight_dtype, a, items, s, true)),
+                    "stage-2 launch");
+  return FH_OK;
+}
+
+FH_API int fh_tp_finalize(const int64_t *best, int rows, int64_t *out_ids, fh_stream_t stream) {
+  if (rows < 0) return fail(FH_ERR_INVALID_ARGUMENT, "rows < 0");
+  if (rows == 0) return FH_OK;
+  if (!best || !out_ids) return fail(FH_ERR_INVALID_ARGUMENT, "null pointer argument");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  FH_CHECK_LAUNCH(launch(fh::k_signed_to_ids, dim3((rows + 255) / 256), dim3(256), 0, s, false,
+                         reinterpret_cast<const long long *>(best), rows, out_ids),
+                  "finalize launch");
+  return FH_OK;
+}
+
+}  // extern "C"
