@@ -222,6 +222,8 @@ __global__ void __launch_bounds__(kSelThreads) k_select(SelectArgs a) {
     if (tid == 0 && a.counter) *a.counter = 0u;
   }
   if (a.wait_prior) grid_dep_wait();
+  // Stage 2 may now be scheduled; its CTAs wait for this grid to finish.
+  grid_dep_launch();
 
   // Load keys; track the finite score range.
   float vmin = INFINITY, vmax = -INFINITY;
@@ -331,13 +333,17 @@ __global__ void __launch_bounds__(kSelThreads) k_select(SelectArgs a) {
     if (cnt <= kSelCandMax) {
       for (int i = tid; i < N; i += blockDim.x) {
         const unsigned long long k = skeys[i];
-        if (k >= alo && k <= ahi) cand[atomicAdd(&s_ncand, 1)] = k;
+        if (k >= alo && k <= ahi) {
+          const int pos = atomicAdd(&s_ncand, 1);
+          if (pos < kSelCandMax) cand[pos] = k;
+        }
       }
       __syncthreads();
-      if (tid < cnt) {
+      const int nc = min(cnt, kSelCandMax);
+      if (tid < nc) {
         const unsigned long long mine = cand[tid];
         int rank = 0;
-        for (int j = 0; j < cnt; ++j) rank += cand[j] > mine;
+        for (int j = 0; j < nc; ++j) rank += cand[j] > mine;
         if (rank == need - 1) s_T = mine;
       }
       __syncthreads();
@@ -364,7 +370,6 @@ __global__ void __launch_bounds__(kSelThreads) k_select(SelectArgs a) {
       ++pos;
     }
   }
-  grid_dep_launch();
 }
 
 // ===========================================================================
@@ -411,15 +416,17 @@ __device__ __forceinline__ __half from_float<__half>(float x) {
   return __float2half_rn(x);
 }
 
-// One CTA per (row, probe) item; warp w computes the logit of slot w of the
-// probed cluster (blockDim = 32 * cap). Lane l streams 16-byte vectors l,
-// l+32, ... of the w_perm row; the hidden row is read through L1.
+// One CTA per (row, probe) item; warp w computes the logits of slots w,
+// w + nwarps, ... of the probed cluster (blockDim = 32 * min(cap, 16)). Lane l
+// streams 16-byte vectors l, l+32, ... of each w_perm row; the hidden row is
+// read through L1.
 template <typename HT, typename IdxT, int MODE, int U>
-__global__ void __launch_bounds__(512) k_stage2(Stage2Args a) {
+__global__ void __launch_bounds__(512, 2) k_stage2(Stage2Args a) {
   __shared__ unsigned long long red[32];
   __shared__ float red_val[32];
   __shared__ unsigned s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
   const int ipr = a.P + a.n_special;
   const int row = blockIdx.x / ipr;
   const int j = blockIdx.x - row * ipr;
@@ -437,19 +444,29 @@ __global__ void __launch_bounds__(512) k_stage2(Stage2Args a) {
   }
   if (a.wait_prior) grid_dep_wait();
 
-  long long slot = -1;
+  long long base = -1;  // first w_perm row of this item
+  int nslots = 0;
   if (j < a.P) {
     long long cid = a.dense ? (long long)j
                             : (long long)reinterpret_cast<const IdxT *>(a.probes)[(size_t)row * a.probe_stride + j];
     cid -= a.cluster_base;
-    if (cid >= 0 && cid < a.K && warp < a.cap) slot = cid * a.cap + warp;
-  } else if (warp == 0) {
-    slot = a.special_slots[j - a.P];
+    if (cid >= 0 && cid < a.K) {
+      base = cid * a.cap;
+      nslots = a.cap;
+    }
+  } else {
+    base = a.special_slots[j - a.P];
+    nslots = (base >= 0 && base < (long long)a.K * a.cap) ? 1 : 0;
   }
 
-  float acc = 0.f;
-  if (slot >= 0) {
+  // hv holds the first chunk of the hidden row; with more than one chunk it
+  // is overwritten and reloaded per slot.
+  const bool one_chunk = nvec <= 32 * U;
+  bool hv_first = true;
+  for (int sl = warp; sl < nslots; sl += nwarps) {
+    const long long slot = base + sl;
     const char *wrow = reinterpret_cast<const char *>(a.w_perm) + (size_t)slot * row_bytes;
+    float acc = 0.f;
     for (int v0 = 0; v0 < nvec; v0 += 32 * U) {
       uint4 wv[U];
 #pragma unroll
@@ -457,13 +474,14 @@ __global__ void __launch_bounds__(512) k_stage2(Stage2Args a) {
         const int v = v0 + u * 32 + lane;
         wv[u] = v < nvec ? ldg_stream(wrow + (size_t)v * 16) : make_uint4(0, 0, 0, 0);
       }
-      if (v0 > 0) {
+      if (!(v0 == 0 && hv_first)) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int v = v0 + u * 32 + lane;
           hv[u] = v < nvec ? ldg_keep(hrow + (size_t)v * 16) : make_uint4(0, 0, 0, 0);
         }
       }
+      hv_first = one_chunk;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
 #pragma unroll
@@ -476,38 +494,30 @@ __global__ void __launch_bounds__(512) k_stage2(Stage2Args a) {
       }
     }
     acc = warp_sum(acc);
+    if (MODE == kLogits) {
+      if (lane == 0)
+        reinterpret_cast<HT *>(a.out_logits)[((size_t)row * a.P + j) * a.cap + sl] =
+            from_float<HT>(acc);
+    } else if (lane == 0) {
+      const uint32_t vid = (uint32_t)reinterpret_cast<const IdxT *>(a.vocab_map)[slot];
+      float key = acc;
+      if (MODE == kSample)
+        key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)(a.row_base + row), vid);
+      red[sl] = pack(key, vid);
+      red_val[sl] = acc;
+    }
   }
-
-  if (MODE == kLogits) {
-    if (lane == 0 && slot >= 0 && j < a.P)
-      reinterpret_cast<HT *>(a.out_logits)[((size_t)row * a.P + j) * a.cap + warp] =
-          from_float<HT>(acc);
-    return;
-  }
-
-  unsigned long long word = 0ull;
-  if (lane == 0 && slot >= 0) {
-    const uint32_t vid = (uint32_t)reinterpret_cast<const IdxT *>(a.vocab_map)[slot];
-    float key = acc;
-    if (MODE == kSample)
-      key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)(a.row_base + row), vid);
-    word = pack(key, vid);
-  }
-  if (lane == 0) {
-    red[warp] = word;
-    red_val[warp] = acc;
-  }
+  if (MODE == kLogits) return;
   __syncthreads();
   if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    unsigned long long w = lane < nw ? red[lane] : 0ull;
+    const unsigned long long w = lane < nslots ? red[lane] : 0ull;
     const unsigned long long best = warp_max_u64(w);
     if (MODE == kProbeMax) {
       if (j < a.P) {
         // value of the winning slot, as the reference stores it (fused.py:78)
-        const unsigned wl = __ffs(__ballot_sync(0xFFFFFFFFu, lane < nw && w == best && best != 0ull)) - 1;
-        const float bv = red_val[wl];
+        const int wl = __ffs(__ballot_sync(0xFFFFFFFFu, lane < nslots && w == best)) - 1;
         if (lane == 0) {
+          const float bv = (nslots > 0 && wl >= 0) ? red_val[wl] : 0.f;
           reinterpret_cast<HT *>(a.out_max)[(size_t)row * a.P + j] = from_float<HT>(bv);
           a.out_vocab[(size_t)row * a.P + j] =
               best ? (int64_t)packed_id(best) : (int64_t)0xFFFFFFFFll;
@@ -517,7 +527,7 @@ __global__ void __launch_bounds__(512) k_stage2(Stage2Args a) {
     }
     if (lane == 0 && best != 0ull) atomicMax(&a.packed[row], best);
   }
-  if (a.counter == nullptr) return;
+  if (MODE == kProbeMax || a.counter == nullptr) return;
   // Last CTA to finish publishes the winners.
   if (threadIdx.x == 0) {
     __threadfence();
@@ -527,7 +537,9 @@ __global__ void __launch_bounds__(512) k_stage2(Stage2Args a) {
   if (s_last) {
     __threadfence();
     for (int r = threadIdx.x; r < a.rows; r += blockDim.x) {
-      const unsigned long long w = atomicOr(&a.packed[r], 0ull);
+      // Every other CTA has finished its atomicMax: read the winner and
+      // leave the accumulator zeroed for the next call on this workspace.
+      const unsigned long long w = atomicExch(&a.packed[r], 0ull);
       if (a.out_ids) a.out_ids[r] = w ? (int64_t)packed_id(w) : (int64_t)0xFFFFFFFFll;
       if (a.out_signed) a.out_signed[r] = to_signed(w);
     }

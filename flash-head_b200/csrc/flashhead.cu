@@ -176,8 +176,9 @@ cudaError_t launch_scores(int hdt, int wdt, const fh::ScoresArgs &a, cudaStream_
 
 template <typename HT, typename IdxT, int MODE>
 cudaError_t launch_stage2_t(const fh::Stage2Args &a, int items, cudaStream_t s, bool pdl) {
-  constexpr int U = 8;
-  return launch(fh::k_stage2<HT, IdxT, MODE, U>, dim3(items), dim3(32 * a.cap), 0, s, pdl, a);
+  constexpr int U = 4;
+  const int warps = a.cap < 16 ? a.cap : 16;
+  return launch(fh::k_stage2<HT, IdxT, MODE, U>, dim3(items), dim3(32 * warps), 0, s, pdl, a);
 }
 
 template <typename IdxT, int MODE>
@@ -401,6 +402,60 @@ FH_API int fh_top_clusters(const fh_head *head, const void *hidden, int rows, in
   const Workspace w = layout(head->d, rows, workspace);
   return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, out_scores,
                     out_probes, nullptr, 0, s);
+}
+
+FH_API int fh_cluster_scores(const fh_head *head, const void *hidden, int rows, int do_sample,
+                             float temperature, uint64_t seed, uint64_t offset, float *out_scores,
+                             fh_stream_t stream) {
+  if (!head) return fail(FH_ERR_INVALID_ARGUMENT, "null head");
+  if (rows < 0) return fail(FH_ERR_INVALID_ARGUMENT, "rows=%d < 0", rows);
+  if (rows == 0) return FH_OK;
+  if (!hidden || !out_scores) return fail(FH_ERR_INVALID_ARGUMENT, "null hidden/output pointer");
+  if (!aligned16(hidden))
+    return fail(FH_ERR_INVALID_ARGUMENT, "hidden states must be 16-byte aligned");
+  if (do_sample) {
+    const int st = check_sampling(head, temperature);
+    if (st != FH_OK) return st;
+  }
+  fh::ScoresArgs sa =
+      scores_args(head->d, hidden, rows, do_sample != 0, temperature, seed, offset);
+  sa.scores = out_scores;
+  sa.score_stride = head->d.n_clusters;
+  const int wdt = do_sample ? head->d.sample_dtype : head->d.score_dtype;
+  FH_CHECK_LAUNCH(launch_scores(head->d.weight_dtype, wdt, sa, reinterpret_cast<cudaStream_t>(stream)),
+                  "stage-1 scores launch");
+  return FH_OK;
+}
+
+FH_API int fh_stage2_next_token(const fh_head *head, const void *hidden, int rows,
+                                const int32_t *probes, int do_sample, float temperature,
+                                uint64_t seed, uint64_t offset, int64_t *out_ids, void *workspace,
+                                size_t workspace_bytes, fh_stream_t stream) {
+  int st = check_call(head, hidden, rows, out_ids, workspace, workspace_bytes);
+  if (st != FH_OK || rows == 0) return st;
+  if (!probes) return fail(FH_ERR_INVALID_ARGUMENT, "null probe list");
+  if (do_sample && (!(temperature > 0.f) || !std::isfinite(temperature)))
+    return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
+  const Workspace w = layout(head->d, rows, workspace);
+  fh::Stage2Args a = stage2_args(head->d, hidden, rows);
+  a.probes = probes;
+  a.probe_stride = head->d.n_probes;
+  a.P = head->d.n_probes;
+  a.cluster_base = 0;
+  a.packed = w.packed;
+  a.counter = w.counter;
+  a.out_ids = out_ids;
+  a.temperature = do_sample ? temperature : 1.f;
+  a.rng = rng_key(seed, offset);
+  const int items = rows * (a.P + a.n_special);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (do_sample)
+    FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kSample>(head->d.weight_dtype, a, items, s, false)),
+                    "stage-2 launch");
+  else
+    FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kGreedy>(head->d.weight_dtype, a, items, s, false)),
+                    "stage-2 launch");
+  return FH_OK;
 }
 
 FH_API int fh_dense_next_token(const fh_head *head, const void *hidden, int rows, int do_sample,

@@ -77,6 +77,8 @@ SIGNATURES = {
     "fh_get_next_token": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "fh_get_next_token_sample": (_I, [_P, _P, _I, _F, _U64, _U64, _P, _P, _SZ, _P]),
     "fh_top_clusters": (_I, [_P, _P, _I, _I, _F, _U64, _U64, _P, _P, _P, _SZ, _P]),
+    "fh_cluster_scores": (_I, [_P, _P, _I, _I, _F, _U64, _U64, _P, _P]),
+    "fh_stage2_next_token": (_I, [_P, _P, _I, _P, _I, _F, _U64, _U64, _P, _P, _SZ, _P]),
     "fh_dense_next_token": (_I, [_P, _P, _I, _I, _F, _U64, _U64, _P, _P, _SZ, _P]),
     "fh_block_sparse_logits": (_I, [_P, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P]),
     "fh_block_sparse_logits_argmax": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _I, _I, _P, _P, _P]),

@@ -134,7 +134,8 @@ class NativeHead:
         need = self.workspace_bytes(rows)
         ws = self._ws.get(idx)
         if ws is None or ws.numel() < need:
-            ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=self.device)
+            # zero-filled: fh_stage2_next_token expects a clean accumulator
+            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=self.device)
             self._ws[idx] = ws
         return ws
 
@@ -175,6 +176,35 @@ class NativeHead:
                       float(temperature), int(seed), int(offset), probes.data_ptr(),
                       _ptr(scores), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
         return (probes, scores) if return_scores else probes
+
+    def cluster_scores(self, hidden, do_sample=False, temperature=1.0, seed=0, offset=0,
+                       out=None):
+        """Stage 1 only: [N, K] fp32 scores (or Gumbel keys when sampling)."""
+        h = self._h(hidden)
+        n = h.shape[0]
+        out = out if out is not None else torch.empty((n, self.K), dtype=torch.float32,
+                                                      device=self.device)
+        if n:
+            _lib.call("fh_cluster_scores", self.handle, h.data_ptr(), n, int(bool(do_sample)),
+                      float(temperature), int(seed), int(offset), out.data_ptr(),
+                      _lib.stream_ptr())
+        return out
+
+    def stage2_next_token(self, hidden, probes, do_sample=False, temperature=1.0, seed=0,
+                          offset=0, out=None):
+        """Stage 2 only for given int32 probe lists [N, p] -> [N] int64."""
+        h = self._h(hidden)
+        n = h.shape[0]
+        pr = probes.to(device=self.device, dtype=torch.int32).contiguous()
+        if pr.shape != (n, self.p):
+            raise ValueError(f"probes must be [{n}, {self.p}], got {tuple(pr.shape)}")
+        out = out if out is not None else torch.empty(n, dtype=torch.int64, device=self.device)
+        if n:
+            ws = self.workspace(n)
+            _lib.call("fh_stage2_next_token", self.handle, h.data_ptr(), n, pr.data_ptr(),
+                      int(bool(do_sample)), float(temperature), int(seed), int(offset),
+                      out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
+        return out
 
     def dense_next_token(self, hidden, do_sample=False, temperature=1.0, seed=0, offset=0):
         h = self._h(hidden)

@@ -150,6 +150,34 @@ FH_API int fh_top_clusters(const fh_head *head, const void *hidden, int rows,
                            size_t workspace_bytes, fh_stream_t stream);
 
 /*
+ * Stage-1 scores only: out_scores [rows, K] fp32 = h . cluster_w^T (times the
+ * fp8 row scale); in sampling mode the Gumbel-perturbed keys
+ * h . centroid_w^T / T + G. Replaces the reference's cluster_linear(h)
+ * (flash_head.py:213) / F.linear(h, centroids.t()) (:203-205). Needs no
+ * workspace.
+ */
+FH_API int fh_cluster_scores(const fh_head *head, const void *hidden, int rows,
+                             int do_sample, float temperature, uint64_t seed,
+                             uint64_t offset, float *out_scores,
+                             fh_stream_t stream);
+
+/*
+ * Stage 2 only, for given probe lists probes [rows, n_probes] (int32 cluster
+ * ids; ids outside [0, K) are skipped): out_ids[rows]. The head's
+ * block_sparse_argmax_atomic (fused.py:167-188) plus its special tokens, or
+ * the within-candidate sample when do_sample != 0. Unlike the other entry
+ * points this one does not reset the workspace's accumulator first: the
+ * workspace must be zero-filled before its first use (and after a failed
+ * call); every completed call leaves it zeroed.
+ */
+FH_API int fh_stage2_next_token(const fh_head *head, const void *hidden,
+                                int rows, const int32_t *probes, int do_sample,
+                                float temperature, uint64_t seed,
+                                uint64_t offset, int64_t *out_ids,
+                                void *workspace, size_t workspace_bytes,
+                                fh_stream_t stream);
+
+/*
  * Full-vocabulary next token over w_perm (greedy, or sampled at temperature
  * when do_sample != 0). Replaces the dense branch of get_next_token for
  * hidden_states.shape[0] > 10 (flash_head.py:292-301).
