@@ -543,6 +543,29 @@ def run_reference(args):
     }
 
 
+def run_profile(args):
+    """Small eager run for ncu: one head replica (about 0.6 GB), W warm-up steps,
+    then --profile-steps greedy steps launched one by one (no graphs)."""
+    import torch
+
+    from flash_head.synthetic import make_hidden
+    wl = workloads()[args.workload]
+    rows = args.rows or wl["rows"]
+    torch.cuda.set_device(0)
+    _, reps = build_replicas(wl, 1, seed=0, device="cuda")
+    nh = reps[0]
+    H = [make_hidden(rows, wl["shape"].hidden, seed=1000 + i, device="cuda") for i in range(8)]
+    out = torch.empty(rows, dtype=torch.int64, device="cuda")
+    for i in range(args.warmup):
+        nh.next_token(H[i % 8], out=out)
+    torch.cuda.synchronize()
+    for i in range(args.profile_steps):
+        nh.next_token(H[i % 8], out=out)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_steps": args.profile_steps, "rows": rows,
+                      "workload": workload_label(wl, rows), "last_ids": out.tolist()}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -553,9 +576,14 @@ def main():
     ap.add_argument("--rows", type=int, default=0)
     ap.add_argument("--no-sweep", dest="sweep", action="store_false")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="eager profiling run (for ncu) instead of the benchmark")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.profile_steps:
+        run_profile(args)
+        return
 
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:

@@ -101,23 +101,30 @@ struct Workspace {
   int32_t *probes;              // [rows, p]
   unsigned long long *packed;   // [rows]
   unsigned *counter;            // [1]
-  size_t bytes;
+  size_t bytes;                 // bytes needed for `rows`
 };
 
-Workspace layout(const fh_head_desc &d, int rows, void *base) {
+// Persistent state first, at offsets that do not depend on `rows`: the
+// last-CTA counter at 0 and the stage-2 accumulator packed[r] at 256 + 8r.
+// Stage 2 leaves both zeroed when it completes, so a workspace zero-filled
+// once stays clean across calls with any row count. Per-call scratch
+// (probes, scores) is placed from the top of the buffer downwards and never
+// reaches the state of a call whose size check passed.
+Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   Workspace w;
   char *p = reinterpret_cast<char *>(base);
-  size_t off = 0;
   w.score_stride = (int)round_up((size_t)d.n_clusters, 64);
-  w.scores = reinterpret_cast<float *>(p + off);
-  off = round_up(off + (size_t)rows * w.score_stride * sizeof(float), 256);
-  w.probes = reinterpret_cast<int32_t *>(p + off);
-  off = round_up(off + (size_t)rows * d.n_probes * sizeof(int32_t), 256);
-  w.packed = reinterpret_cast<unsigned long long *>(p + off);
-  off = round_up(off + (size_t)rows * sizeof(unsigned long long), 256);
-  w.counter = reinterpret_cast<unsigned *>(p + off);
-  off = round_up(off + 256, 256);
-  w.bytes = off;
+  const size_t state = 256 + round_up((size_t)rows * sizeof(unsigned long long), 256);
+  const size_t probes = round_up((size_t)rows * d.n_probes * sizeof(int32_t), 256);
+  const size_t scores = round_up((size_t)rows * w.score_stride * sizeof(float), 256);
+  w.bytes = state + probes + scores + 256;
+  w.counter = reinterpret_cast<unsigned *>(p);
+  w.packed = reinterpret_cast<unsigned long long *>(p + 256);
+  const size_t top = (ws_bytes / 256) * 256;
+  const size_t probes_off = top >= probes ? top - probes : 0;
+  const size_t scores_off = probes_off >= scores ? probes_off - scores : 0;
+  w.probes = reinterpret_cast<int32_t *>(p + probes_off);
+  w.scores = reinterpret_cast<float *>(p + scores_off);
   return w;
 }
 
@@ -130,7 +137,7 @@ int check_call(const fh_head *h, const void *hidden, int rows, const void *out, 
   if (!aligned16(hidden))
     return fail(FH_ERR_INVALID_ARGUMENT, "hidden states must be 16-byte aligned");
   if (!ws) return fail(FH_ERR_WORKSPACE, "null workspace");
-  const size_t need = layout(h->d, rows, nullptr).bytes;
+  const size_t need = layout(h->d, rows, nullptr, 0).bytes;
   if (ws_bytes < need)
     return fail(FH_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed for %d rows", ws_bytes,
                 need, rows);
@@ -331,7 +338,7 @@ FH_API int fh_head_destroy(fh_head *head) {
 
 FH_API size_t fh_workspace_bytes(const fh_head *head, int rows) {
   if (!head || rows < 0) return 0;
-  return layout(head->d, rows, nullptr).bytes;
+  return layout(head->d, rows, nullptr, 0).bytes;
 }
 
 FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
@@ -340,7 +347,7 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
   int st = check_call(head, hidden, rows, out_ids, workspace, workspace_bytes);
   if (st != FH_OK || rows == 0) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const Workspace w = layout(head->d, rows, workspace);
+  const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
   if (st != FH_OK) return st;
   fh::Stage2Args a = stage2_args(head->d, hidden, rows);
@@ -367,7 +374,7 @@ FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int
   st = check_sampling(head, temperature);
   if (st != FH_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const Workspace w = layout(head->d, rows, workspace);
+  const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
                   nullptr, 0, s);
   if (st != FH_OK) return st;
@@ -399,7 +406,7 @@ FH_API int fh_top_clusters(const fh_head *head, const void *hidden, int rows, in
     if (st != FH_OK) return st;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const Workspace w = layout(head->d, rows, workspace);
+  const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, out_scores,
                     out_probes, nullptr, 0, s);
 }
@@ -436,7 +443,7 @@ FH_API int fh_stage2_next_token(const fh_head *head, const void *hidden, int row
   if (!probes) return fail(FH_ERR_INVALID_ARGUMENT, "null probe list");
   if (do_sample && (!(temperature > 0.f) || !std::isfinite(temperature)))
     return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
-  const Workspace w = layout(head->d, rows, workspace);
+  const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   fh::Stage2Args a = stage2_args(head->d, hidden, rows);
   a.probes = probes;
   a.probe_stride = head->d.n_probes;
@@ -467,7 +474,7 @@ FH_API int fh_dense_next_token(const fh_head *head, const void *hidden, int rows
   if (do_sample && (!(temperature > 0.f) || !std::isfinite(temperature)))
     return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const Workspace w = layout(head->d, rows, workspace);
+  const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   FH_CHECK_LAUNCH(launch(fh::k_fill_u64, dim3((rows + 255) / 256), dim3(256), 0, s, false,
                          w.packed, rows, 0ull),
                   "fill launch");
@@ -602,7 +609,7 @@ FH_API int fh_tp_local_candidates(const fh_head *head, const void *hidden, int r
     if (st != FH_OK) return st;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const Workspace w = layout(head->d, rows, workspace);
+  const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, nullptr,
                     nullptr, reinterpret_cast<long long *>(cand), head->d.cluster_base, s);
 }
@@ -620,7 +627,7 @@ FH_API int fh_tp_select_and_score(const fh_head *head, const void *hidden, int r
   if (do_sample && (!(temperature > 0.f) || !std::isfinite(temperature)))
     return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const Workspace w = layout(head->d, rows, workspace);
+  const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   FH_CHECK_LAUNCH(prepare_select(), "select kernel attribute");
   fh::SelectArgs se;
   memset(&se, 0, sizeof(se));

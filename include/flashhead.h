@@ -19,8 +19,9 @@
  *   - Every pointer argument named hidden/w_perm/... is a DEVICE pointer; the
  *     library never allocates, frees, or synchronises, and never reads device
  *     memory on the host, so every call can be captured in a CUDA graph.
- *   - Scratch memory is caller-owned: size it with fh_workspace_bytes().
- *     A workspace may be reused by consecutive calls on one stream; calls
+ *   - Scratch memory is caller-owned: size it with fh_workspace_bytes() and
+ *     zero-fill it once before its first use. A workspace may be reused by
+ *     consecutive calls on one stream, with any row count that fits; calls
  *     that may overlap on the GPU need separate workspaces.
  *   - All functions return FH_OK (0) or an fh_status code; the message of
  *     the last failure on the calling thread is available from

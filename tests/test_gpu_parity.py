@@ -88,10 +88,16 @@ def test_small_special_tokens(golden_small):
         assert O.token_within_tolerance(toks[r], want, lambda v: ov.logit(Hn[r], v), 1e-5)
         assert O.token_within_tolerance(toks[r], g["ref_tok_special"][r],
                                         lambda v: ov.logit(Hn[r], v), RTOL), r
-    # a special token with a huge logit always wins, whatever the probes
+    # special tokens are scored even when their cluster is not probed: with
+    # probe lists that exclude its cluster, h = 50 * W[sp] must still pick sp
     sp = int(g["specials"][1])
-    h = torch.from_numpy(ov.W[sp] * 50).to("cuda", torch.bfloat16)
-    assert int(fh.get_next_token_batched(h.view(1, -1))[0]) == sp
+    cl = int(np.nonzero(ov.vm == sp)[0][0])
+    others = [c for c in range(fh._K) if c != cl][:fh.n_probes]
+    pr = torch.tensor([others], dtype=torch.int32, device="cuda")
+    h = torch.from_numpy(ov.W[sp] * 50).to("cuda", torch.bfloat16).view(1, -1)
+    assert int(fh.native().stage2_next_token(h, pr)[0]) == sp
+    plain, _ = _small(g, "model")
+    assert int(plain.native().stage2_next_token(h, pr)[0]) != sp
 
 
 def test_fp16_head(golden_small):
@@ -364,3 +370,17 @@ def test_tp_shards_reproduce_unsharded(llama1b_heads, world, do_sample):
     ids = NativeHead.tp_finalize(bests.max(dim=0).values)
     whole = fh.get_next_token_batched(H, do_sample=do_sample, temperature=0.8, seed=99, offset=3)
     assert torch.equal(ids, whole)
+
+
+def test_workspace_reuse_across_row_counts(llama1b_heads):
+    """One workspace serves calls with any row count: stage 2 alone (which
+    relies on the accumulator left zeroed by earlier calls) matches the full
+    step whatever row counts ran before it."""
+    from flash_head.synthetic import make_hidden
+    nh = llama1b_heads["fp8"].native()
+    for i, rows in enumerate((64, 1, 17, 3, 64, 2, 1)):
+        H = make_hidden(rows, nh.D, seed=600 + i, device="cuda")
+        probes = nh.top_clusters(H)
+        a = nh.stage2_next_token(H, probes)
+        b = nh.next_token(H)
+        assert torch.equal(a, b), rows
