@@ -1,0 +1,504 @@
+// One-kernel FlashHead decode step for a few hidden rows (R <= 4).
+//
+// A persistent cooperative grid of one 512-thread CTA per SM runs all three
+// stages with a single grid-wide dependency:
+//
+//  1. stage 1   CTA b streams its contiguous slice of centroid rows
+//               [b*K/G, (b+1)*K/G) through a 4-slot ring of shared-memory
+//               buffers filled by bulk asynchronous copies (TMA engine,
+//               completion on mbarriers) and scores them against the R hidden
+//               rows held in registers; scores go to global memory and the
+//               per-row min/max to two atomic words.
+//  2. barrier   one arrive counter, bounded spin (a timeout sets an error
+//               bit and the kernel still runs to completion).
+//  3. select    every CTA redundantly selects the top-p clusters of the
+//               hidden rows its stage-2 share needs, from the L2-resident
+//               scores, with a 512-bin histogram over [min, max] and an exact
+//               ranking of the threshold bin. Redundant selection costs no
+//               second grid-wide dependency.
+//  4. stage 2   the R * (p * cap + n_special) w_perm rows to score are split
+//               evenly across CTAs in (row, probe, slot) order; each CTA
+//               streams its contiguous runs through the same ring, packs
+//               (logit or Gumbel key, vocab id) words, and reduces them with a
+//               64-bit atomicMax. The last CTA to finish publishes the ids and
+//               resets the shared state words.
+#pragma once
+
+#include "fh_kernels.cuh"
+
+namespace fh {
+
+constexpr int kFThreads = 512;
+constexpr int kFWarps = kFThreads / 32;
+constexpr int kFSlots = 4;
+constexpr int kFSlotBytes = 24 * 1024;
+constexpr int kFChunkRows = 16;
+constexpr int kFBins = 512;
+constexpr int kFCand = 256;
+constexpr int kFMaxRows = 4;
+constexpr int kFMaxProbes = 4096;
+
+// State words at the start of the workspace (uint32 index).
+constexpr int kSyncArrive = 1;
+constexpr int kSyncDone = 2;
+constexpr int kSyncError = 3;
+constexpr int kSyncMinMax = 8;  // [8 + 2r] = max(~mono(min)), [9 + 2r] = max(mono(max))
+
+constexpr uint32_t kErrBarrierTimeout = 1u;
+constexpr uint32_t kErrCopyTimeout = 2u;
+
+struct FusedArgs {
+  const void *hidden;  // [R, D]
+  int rows;
+  int D;
+  const void *cw;      // stage-1 matrix [K, D] (WT)
+  const float *cscale; // [K] or null
+  int K;
+  const void *w_perm;  // [K * cap, D] (HT)
+  const int32_t *vocab_map;
+  int cap;
+  int p;
+  const int32_t *special_slots;
+  int n_special;
+  int do_sample;
+  float temperature;
+  RngKey rng;
+  float *scores;       // [R, K] global scratch
+  uint32_t *sync;      // workspace state words
+  unsigned long long *packed;  // [R]
+  int64_t *out_ids;    // [R]
+  uint32_t barrier_polls;      // grid-barrier poll limit
+  uint32_t copy_polls;         // mbarrier poll limit
+  int extra_arrivals;          // >0 only in the timeout test: wait for more CTAs than exist
+};
+
+struct FusedSmem {
+  uint64_t mbar[kFSlots];
+  float part[kFSlots][kFChunkRows][16][kFMaxRows];
+  float local[kFMaxRows][128];
+  uint32_t hist[kFBins];
+  unsigned long long cand[kFCand];
+  unsigned long long best[2];
+  int scan[33];
+  int s_bstar, s_above, s_cnt, s_ncand;
+  unsigned long long s_T, s_kmin, s_kmax;
+  uint32_t s_err;
+};
+
+constexpr size_t kFRingBytes = (size_t)kFSlots * kFSlotBytes;
+constexpr size_t kFSmemBytes = kFRingBytes + sizeof(FusedSmem) + 2ull * kFMaxProbes * 4;
+
+template <typename T>
+__device__ __forceinline__ void vec_to_float(const uint4 &v, float *f);
+template <>
+__device__ __forceinline__ void vec_to_float<__nv_bfloat16>(const uint4 &v, float *f) {
+  Vec<__nv_bfloat16>::to_float(v, f);
+}
+template <>
+__device__ __forceinline__ void vec_to_float<__half>(const uint4 &v, float *f) {
+  Vec<__half>::to_float(v, f);
+}
+template <>
+__device__ __forceinline__ void vec_to_float<__nv_fp8_e4m3>(const uint4 &v, float *f) {
+  Vec<__nv_fp8_e4m3>::to_float(v, f);
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide top-p selection over K scores in shared memory (512 threads).
+// Same rule as k_select: the p largest (score, -id) keys; output ascending ids.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int fsel_bin_value(float s, float vmin, float scale) {
+  const float f = (s - vmin) * scale;
+  const int b = f >= (float)(kFBins - 1) ? kFBins - 1 : (int)f;
+  return b < 0 ? 0 : b;
+}
+
+__device__ void fused_select(const float *sc, int K, int p, float vmin, float vmax, int *out,
+                             FusedSmem &S) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float vscale = (float)kFBins / (vmax - vmin);
+  const bool value_ok = vmax > vmin && isfinite(vscale) && vscale > 0.f;
+  auto key_of = [&](int i) { return pack(sanitize(sc[i]), (uint32_t)i); };
+
+  unsigned long long alo = 0ull, ahi = ~0ull, T = 0ull;
+  int need = p;
+  for (int level = 0; level < kSelMaxLevels; ++level) {
+    const bool vm = value_ok && level == 0;
+    const unsigned long long range = ahi - alo;
+    const int shift = range == 0ull ? 0 : max(0, 64 - __clzll((long long)range) - 9);
+    for (int i = tid; i < kFBins; i += kFThreads) S.hist[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < K; i += kFThreads) {
+      const unsigned long long k = key_of(i);
+      if (k < alo || k > ahi) continue;
+      const int b = vm ? fsel_bin_value(unmono((uint32_t)(k >> 32)), vmin, vscale)
+                       : (int)((k - alo) >> shift);
+      atomicAdd(&S.hist[b], 1u);
+    }
+    __syncthreads();
+    const int mybin = kFBins - 1 - tid;  // thread t owns bin 511 - t (highest first)
+    const int c = (int)S.hist[mybin];
+    int total;
+    const int before = block_exclusive_scan(c, S.scan, &total);
+    if (before < need && need <= before + c) {
+      S.s_bstar = mybin;
+      S.s_above = before;
+      S.s_cnt = c;
+    }
+    __syncthreads();
+    const int bstar = S.s_bstar, cnt = S.s_cnt;
+    need -= S.s_above;
+    unsigned long long kmin = ~0ull, kmax = 0ull;
+    for (int i = tid; i < K; i += kFThreads) {
+      const unsigned long long k = key_of(i);
+      if (k < alo || k > ahi) continue;
+      const int b = vm ? fsel_bin_value(unmono((uint32_t)(k >> 32)), vmin, vscale)
+                       : (int)((k - alo) >> shift);
+      if (b == bstar) {
+        kmin = k < kmin ? k : kmin;
+        kmax = k > kmax ? k : kmax;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long x = __shfl_xor_sync(0xFFFFFFFFu, kmin, o);
+      const unsigned long long y = __shfl_xor_sync(0xFFFFFFFFu, kmax, o);
+      kmin = x < kmin ? x : kmin;
+      kmax = y > kmax ? y : kmax;
+    }
+    if (tid == 0) {
+      S.s_kmin = ~0ull;
+      S.s_kmax = 0ull;
+      S.s_ncand = 0;
+    }
+    __syncthreads();
+    if (lane == 0) {
+      atomicMin(&S.s_kmin, kmin);
+      atomicMax(&S.s_kmax, kmax);
+    }
+    __syncthreads();
+    alo = S.s_kmin;
+    ahi = S.s_kmax;
+    if (cnt == need) {
+      T = alo;
+      break;
+    }
+    if (cnt <= kFCand) {
+      for (int i = tid; i < K; i += kFThreads) {
+        const unsigned long long k = key_of(i);
+        if (k >= alo && k <= ahi) {
+          const int pos = atomicAdd(&S.s_ncand, 1);
+          if (pos < kFCand) S.cand[pos] = k;
+        }
+      }
+      __syncthreads();
+      const int nc = min(cnt, kFCand);
+      if (tid < nc) {
+        const unsigned long long mine = S.cand[tid];
+        int rank = 0;
+        for (int j = 0; j < nc; ++j) rank += S.cand[j] > mine;
+        if (rank == need - 1) S.s_T = mine;
+      }
+      __syncthreads();
+      T = S.s_T;
+      break;
+    }
+    __syncthreads();
+    (void)warp;
+  }
+  // Compaction in id order: thread t owns a contiguous run of ids.
+  const int per = (K + kFThreads - 1) / kFThreads;
+  const int i0 = min(K, tid * per), i1 = min(K, i0 + per);
+  int mine = 0;
+  for (int i = i0; i < i1; ++i) mine += key_of(i) >= T;
+  int total;
+  int pos = block_exclusive_scan(mine, S.scan, &total);
+  for (int i = i0; i < i1; ++i) {
+    if (key_of(i) >= T) {
+      if (pos < p) out[pos] = i;
+      ++pos;
+    }
+  }
+  __syncthreads();
+}
+
+// Stage-2 work walk: work index w of row-major (hidden row, probe, slot) items,
+// then the special tokens of each hidden row. Returns the w_perm row of w and
+// how many following work items are contiguous in w_perm (run length).
+struct S2Item {
+  long long src;  // w_perm row, -1 if invalid
+  int run;
+  int hrow;
+};
+
+__device__ __forceinline__ S2Item s2_item(const FusedArgs &a, const int *probes_sm, int r_lo,
+                                          long long w, long long w_end) {
+  const long long per_row = (long long)a.p * a.cap + a.n_special;
+  S2Item it;
+  it.hrow = (int)(w / per_row);
+  const long long j = w - (long long)it.hrow * per_row;
+  if (j < (long long)a.p * a.cap) {
+    const int pi = (int)(j / a.cap), sl = (int)(j - (long long)pi * a.cap);
+    const int cl = probes_sm[(it.hrow - r_lo) * a.p + pi];
+    it.src = (long long)cl * a.cap + sl;
+    it.run = (int)min((long long)(a.cap - sl), w_end - w);
+  } else {
+    const long long sp = a.special_slots[j - (long long)a.p * a.cap];
+    it.src = (sp >= 0 && sp < (long long)a.K * a.cap) ? sp : -1;
+    it.run = 1;
+  }
+  return it;
+}
+
+template <typename HT, typename WT, int R>
+__global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char *ring = smem;
+  FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem + kFRingBytes);
+  int *probes_sm = reinterpret_cast<int *>(smem + kFRingBytes + sizeof(FusedSmem));
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, b = blockIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kFSlots; ++s) mbar_init(&S.mbar[s], 1);
+    fence_mbar_init();
+    S.s_err = 0u;
+    S.best[0] = S.best[1] = 0ull;
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------ stage 1
+  const int c0 = (int)((long long)b * a.K / G), c1 = (int)((long long)(b + 1) * a.K / G);
+  const int nc = c1 - c0;
+  const int row1 = a.D * (int)sizeof(WT);
+  const int rpc1 = max(1, min(kFChunkRows, kFSlotBytes / row1));
+  const int n1 = (nc + rpc1 - 1) / rpc1;
+  const char *wsrc = reinterpret_cast<const char *>(a.cw) + (size_t)c0 * row1;
+  uint32_t gi = 0;  // running chunk counter over both stages (slot = gi % kFSlots)
+
+  auto issue1 = [&](int i) {
+    const int s = i % kFSlots;
+    const int rows = min(rpc1, nc - i * rpc1);
+    const uint32_t bytes = (uint32_t)(rows * row1);
+    fence_proxy_async_smem();
+    mbar_expect_tx(&S.mbar[s], bytes);
+    bulk_g2s(ring + (size_t)s * kFSlotBytes, wsrc + (size_t)i * rpc1 * row1, bytes, &S.mbar[s]);
+  };
+  if (tid == 0)
+    for (int i = 0; i < min(kFSlots, n1); ++i) issue1(i);
+
+  constexpr int VE1 = Vec<WT>::kElems;
+  const int NV1 = row1 / 16, Q1 = NV1 / 32, RG1 = kFWarps / Q1;
+  const int g1 = warp / Q1, q1 = warp % Q1, col1 = q1 * 32 + lane;
+  float h1[R][VE1];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    // VE1 elements of hidden row r at column col1 (VE1 * 2 bytes)
+    const char *hp = reinterpret_cast<const char *>(a.hidden) + (size_t)r * a.D * sizeof(HT) +
+                     (size_t)col1 * VE1 * sizeof(HT);
+#pragma unroll
+    for (int v = 0; v < VE1 / 8; ++v) {
+      const uint4 x = (r < a.rows && g1 < RG1) ? ldg_keep(hp + v * 16) : make_uint4(0, 0, 0, 0);
+      vec_to_float<HT>(x, &h1[r][v * 8]);
+    }
+  }
+
+  for (int i = 0; i < n1; ++i, ++gi) {
+    const int s = gi % kFSlots;
+    const int rows = min(rpc1, nc - i * rpc1);
+    if (!mbar_wait(&S.mbar[s], (gi / kFSlots) & 1, a.copy_polls) && lane == 0)
+      atomicOr(&S.s_err, kErrCopyTimeout);
+    if (g1 < RG1) {
+      const unsigned char *base = ring + (size_t)s * kFSlotBytes + (size_t)col1 * 16;
+      for (int r = g1; r < rows; r += RG1) {
+        float w[VE1];
+        vec_to_float<WT>(lds128(base + (size_t)r * row1), w);
+#pragma unroll
+        for (int hr = 0; hr < R; ++hr) {
+          float acc = 0.f;
+#pragma unroll
+          for (int e = 0; e < VE1; ++e) acc = fmaf(w[e], h1[hr][e], acc);
+          acc = warp_sum(acc);
+          if (lane == 0) S.part[s][r][q1][hr] = acc;
+        }
+      }
+    }
+    __syncthreads();
+    if (tid < rows * R) {
+      const int r = tid / R, hr = tid - (tid / R) * R;
+      float acc = 0.f;
+      for (int q = 0; q < Q1; ++q) acc += S.part[s][r][q][hr];
+      const int k = c0 + i * rpc1 + r;
+      float sc = acc * (a.cscale ? a.cscale[k] : 1.f);
+      if (a.do_sample)
+        sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)hr, (uint32_t)k);
+      if (hr < a.rows) {
+        S.local[hr][k - c0] = sc;
+        a.scores[(size_t)hr * a.K + k] = sc;
+      }
+    }
+    if (tid == 0 && i + kFSlots < n1) issue1(i + kFSlots);
+  }
+  __syncthreads();
+  // Per-row finite min / max of this CTA's scores -> global atomic words.
+  if (warp < a.rows && warp < R) {
+    float mn = INFINITY, mx = -INFINITY;
+    for (int i = lane; i < nc; i += 32) {
+      const float v = S.local[warp][i];
+      if (isfinite(v)) {
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    }
+    if (lane == 0 && mx >= mn) {
+      atomicMax(&a.sync[kSyncMinMax + 2 * warp], ~mono(mn));
+      atomicMax(&a.sync[kSyncMinMax + 2 * warp + 1], mono(mx));
+    }
+  }
+
+  // ------------------------------------------------------------- grid barrier
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    atomicAdd(&a.sync[kSyncArrive], 1u);
+    const uint32_t target = (uint32_t)(G + a.extra_arrivals);
+    uint32_t polls = 0;
+    while (ld_acquire_gpu(&a.sync[kSyncArrive]) < target) {
+      if (++polls >= a.barrier_polls) {
+        atomicOr(&S.s_err, kErrBarrierTimeout);
+        break;
+      }
+      __nanosleep(32);
+    }
+    __threadfence();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------- select
+  const long long per_row = (long long)a.p * a.cap + a.n_special;
+  const long long W = per_row * a.rows;
+  const long long w0 = W * b / G, w1 = W * (b + 1) / G;
+  const int r_lo = (int)(w0 / per_row);
+  const int r_hi = w1 > w0 ? (int)((w1 - 1) / per_row) : r_lo - 1;
+  float *sc_sm = reinterpret_cast<float *>(ring);
+  for (int hr = r_lo; hr <= r_hi; ++hr) {
+    for (int i = tid; i < a.K; i += kFThreads) sc_sm[i] = __ldcg(&a.scores[(size_t)hr * a.K + i]);
+    const float vmin = unmono(~__ldcg(&a.sync[kSyncMinMax + 2 * hr]));
+    const float vmax = unmono(__ldcg(&a.sync[kSyncMinMax + 2 * hr + 1]));
+    __syncthreads();
+    fused_select(sc_sm, a.K, a.p, vmin, vmax, probes_sm + (hr - r_lo) * a.p, S);
+  }
+
+  // ------------------------------------------------------------------ stage 2
+  const int row3 = a.D * (int)sizeof(HT);
+  const int rpc3 = max(1, min(kFChunkRows, kFSlotBytes / row3));
+  const int NV3 = row3 / 16, Q3 = NV3 / 32, RG3 = kFWarps / Q3;
+  const int g3 = warp / Q3, q3 = warp % Q3, col3 = q3 * 32 + lane;
+  float h3[R][8];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const uint4 x = (r < a.rows && g3 < RG3)
+                        ? ldg_keep(reinterpret_cast<const char *>(a.hidden) +
+                                   (size_t)r * row3 + (size_t)col3 * 16)
+                        : make_uint4(0, 0, 0, 0);
+    vec_to_float<HT>(x, h3[r]);
+  }
+  const char *wp = reinterpret_cast<const char *>(a.w_perm);
+  // Producer cursor (thread 0) and consumer cursor (all threads) walk the same
+  // chunk sequence; a chunk is at most rpc3 rows contiguous in w_perm.
+  long long w_issue = w0, w_cons = w0;
+  int n_issued = 0;
+  auto issue3 = [&](uint32_t gidx) {
+    const S2Item it = s2_item(a, probes_sm, r_lo, w_issue, w1);
+    const int n = min(it.run, rpc3);
+    const int s = gidx % kFSlots;
+    fence_proxy_async_smem();
+    if (it.src >= 0) {
+      mbar_expect_tx(&S.mbar[s], (uint32_t)(n * row3));
+      bulk_g2s(ring + (size_t)s * kFSlotBytes, wp + (size_t)it.src * row3, (uint32_t)(n * row3),
+               &S.mbar[s]);
+    } else {
+      mbar_expect_tx(&S.mbar[s], 0u);  // invalid special slot: empty chunk
+    }
+    w_issue += n;
+  };
+  __syncthreads();  // ring free: selection done by every thread
+  if (tid == 0) {
+    uint32_t gidx = gi;
+    while (n_issued < kFSlots && w_issue < w1) {
+      issue3(gidx++);
+      ++n_issued;
+    }
+  }
+  while (w_cons < w1) {
+    const S2Item it = s2_item(a, probes_sm, r_lo, w_cons, w1);
+    const int n = min(it.run, rpc3);
+    const int s = gi % kFSlots;
+    if (!mbar_wait(&S.mbar[s], (gi / kFSlots) & 1, a.copy_polls) && lane == 0)
+      atomicOr(&S.s_err, kErrCopyTimeout);
+    const int hr = it.hrow;
+    if (it.src >= 0 && g3 < RG3) {
+      const unsigned char *base = ring + (size_t)s * kFSlotBytes + (size_t)col3 * 16;
+      for (int r = g3; r < n; r += RG3) {
+        float w[8];
+        vec_to_float<HT>(lds128(base + (size_t)r * row3), w);
+        float acc = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < R; ++hh) {
+          if (hh == hr) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc = fmaf(w[e], h3[hh][e], acc);
+          }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) S.part[s][r][q3][0] = acc;
+      }
+    }
+    __syncthreads();
+    if (it.src >= 0 && tid < n) {
+      float acc = 0.f;
+      for (int q = 0; q < Q3; ++q) acc += S.part[s][tid][q][0];
+      const long long src = it.src + tid;
+      const uint32_t vid = (uint32_t)a.vocab_map[src];
+      float key = acc;
+      if (a.do_sample)
+        key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)hr, vid);
+      atomicMax(&S.best[hr - r_lo], pack(key, vid));
+    }
+    w_cons += n;
+    ++gi;
+    if (tid == 0 && w_issue < w1) issue3(gi + kFSlots - 1);
+  }
+  __syncthreads();
+
+  // --------------------------------------------------------------- reduction
+  if (tid <= r_hi - r_lo && S.best[tid] != 0ull) atomicMax(&a.packed[r_lo + tid], S.best[tid]);
+  if (tid == 0 && S.s_err) atomicOr(&a.sync[kSyncError], S.s_err);
+  __syncthreads();
+  __shared__ uint32_t s_last;
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&a.sync[kSyncDone], 1u) == (uint32_t)G - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    if (tid < a.rows) {
+      const unsigned long long wv = atomicExch(&a.packed[tid], 0ull);
+      a.out_ids[tid] = wv ? (int64_t)packed_id(wv) : (int64_t)0xFFFFFFFFll;
+      a.sync[kSyncMinMax + 2 * tid] = 0u;
+      a.sync[kSyncMinMax + 2 * tid + 1] = 0u;
+    }
+    if (tid == 0) {
+      a.sync[kSyncArrive] = 0u;
+      a.sync[kSyncDone] = 0u;
+    }
+  }
+}
+
+}  // namespace fh

@@ -17,7 +17,7 @@
 #include <string>
 
 #include "../../include/flashhead.h"
-#include "fh_kernels.cuh"
+#include "fh_fused.cuh"
 
 namespace {
 
@@ -82,6 +82,69 @@ cudaError_t prepare_select() {
     g_select_attr_done[dev] = true;
   }
   return cudaSuccess;
+}
+
+// ---------------------------------------------------------------------------
+// One-kernel step (fh_fused.cuh): cooperative grid of one CTA per SM.
+// ---------------------------------------------------------------------------
+int g_sm_count[128];
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 0;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+template <typename HT, typename WT, int R>
+cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream) {
+  static bool attr_done[128];
+  auto kern = fh::k_fused_step<HT, WT, R>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (!attr_done[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fh::kFSmemBytes);
+      if (e != cudaSuccess) return e;
+      attr_done[dev] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(fh::kFThreads);
+  cfg.dynamicSmemBytes = fh::kFSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <typename HT, typename WT>
+cudaError_t launch_fused_rows(const fh::FusedArgs &a, int grid, cudaStream_t s) {
+  if (a.rows == 1) return launch_fused_t<HT, WT, 1>(a, grid, s);
+  if (a.rows == 2) return launch_fused_t<HT, WT, 2>(a, grid, s);
+  return launch_fused_t<HT, WT, 4>(a, grid, s);
+}
+
+cudaError_t launch_fused(int hdt, int wdt, const fh::FusedArgs &a, int grid, cudaStream_t s) {
+  if (hdt == FH_BF16) {
+    if (wdt == FH_FP8_E4M3) return launch_fused_rows<__nv_bfloat16, __nv_fp8_e4m3>(a, grid, s);
+    return launch_fused_rows<__nv_bfloat16, __nv_bfloat16>(a, grid, s);
+  }
+  if (wdt == FH_FP8_E4M3) return launch_fused_rows<__half, __nv_fp8_e4m3>(a, grid, s);
+  return launch_fused_rows<__half, __half>(a, grid, s);
 }
 
 }  // namespace
@@ -275,6 +338,54 @@ int run_stage1(const fh_head *h, const void *hidden, int rows, bool sample, floa
   return FH_OK;
 }
 
+// Shapes the one-kernel step supports; everything else takes the
+// three-kernel path.
+bool fused_ok(const fh_head_desc &d, int rows, bool sample, int grid) {
+  if (d.flags & FH_FLAG_NO_FUSED) return false;
+  if (rows < 1 || rows > fh::kFMaxRows || grid < rows || d.cluster_base != 0) return false;
+  const int wdt = sample ? d.sample_dtype : d.score_dtype;
+  const int nv1 = d.hidden * (wdt == FH_FP8_E4M3 ? 1 : 2) / 16;
+  const int nv3 = d.hidden * 2 / 16;
+  if (nv1 % 32 || nv1 > 512 || nv3 % 32 || nv3 > 512) return false;
+  if (d.n_clusters > 128 * grid || d.n_clusters > fh::kSelMaxItems) return false;
+  if (d.n_probes > fh::kFMaxProbes || d.cluster_size > fh::kFChunkRows) return false;
+  return true;
+}
+
+int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+              uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w, int grid,
+              cudaStream_t s) {
+  const fh_head_desc &d = h->d;
+  fh::FusedArgs a;
+  memset(&a, 0, sizeof(a));
+  a.hidden = hidden;
+  a.rows = rows;
+  a.D = d.hidden;
+  a.cw = sample ? d.centroid_w : d.cluster_w;
+  a.cscale = sample ? d.centroid_scale : d.cluster_scale;
+  a.K = d.n_clusters;
+  a.w_perm = d.w_perm;
+  a.vocab_map = d.vocab_map;
+  a.cap = d.cluster_size;
+  a.p = d.n_probes;
+  a.special_slots = d.special_slots;
+  a.n_special = d.n_special;
+  a.do_sample = sample ? 1 : 0;
+  a.temperature = temperature;
+  a.rng = rng_key(seed, offset);
+  a.scores = w.scores;
+  a.sync = reinterpret_cast<uint32_t *>(w.counter);
+  a.packed = w.packed;
+  a.out_ids = out_ids;
+  const bool test_timeout = (d.flags & FH_FLAG_TEST_TIMEOUT) != 0;
+  a.barrier_polls = test_timeout ? (1u << 14) : (1u << 25);
+  a.copy_polls = 1u << 22;
+  a.extra_arrivals = test_timeout ? 1 : 0;
+  const int wdt = sample ? d.sample_dtype : d.score_dtype;
+  FH_CHECK_LAUNCH(launch_fused(d.weight_dtype, wdt, a, grid, s), "one-kernel step launch");
+  return FH_OK;
+}
+
 int validate_desc(const fh_head_desc *d) {
   if (!d) return fail(FH_ERR_INVALID_ARGUMENT, "null descriptor");
   if (d->hidden <= 0 || d->hidden % 16 != 0)
@@ -336,6 +447,8 @@ FH_API int fh_head_destroy(fh_head *head) {
   return FH_OK;
 }
 
+FH_API size_t fh_workspace_error_offset(void) { return fh::kSyncError * sizeof(uint32_t); }
+
 FH_API size_t fh_workspace_bytes(const fh_head *head, int rows) {
   if (!head || rows < 0) return 0;
   return layout(head->d, rows, nullptr, 0).bytes;
@@ -348,6 +461,9 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
   if (st != FH_OK || rows == 0) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
+  const int grid = sm_count();
+  if (fused_ok(head->d, rows, false, grid))
+    return run_fused(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, grid, s);
   st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
   if (st != FH_OK) return st;
   fh::Stage2Args a = stage2_args(head->d, hidden, rows);
@@ -375,6 +491,9 @@ FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int
   if (st != FH_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
+  const int grid = sm_count();
+  if (fused_ok(head->d, rows, true, grid))
+    return run_fused(head, hidden, rows, true, temperature, seed, offset, out_ids, w, grid, s);
   st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
                   nullptr, 0, s);
   if (st != FH_OK) return st;

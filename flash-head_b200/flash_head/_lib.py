@@ -20,6 +20,9 @@ FH_ERR_CUDA = 2
 FH_ERR_WORKSPACE = 3
 FH_ERR_UNSUPPORTED = 4
 
+FH_FLAG_NO_FUSED = 1
+FH_FLAG_TEST_TIMEOUT = 2
+
 FH_BF16 = 0
 FH_FP16 = 1
 FH_FP8_E4M3 = 2
@@ -50,7 +53,7 @@ class HeadDesc(ctypes.Structure):
         ("sample_dtype", ctypes.c_int32),
         ("n_special", ctypes.c_int32),
         ("cluster_base", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
         ("w_perm", ctypes.c_void_p),
         ("vocab_map", ctypes.c_void_p),
         ("cluster_w", ctypes.c_void_p),
@@ -74,6 +77,7 @@ SIGNATURES = {
     "fh_head_create": (_I, [ctypes.POINTER(HeadDesc), ctypes.POINTER(_P)]),
     "fh_head_destroy": (_I, [_P]),
     "fh_workspace_bytes": (_SZ, [_P, _I]),
+    "fh_workspace_error_offset": (_SZ, []),
     "fh_get_next_token": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "fh_get_next_token_sample": (_I, [_P, _P, _I, _F, _U64, _U64, _P, _P, _SZ, _P]),
     "fh_top_clusters": (_I, [_P, _P, _I, _I, _F, _U64, _U64, _P, _P, _P, _SZ, _P]),

@@ -83,7 +83,7 @@ class NativeHead:
     """A validated ``fh_head`` over device buffers, plus its workspaces."""
 
     def __init__(self, bufs: dict, hidden: int, cluster_size: int, n_probes: int,
-                 cluster_base: int = 0):
+                 cluster_base: int = 0, flags: int = 0):
         self.bufs = bufs
         w = bufs["w_perm"]
         self.device = w.device
@@ -101,6 +101,7 @@ class NativeHead:
         sp = bufs["special_slots"]
         d.n_special = 0 if sp is None else sp.numel()
         d.cluster_base = cluster_base
+        d.flags = flags
         d.w_perm = w.data_ptr()
         d.vocab_map = bufs["vocab_map"].data_ptr()
         d.cluster_w = bufs["cluster_w"].data_ptr()
@@ -138,6 +139,21 @@ class NativeHead:
             ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=self.device)
             self._ws[idx] = ws
         return ws
+
+    def workspace_error(self, clear: bool = True) -> int:
+        """Error bits the one-kernel step recorded in this device's workspace
+        (bit 0 grid-barrier timeout, bit 1 copy timeout); synchronises."""
+        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        ws = self._ws.get(idx)
+        if ws is None:
+            return 0
+        off = int(self.lib.fh_workspace_error_offset())
+        word = ws[off:off + 4]
+        torch.cuda.synchronize(self.device)
+        val = int(word.view(torch.int32).item())
+        if clear:
+            word.zero_()
+        return val
 
     def _h(self, hidden: torch.Tensor) -> torch.Tensor:
         h = hidden.reshape(-1, self.D)

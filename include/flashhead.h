@@ -90,7 +90,7 @@ typedef struct fh_head_desc {
   int32_t sample_dtype; /* fh_dtype of centroid_w: FP8_E4M3 or weight_dtype */
   int32_t n_special;
   int32_t cluster_base;
-  int32_t reserved;
+  int32_t flags;        /* FH_FLAG_* bits, 0 by default */
   const void *w_perm;
   const int32_t *vocab_map;
   const void *cluster_w;
@@ -99,6 +99,12 @@ typedef struct fh_head_desc {
   const float *centroid_scale;
   const int32_t *special_slots;
 } fh_head_desc;
+
+/* fh_head_desc.flags */
+#define FH_FLAG_NO_FUSED 1u      /* always use the three-kernel path */
+#define FH_FLAG_TEST_TIMEOUT 2u  /* test only: the fused step's grid barrier
+                                    waits for one CTA more than it launches and
+                                    gives up after ~1 ms, setting error bit 1 */
 
 typedef struct fh_head fh_head; /* opaque, host memory only */
 
@@ -113,6 +119,15 @@ FH_API int fh_head_destroy(fh_head *head);
 
 /* Bytes of caller-provided scratch for a call with `rows` hidden states. */
 FH_API size_t fh_workspace_bytes(const fh_head *head, int rows);
+
+/*
+ * Byte offset, within a workspace, of a 32-bit word in which the one-kernel
+ * step (used for up to 4 rows) records failures of its bounded waits: bit 0
+ * = the grid barrier timed out, bit 1 = a bulk-copy wait timed out. The
+ * kernel still completes (its outputs are then meaningless). The word is
+ * sticky: the caller reads it (after synchronising) and clears it.
+ */
+FH_API size_t fh_workspace_error_offset(void);
 
 /*
  * Greedy next token for `rows` hidden states [rows, hidden]:

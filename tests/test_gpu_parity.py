@@ -384,3 +384,112 @@ def test_workspace_reuse_across_row_counts(llama1b_heads):
         a = nh.stage2_next_token(H, probes)
         b = nh.next_token(H)
         assert torch.equal(a, b), rows
+
+
+# ---------------------------------------------------------------------------
+# The one-kernel step (rows <= 4) against the oracle and the three-kernel path
+# ---------------------------------------------------------------------------
+
+def _native_pair(fh):
+    """The head's NativeHead and a twin that always takes the three-kernel path."""
+    from flash_head import _lib
+    from flash_head.native import NativeHead
+    nh = fh.native()
+    twin = NativeHead(nh.bufs, nh.D, nh.cap, nh.p, flags=_lib.FH_FLAG_NO_FUSED)
+    return nh, twin
+
+
+@pytest.mark.parametrize("rows", [1, 2, 3, 4])
+@pytest.mark.parametrize("stage1", ["model", "fp8"])
+def test_fused_step_matches_oracle(llama1b_heads, rows, stage1):
+    from flash_head.synthetic import make_hidden
+    fh = llama1b_heads[stage1]
+    nh, twin = _native_pair(fh)
+    for seed in range(3):
+        H = make_hidden(rows, fh._D, seed=700 + 10 * rows + seed, device="cuda")
+        fused = nh.next_token(H).cpu().numpy()
+        three = twin.next_token(H).cpu().numpy()
+        probes = nh.top_clusters(H).cpu().numpy()
+        check_greedy_rows(fh, H, fused, probes)
+        check_greedy_rows(fh, H, three, probes)
+    assert nh.workspace_error() == 0
+
+
+@pytest.mark.parametrize("K,cap,D,p", [(100, 16, 512, 1), (100, 16, 512, 100), (37, 4, 1024, 5),
+                                       (513, 8, 256, 40), (16384, 16, 512, 256),
+                                       (300, 16, 4096, 64)])
+def test_fused_step_shapes(K, cap, D, p):
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(K, cap, D)
+    for stage1 in ("model", "fp8"):
+        fh = build_head(head.weight, head.centroids, head.assignments, p, stage1=stage1)
+        nh, _ = _native_pair(fh)
+        for rows in (1, 3):
+            H = make_hidden(rows, D, seed=9 + rows, device="cuda")
+            toks = nh.next_token(H).cpu().numpy()
+            check_greedy_rows(fh, H, toks, nh.top_clusters(H).cpu().numpy())
+        assert nh.workspace_error() == 0
+
+
+def test_fused_step_special_tokens(golden_small):
+    """Fused path (D=64 is below its minimum, so use a D=512 head) with specials."""
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(256, 16, 512, seed=3)
+    specials = [0, 17, 4095]
+    fh = build_head(head.weight, head.centroids, head.assignments, 12, specials=specials,
+                    stage1="model")
+    nh, twin = _native_pair(fh)
+    ov = OracleView(fh)
+    for rows in (1, 2, 4):
+        H = make_hidden(rows, 512, seed=40 + rows, device="cuda")
+        Hn = to_np_f32(H)
+        probes = nh.top_clusters(H).cpu().numpy()
+        toks = nh.next_token(H).cpu().numpy()
+        for r in range(rows):
+            want = ov.greedy_given_probes(Hn[r], probes[r])
+            assert O.token_within_tolerance(toks[r], want, lambda v: ov.logit(Hn[r], v), 1e-5)
+    # a special token far outside the probed clusters still wins
+    sp = 4095
+    h = torch.from_numpy(ov.W[sp] * 50).to("cuda", torch.bfloat16).view(1, -1)
+    assert int(nh.next_token(h)[0]) == int(twin.next_token(h)[0])
+
+
+@pytest.mark.parametrize("stage1", ["model", "fp8"])
+def test_fused_sampling_matches_oracle_draw_for_draw(golden_small, stage1):
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(256, 16, 512, seed=8)
+    fh = build_head(head.weight, head.centroids, head.assignments, 12, stage1=stage1)
+    nh, _ = _native_pair(fh)
+    ov = OracleView(fh)
+    h = make_hidden(1, 512, seed=5, device="cuda", std=4.0)
+    hn = to_np_f32(h)[0]
+    cd = ov.sw * (ov.sscale[:, None] if ov.sscale is not None else 1.0)
+    n, agree = 300, 0
+    for off in range(n):
+        tok = int(nh.next_token(h, do_sample=True, temperature=0.7, seed=77, offset=off)[0])
+        agree += tok == O.sample_token(hn, ov.w_perm, ov.vm, cd, ov.p, 0.7, 77, off, 0)[0]
+    assert agree >= 0.98 * n
+
+
+def test_fused_barrier_timeout_is_reported_not_hung():
+    """The grid barrier of the one-kernel step waits with a poll limit. In the
+    test mode it waits for one CTA more than it launched: the wait must run
+    out, set error bit 0 in the workspace, and the kernel must still finish,
+    leaving the context and the workspace usable."""
+    from flash_head import _lib
+    from flash_head.native import NativeHead
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(300, 16, 512, seed=2)
+    fh = build_head(head.weight, head.centroids, head.assignments, 16, stage1="fp8")
+    nh = fh.native()
+    bad = NativeHead(nh.bufs, nh.D, nh.cap, nh.p, flags=_lib.FH_FLAG_TEST_TIMEOUT)
+    H = make_hidden(1, 512, seed=1, device="cuda")
+    bad.next_token(H)
+    torch.cuda.synchronize()
+    assert bad.workspace_error() & 1
+    assert bad.workspace_error() == 0  # cleared by the read
+    # same workspace afterwards, normal head: correct results
+    bad._ws = nh._ws
+    toks = nh.next_token(H).cpu().numpy()
+    check_greedy_rows(fh, H, toks, nh.top_clusters(H).cpu().numpy())
+    assert nh.workspace_error() == 0
