@@ -447,6 +447,11 @@ FH_API int fh_head_destroy(fh_head *head) {
   return FH_OK;
 }
 
+FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample) {
+  if (!head || rows <= 0) return 0;
+  return fused_ok(head->d, rows, do_sample != 0, sm_count()) ? 1 : 3;
+}
+
 FH_API size_t fh_workspace_error_offset(void) { return fh::kSyncError * sizeof(uint32_t); }
 
 FH_API size_t fh_workspace_bytes(const fh_head *head, int rows) {

@@ -140,6 +140,10 @@ class NativeHead:
             self._ws[idx] = ws
         return ws
 
+    def step_kernel_count(self, rows: int, do_sample: bool = False) -> int:
+        """Launches per step for `rows` rows: 1 (one-kernel step) or 3."""
+        return int(self.lib.fh_step_kernel_count(self.handle, rows, int(bool(do_sample))))
+
     def workspace_error(self, clear: bool = True) -> int:
         """Error bits the one-kernel step recorded in this device's workspace
         (bit 0 grid-barrier timeout, bit 1 copy timeout); synchronises."""

@@ -130,6 +130,13 @@ FH_API size_t fh_workspace_bytes(const fh_head *head, int rows);
 FH_API size_t fh_workspace_error_offset(void);
 
 /*
+ * Kernel launches one fh_get_next_token / fh_get_next_token_sample call makes
+ * for `rows` hidden states on the current device: 1 when the one-kernel step
+ * applies (rows <= 4 and supported shapes), else 3.
+ */
+FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample);
+
+/*
  * Greedy next token for `rows` hidden states [rows, hidden]:
  * out_ids[rows] (int64). Replaces FlashHead.get_next_token(h) on its fused
  * greedy branch (flash_head.py:277-321: cluster_linear + topk +

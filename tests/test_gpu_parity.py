@@ -488,8 +488,8 @@ def test_fused_barrier_timeout_is_reported_not_hung():
     torch.cuda.synchronize()
     assert bad.workspace_error() & 1
     assert bad.workspace_error() == 0  # cleared by the read
-    # same workspace afterwards, normal head: correct results
-    bad._ws = nh._ws
+    # the timed-out workspace, reused by the normal head: correct results
+    nh._ws = dict(bad._ws)
     toks = nh.next_token(H).cpu().numpy()
     check_greedy_rows(fh, H, toks, nh.top_clusters(H).cpu().numpy())
     assert nh.workspace_error() == 0
