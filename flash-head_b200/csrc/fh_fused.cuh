@@ -7,15 +7,17 @@
 //               [b*K/G, (b+1)*K/G) through a 4-slot ring of shared-memory
 //               buffers filled by bulk asynchronous copies (TMA engine,
 //               completion on mbarriers) and scores them against the R hidden
-//               rows held in registers; scores go to global memory and the
-//               per-row min/max to two atomic words.
+//               rows held in registers; scores go to global memory and
+//               their keys into global histograms (see 3).
 //  2. barrier   one arrive counter, bounded spin (a timeout sets an error
 //               bit and the kernel still runs to completion).
-//  3. select    every CTA redundantly selects the top-p clusters of the
-//               hidden rows its stage-2 share needs, from the L2-resident
-//               scores, with a 512-bin histogram over [min, max] and an exact
-//               ranking of the threshold bin. Redundant selection costs no
-//               second grid-wide dependency.
+//  3. select    stage 1 also built global two-level histograms of the
+//               score keys (256 coarse x 256 fine bins = bf16 resolution),
+//               so after the barrier every CTA finds the threshold bin from
+//               two 1 KB reads, ranks the few keys that share its 16-bit
+//               prefix exactly and compacts the selected ids from the
+//               L2-resident scores. Redundant selection costs no second
+//               grid-wide dependency.
 //  4. stage 2   the R * (p * cap + n_special) w_perm rows to score are split
 //               evenly across CTAs in (row, probe, slot) order; each CTA
 //               streams its contiguous runs through the same ring, packs
@@ -42,7 +44,14 @@ constexpr int kFMaxProbes = 4096;
 constexpr int kSyncArrive = 1;
 constexpr int kSyncDone = 2;
 constexpr int kSyncError = 3;
-constexpr int kSyncMinMax = 8;  // [8 + 2r] = max(~mono(min)), [9 + 2r] = max(mono(max))
+constexpr int kSyncEpoch = 4;
+
+// Two-level key histograms per hidden row: 256 coarse bins (key >> 24) then
+// 65536 fine bins (key >> 16, i.e. bf16 resolution). Two buffers alternate
+// by call epoch; each call zeroes the buffer the next call will use.
+constexpr int kHistCoarse = 256;
+constexpr int kHistWords = kHistCoarse + 65536;
+constexpr size_t kHistBytes = 2ull * kFMaxRows * kHistWords * sizeof(uint32_t);
 
 constexpr uint32_t kErrBarrierTimeout = 1u;
 constexpr uint32_t kErrCopyTimeout = 2u;
@@ -65,6 +74,7 @@ struct FusedArgs {
   RngKey rng;
   float *scores;       // [R, K] global scratch
   uint32_t *sync;      // workspace state words
+  uint32_t *hist;      // [2][kFMaxRows][kHistWords] key histograms
   unsigned long long *packed;  // [R]
   int64_t *out_ids;    // [R]
   uint32_t barrier_polls;      // grid-barrier poll limit
@@ -76,11 +86,12 @@ struct FusedSmem {
   uint64_t mbar[kFSlots];
   float part[kFSlots][kFChunkRows][16][kFMaxRows];
   float local[kFMaxRows][128];
+  uint32_t coarse[kFMaxRows][kHistCoarse];
   uint32_t hist[kFBins];
   unsigned long long cand[kFCand];
   unsigned long long best[2];
   int scan[33];
-  int s_bstar, s_above, s_cnt, s_ncand;
+  int s_bstar, s_above, s_cnt, s_ncand, s_cb, s_fb;
   unsigned long long s_T, s_kmin, s_kmax;
   uint32_t s_err;
 };
@@ -340,25 +351,24 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     if (tid == 0 && i + kFSlots < n1) issue1(i + kFSlots);
   }
   __syncthreads();
-  // Per-row finite min / max of this CTA's scores -> global atomic words.
-  if (warp < a.rows && warp < R) {
-    float mn = INFINITY, mx = -INFINITY;
-    for (int i = lane; i < nc; i += 32) {
-      const float v = S.local[warp][i];
-      if (isfinite(v)) {
-        mn = fminf(mn, v);
-        mx = fmaxf(mx, v);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
-      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-    }
-    if (lane == 0 && mx >= mn) {
-      atomicMax(&a.sync[kSyncMinMax + 2 * warp], ~mono(mn));
-      atomicMax(&a.sync[kSyncMinMax + 2 * warp + 1], mono(mx));
-    }
+  // Publish this CTA's keys to the global two-level histograms of its rows:
+  // fine bins directly, coarse bins aggregated in shared memory first (they
+  // are few and hot).
+  const uint32_t epoch = __ldcg(&a.sync[kSyncEpoch]);
+  uint32_t *hist_cur = a.hist + (size_t)(epoch & 1u) * kFMaxRows * kHistWords;
+  uint32_t *hist_next = a.hist + (size_t)((epoch + 1u) & 1u) * kFMaxRows * kHistWords;
+  for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFThreads) (&S.coarse[0][0])[i] = 0u;
+  __syncthreads();
+  for (int i = tid; i < a.rows * nc; i += kFThreads) {
+    const int hr = i / nc, k = i - (i / nc) * nc;
+    const uint32_t key = mono(sanitize(S.local[hr][k]));
+    atomicAdd(&hist_cur[(size_t)hr * kHistWords + kHistCoarse + (key >> 16)], 1u);
+    atomicAdd(&S.coarse[hr][key >> 24], 1u);
+  }
+  __syncthreads();
+  for (int i = tid; i < a.rows * kHistCoarse; i += kFThreads) {
+    const uint32_t c = (&S.coarse[0][0])[i];
+    if (c) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], c);
   }
 
   // ------------------------------------------------------------- grid barrier
@@ -388,10 +398,89 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   float *sc_sm = reinterpret_cast<float *>(ring);
   for (int hr = r_lo; hr <= r_hi; ++hr) {
     for (int i = tid; i < a.K; i += kFThreads) sc_sm[i] = __ldcg(&a.scores[(size_t)hr * a.K + i]);
-    const float vmin = unmono(~__ldcg(&a.sync[kSyncMinMax + 2 * hr]));
-    const float vmax = unmono(__ldcg(&a.sync[kSyncMinMax + 2 * hr + 1]));
-    __syncthreads();
-    fused_select(sc_sm, a.K, a.p, vmin, vmax, probes_sm + (hr - r_lo) * a.p, S);
+    const uint32_t *h1g = hist_cur + (size_t)hr * kHistWords;
+    // Defaults keep every index in range even when the histogram is
+    // incomplete (a timed-out barrier); the scan's first barrier publishes them.
+    if (tid == 0) {
+      S.s_cb = 0;
+      S.s_fb = 0;
+      S.s_cnt = 0;
+      S.s_above = 0;
+      S.s_T = ~0ull;
+    }
+    // coarse level: thread t owns bin 255 - t (highest first)
+    int need = a.p;
+    {
+      const int c = tid < kHistCoarse ? (int)__ldcg(&h1g[kHistCoarse - 1 - tid]) : 0;
+      int total;
+      const int before = block_exclusive_scan(c, S.scan, &total);
+      if (before < need && need <= before + c) {
+        S.s_cb = kHistCoarse - 1 - tid;
+        S.s_above = before;
+      }
+      __syncthreads();
+    }
+    need -= S.s_above;
+    const int cb = min(max(S.s_cb, 0), kHistCoarse - 1);
+    {
+      const int f = tid < 256 ? (int)__ldcg(&h1g[kHistCoarse + cb * 256 + 255 - tid]) : 0;
+      int total;
+      const int before = block_exclusive_scan(f, S.scan, &total);
+      if (before < need && need <= before + f) {
+        S.s_fb = 255 - tid;
+        S.s_above = before;
+        S.s_cnt = f;
+      }
+      if (tid == 0) S.s_ncand = 0;
+      __syncthreads();
+    }
+    need -= S.s_above;
+    const uint32_t prefix = (uint32_t)(cb * 256 + (S.s_fb & 255));
+    const int cnt = S.s_cnt;
+    int *probes_out = probes_sm + (hr - r_lo) * a.p;
+    if (cnt <= kFCand) {
+      // exact ranking of the keys that share the threshold's 16-bit prefix
+      for (int i = tid; i < a.K; i += kFThreads) {
+        const float v = sanitize(sc_sm[i]);
+        if ((mono(v) >> 16) == prefix) {
+          const int pos = atomicAdd(&S.s_ncand, 1);
+          if (pos < kFCand) S.cand[pos] = pack(v, (uint32_t)i);
+        }
+      }
+      __syncthreads();
+      const int nc2 = min(cnt, kFCand);
+      if (tid < nc2) {
+        const unsigned long long mine = S.cand[tid];
+        int rank = 0;
+        for (int j = 0; j < nc2; ++j) rank += S.cand[j] > mine;
+        if (rank == need - 1) S.s_T = mine;
+      }
+      __syncthreads();
+      const unsigned long long T = S.s_T;
+      const int per = (a.K + kFThreads - 1) / kFThreads;
+      const int i0 = min(a.K, tid * per), i1 = min(a.K, i0 + per);
+      int mine = 0;
+      for (int i = i0; i < i1; ++i) mine += pack(sanitize(sc_sm[i]), (uint32_t)i) >= T;
+      int total;
+      int pos = block_exclusive_scan(mine, S.scan, &total);
+      for (int i = i0; i < i1; ++i) {
+        if (pack(sanitize(sc_sm[i]), (uint32_t)i) >= T) {
+          if (pos < a.p) probes_out[pos] = i;
+          ++pos;
+        }
+      }
+      __syncthreads();
+    } else {
+      // many keys share the threshold's bf16 prefix: full refinement
+      fused_select(sc_sm, a.K, a.p, -INFINITY, -INFINITY, probes_out, S);
+    }
+  }
+  // Zero the histogram buffer the next call will use (this call never reads it).
+  {
+    const size_t n4 = (size_t)kFMaxRows * kHistWords / 4;
+    uint4 *z = reinterpret_cast<uint4 *>(hist_next);
+    for (size_t i = (size_t)b * n4 / G + tid; i < (size_t)(b + 1) * n4 / G; i += kFThreads)
+      z[i] = make_uint4(0, 0, 0, 0);
   }
 
   // ------------------------------------------------------------------ stage 2
@@ -491,12 +580,11 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     if (tid < a.rows) {
       const unsigned long long wv = atomicExch(&a.packed[tid], 0ull);
       a.out_ids[tid] = wv ? (int64_t)packed_id(wv) : (int64_t)0xFFFFFFFFll;
-      a.sync[kSyncMinMax + 2 * tid] = 0u;
-      a.sync[kSyncMinMax + 2 * tid + 1] = 0u;
     }
     if (tid == 0) {
       a.sync[kSyncArrive] = 0u;
       a.sync[kSyncDone] = 0u;
+      a.sync[kSyncEpoch] = epoch + 1u;
     }
   }
 }

@@ -164,11 +164,14 @@ struct Workspace {
   int32_t *probes;              // [rows, p]
   unsigned long long *packed;   // [rows]
   unsigned *counter;            // [1]
+  uint32_t *hist;               // one-kernel key histograms
   size_t bytes;                 // bytes needed for `rows`
 };
 
-// Persistent state first, at offsets that do not depend on `rows`: the
-// last-CTA counter at 0 and the stage-2 accumulator packed[r] at 256 + 8r.
+// Persistent state first, at offsets that do not depend on `rows`: state
+// words at 0 (three-kernel stage-2 counter, one-kernel barrier / done /
+// error / epoch words), the one-kernel step's key histograms at 256, then the
+// stage-2 accumulator packed[r].
 // Stage 2 leaves both zeroed when it completes, so a workspace zero-filled
 // once stays clean across calls with any row count. Per-call scratch
 // (probes, scores) is placed from the top of the buffer downwards and never
@@ -177,12 +180,14 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   Workspace w;
   char *p = reinterpret_cast<char *>(base);
   w.score_stride = (int)round_up((size_t)d.n_clusters, 64);
-  const size_t state = 256 + round_up((size_t)rows * sizeof(unsigned long long), 256);
+  const size_t state =
+      256 + fh::kHistBytes + round_up((size_t)rows * sizeof(unsigned long long), 256);
   const size_t probes = round_up((size_t)rows * d.n_probes * sizeof(int32_t), 256);
   const size_t scores = round_up((size_t)rows * w.score_stride * sizeof(float), 256);
   w.bytes = state + probes + scores + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
-  w.packed = reinterpret_cast<unsigned long long *>(p + 256);
+  w.hist = reinterpret_cast<uint32_t *>(p + 256);
+  w.packed = reinterpret_cast<unsigned long long *>(p + 256 + fh::kHistBytes);
   const size_t top = (ws_bytes / 256) * 256;
   const size_t probes_off = top >= probes ? top - probes : 0;
   const size_t scores_off = probes_off >= scores ? probes_off - scores : 0;
@@ -375,6 +380,7 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
   a.rng = rng_key(seed, offset);
   a.scores = w.scores;
   a.sync = reinterpret_cast<uint32_t *>(w.counter);
+  a.hist = w.hist;
   a.packed = w.packed;
   a.out_ids = out_ids;
   const bool test_timeout = (d.flags & FH_FLAG_TEST_TIMEOUT) != 0;
