@@ -258,4 +258,37 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *scratch, int *to
   return before + x - v;
 }
 
+// Ordered stream compaction over ids [0, N): calls emit(pos, i) for every i
+// with pred(i), pos = rank of i among the selected ids (ascending). Warp w
+// owns a contiguous id range and walks it 32 ids at a time (lane = id % 32,
+// so shared-memory reads inside pred are conflict-free); ballots give the
+// in-warp ranks and one barrier the cross-warp offsets. `warp_counts` holds
+// one int per warp. Ends with __syncthreads().
+template <typename Pred, typename Emit>
+__device__ __forceinline__ void block_ordered_compact(int N, Pred pred, Emit emit,
+                                                      int *warp_counts) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int per = (N + nw - 1) / nw;
+  const int lo = min(N, warp * per), hi = min(N, lo + per);
+  int cnt = 0;
+  for (int base = lo; base < hi; base += 32) {
+    const int i = base + lane;
+    cnt += __popc(__ballot_sync(0xFFFFFFFFu, i < hi && pred(i)));
+  }
+  __syncthreads();  // warp_counts may still be read by a previous use
+  if (lane == 0) warp_counts[warp] = cnt;
+  __syncthreads();
+  int off = 0;
+  for (int w = 0; w < warp; ++w) off += warp_counts[w];
+  for (int base = lo; base < hi; base += 32) {
+    const int i = base + lane;
+    const bool f = i < hi && pred(i);
+    const unsigned m = __ballot_sync(0xFFFFFFFFu, f);
+    if (f) emit(off + __popc(m & ((1u << lane) - 1u)), i);
+    off += __popc(m);
+  }
+  __syncthreads();
+}
+
 }  // namespace fh

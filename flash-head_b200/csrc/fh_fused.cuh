@@ -86,6 +86,7 @@ struct FusedSmem {
   uint64_t mbar[kFSlots];
   float part[kFSlots][kFChunkRows][16][kFMaxRows];
   float local[kFMaxRows][128];
+  float scale[128];
   uint32_t coarse[kFMaxRows][kHistCoarse];
   uint32_t hist[kFBins];
   unsigned long long cand[kFCand];
@@ -96,8 +97,10 @@ struct FusedSmem {
   uint32_t s_err;
 };
 
+constexpr int kFVidCache = 4096;  // vocab ids of a CTA's stage-2 rows, prefetched
 constexpr size_t kFRingBytes = (size_t)kFSlots * kFSlotBytes;
-constexpr size_t kFSmemBytes = kFRingBytes + sizeof(FusedSmem) + 2ull * kFMaxProbes * 4;
+constexpr size_t kFSmemBytes =
+    kFRingBytes + sizeof(FusedSmem) + 2ull * kFMaxProbes * 4 + (size_t)kFVidCache * 4;
 
 template <typename T>
 __device__ __forceinline__ void vec_to_float(const uint4 &v, float *f);
@@ -217,20 +220,13 @@ __device__ void fused_select(const float *sc, int K, int p, float vmin, float vm
     __syncthreads();
     (void)warp;
   }
-  // Compaction in id order: thread t owns a contiguous run of ids.
-  const int per = (K + kFThreads - 1) / kFThreads;
-  const int i0 = min(K, tid * per), i1 = min(K, i0 + per);
-  int mine = 0;
-  for (int i = i0; i < i1; ++i) mine += key_of(i) >= T;
-  int total;
-  int pos = block_exclusive_scan(mine, S.scan, &total);
-  for (int i = i0; i < i1; ++i) {
-    if (key_of(i) >= T) {
-      if (pos < p) out[pos] = i;
-      ++pos;
-    }
-  }
-  __syncthreads();
+  // Compaction in id order.
+  block_ordered_compact(
+      K, [&](int i) { return key_of(i) >= T; },
+      [&](int pos, int i) {
+        if (pos < p) out[pos] = i;
+      },
+      S.scan);
 }
 
 // Stage-2 work walk: work index w of row-major (hidden row, probe, slot) items,
@@ -261,12 +257,28 @@ __device__ __forceinline__ S2Item s2_item(const FusedArgs &a, const int *probes_
   return it;
 }
 
+#ifdef FH_TRACE
+// Profiling builds only: per-CTA %globaltimer stamps at phase boundaries.
+__device__ unsigned long long *g_fh_trace;
+__device__ __forceinline__ void trace_stamp(int phase) {
+  if (threadIdx.x == 0 && g_fh_trace) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_fh_trace[blockIdx.x * 8 + phase] = t;
+  }
+}
+#define FH_STAMP(p) trace_stamp(p)
+#else
+#define FH_STAMP(p) ((void)0)
+#endif
+
 template <typename HT, typename WT, int R>
 __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char *ring = smem;
   FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem + kFRingBytes);
   int *probes_sm = reinterpret_cast<int *>(smem + kFRingBytes + sizeof(FusedSmem));
+  int *vid_sm = probes_sm + 2 * kFMaxProbes;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x;
@@ -277,6 +289,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     S.best[0] = S.best[1] = 0ull;
   }
   __syncthreads();
+  FH_STAMP(0);
 
   // ------------------------------------------------------------------ stage 1
   const int c0 = (int)((long long)b * a.K / G), c1 = (int)((long long)(b + 1) * a.K / G);
@@ -297,6 +310,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   };
   if (tid == 0)
     for (int i = 0; i < min(kFSlots, n1); ++i) issue1(i);
+  if (tid < nc) S.scale[tid] = a.cscale ? a.cscale[c0 + tid] : 1.f;
 
   constexpr int VE1 = Vec<WT>::kElems;
   const int NV1 = row1 / 16, Q1 = NV1 / 32, RG1 = kFWarps / Q1;
@@ -340,7 +354,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       float acc = 0.f;
       for (int q = 0; q < Q1; ++q) acc += S.part[s][r][q][hr];
       const int k = c0 + i * rpc1 + r;
-      float sc = acc * (a.cscale ? a.cscale[k] : 1.f);
+      float sc = acc * S.scale[k - c0];
       if (a.do_sample)
         sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)hr, (uint32_t)k);
       if (hr < a.rows) {
@@ -351,6 +365,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     if (tid == 0 && i + kFSlots < n1) issue1(i + kFSlots);
   }
   __syncthreads();
+  FH_STAMP(1);
   // Publish this CTA's keys to the global two-level histograms of its rows:
   // fine bins directly, coarse bins aggregated in shared memory first (they
   // are few and hot).
@@ -373,6 +388,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
 
   // ------------------------------------------------------------- grid barrier
   __syncthreads();
+  FH_STAMP(2);
   if (tid == 0) {
     __threadfence();
     atomicAdd(&a.sync[kSyncArrive], 1u);
@@ -383,11 +399,11 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         atomicOr(&S.s_err, kErrBarrierTimeout);
         break;
       }
-      __nanosleep(32);
     }
     __threadfence();
   }
   __syncthreads();
+  FH_STAMP(3);
 
   // ------------------------------------------------------------------- select
   const long long per_row = (long long)a.p * a.cap + a.n_special;
@@ -397,8 +413,25 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   const int r_hi = w1 > w0 ? (int)((w1 - 1) / per_row) : r_lo - 1;
   float *sc_sm = reinterpret_cast<float *>(ring);
   for (int hr = r_lo; hr <= r_hi; ++hr) {
-    for (int i = tid; i < a.K; i += kFThreads) sc_sm[i] = __ldcg(&a.scores[(size_t)hr * a.K + i]);
     const uint32_t *h1g = hist_cur + (size_t)hr * kHistWords;
+    // All loads of this row's scores (and its coarse histogram) in flight at once.
+    const uint32_t coarse_v = tid < kHistCoarse ? __ldcg(&h1g[kHistCoarse - 1 - tid]) : 0u;
+    {
+      const float *src = a.scores + (size_t)hr * a.K;
+      for (int base = 0; base < a.K; base += kFThreads * 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = base + u * kFThreads + tid;
+          v[u] = i < a.K ? __ldcg(&src[i]) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = base + u * kFThreads + tid;
+          if (i < a.K) sc_sm[i] = v[u];
+        }
+      }
+    }
     // Defaults keep every index in range even when the histogram is
     // incomplete (a timed-out barrier); the scan's first barrier publishes them.
     if (tid == 0) {
@@ -411,7 +444,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     // coarse level: thread t owns bin 255 - t (highest first)
     int need = a.p;
     {
-      const int c = tid < kHistCoarse ? (int)__ldcg(&h1g[kHistCoarse - 1 - tid]) : 0;
+      const int c = (int)coarse_v;
       int total;
       const int before = block_exclusive_scan(c, S.scan, &total);
       if (before < need && need <= before + c) {
@@ -457,19 +490,12 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       }
       __syncthreads();
       const unsigned long long T = S.s_T;
-      const int per = (a.K + kFThreads - 1) / kFThreads;
-      const int i0 = min(a.K, tid * per), i1 = min(a.K, i0 + per);
-      int mine = 0;
-      for (int i = i0; i < i1; ++i) mine += pack(sanitize(sc_sm[i]), (uint32_t)i) >= T;
-      int total;
-      int pos = block_exclusive_scan(mine, S.scan, &total);
-      for (int i = i0; i < i1; ++i) {
-        if (pack(sanitize(sc_sm[i]), (uint32_t)i) >= T) {
-          if (pos < a.p) probes_out[pos] = i;
-          ++pos;
-        }
-      }
-      __syncthreads();
+      block_ordered_compact(
+          a.K, [&](int i) { return pack(sanitize(sc_sm[i]), (uint32_t)i) >= T; },
+          [&](int pos, int i) {
+            if (pos < a.p) probes_out[pos] = i;
+          },
+          S.scan);
     } else {
       // many keys share the threshold's bf16 prefix: full refinement
       fused_select(sc_sm, a.K, a.p, -INFINITY, -INFINITY, probes_out, S);
@@ -483,6 +509,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       z[i] = make_uint4(0, 0, 0, 0);
   }
 
+  FH_STAMP(4);
   // ------------------------------------------------------------------ stage 2
   const int row3 = a.D * (int)sizeof(HT);
   const int rpc3 = max(1, min(kFChunkRows, kFSlotBytes / row3));
@@ -516,6 +543,12 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     }
     w_issue += n;
   };
+  // Vocab ids of this CTA's stage-2 rows, fetched once (off the per-chunk path).
+  const int n_vid = (int)min((long long)kFVidCache, w1 - w0);
+  for (int t = tid; t < n_vid; t += kFThreads) {
+    const S2Item it = s2_item(a, probes_sm, r_lo, w0 + t, w0 + t + 1);
+    vid_sm[t] = it.src >= 0 ? a.vocab_map[it.src] : 0;
+  }
   __syncthreads();  // ring free: selection done by every thread
   if (tid == 0) {
     uint32_t gidx = gi;
@@ -553,7 +586,8 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       float acc = 0.f;
       for (int q = 0; q < Q3; ++q) acc += S.part[s][tid][q][0];
       const long long src = it.src + tid;
-      const uint32_t vid = (uint32_t)a.vocab_map[src];
+      const long long wi = w_cons - w0 + tid;
+      const uint32_t vid = (uint32_t)(wi < n_vid ? vid_sm[wi] : a.vocab_map[src]);
       float key = acc;
       if (a.do_sample)
         key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)hr, vid);
@@ -564,6 +598,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     if (tid == 0 && w_issue < w1) issue3(gi + kFSlots - 1);
   }
   __syncthreads();
+  FH_STAMP(5);
 
   // --------------------------------------------------------------- reduction
   if (tid <= r_hi - r_lo && S.best[tid] != 0ull) atomicMax(&a.packed[r_lo + tid], S.best[tid]);
@@ -575,6 +610,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     s_last = atomicAdd(&a.sync[kSyncDone], 1u) == (uint32_t)G - 1;
   }
   __syncthreads();
+  FH_STAMP(6);
   if (s_last) {
     __threadfence();
     if (tid < a.rows) {

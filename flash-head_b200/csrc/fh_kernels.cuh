@@ -353,23 +353,17 @@ __global__ void __launch_bounds__(kSelThreads) k_select(SelectArgs a) {
     __syncthreads();
   }
 
-  // Compaction in item order: thread t owns a contiguous run of items.
-  const int per = (N + blockDim.x - 1) / blockDim.x;
-  const int i0 = min(N, tid * per), i1 = min(N, i0 + per);
-  int mine = 0;
-  for (int i = i0; i < i1; ++i) mine += skeys[i] >= T;
-  int total;
-  int pos = block_exclusive_scan(mine, scan_scratch, &total);
-  for (int i = i0; i < i1; ++i) {
-    const unsigned long long k = skeys[i];
-    if (k >= T) {
-      if (pos < a.p) {
-        if (a.probes) a.probes[(size_t)row * a.p + pos] = (int32_t)packed_id(k);
-        if (a.cand_out) a.cand_out[(size_t)row * a.p + pos] = to_signed(k);
-      }
-      ++pos;
-    }
-  }
+  // Compaction in item order (ascending cluster id in dense mode).
+  block_ordered_compact(
+      N, [&](int i) { return skeys[i] >= T; },
+      [&](int pos, int i) {
+        if (pos < a.p) {
+          const unsigned long long k = skeys[i];
+          if (a.probes) a.probes[(size_t)row * a.p + pos] = (int32_t)packed_id(k);
+          if (a.cand_out) a.cand_out[(size_t)row * a.p + pos] = to_signed(k);
+        }
+      },
+      scan_scratch);
 }
 
 // ===========================================================================

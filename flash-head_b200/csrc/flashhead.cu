@@ -384,7 +384,7 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
   a.packed = w.packed;
   a.out_ids = out_ids;
   const bool test_timeout = (d.flags & FH_FLAG_TEST_TIMEOUT) != 0;
-  a.barrier_polls = test_timeout ? (1u << 14) : (1u << 25);
+  a.barrier_polls = test_timeout ? (1u << 12) : (1u << 22);
   a.copy_polls = 1u << 22;
   a.extra_arrivals = test_timeout ? 1 : 0;
   const int wdt = sample ? d.sample_dtype : d.score_dtype;
@@ -433,6 +433,14 @@ int validate_desc(const fh_head_desc *d) {
 extern "C" {
 
 FH_API int fh_version(void) { return 1; }
+
+#ifdef FH_TRACE
+// Profiling builds only (not declared in the public header).
+FH_API int fh_debug_set_trace(void *buf) {
+  const cudaError_t e = cudaMemcpyToSymbol(fh::g_fh_trace, &buf, sizeof(buf));
+  return e == cudaSuccess ? FH_OK : cuda_fail(e, "trace buffer");
+}
+#endif
 
 FH_API const char *fh_last_error(void) { return g_last_error.c_str(); }
 
