@@ -82,6 +82,15 @@ struct FusedArgs {
   int extra_arrivals;          // >0 only in the timeout test: wait for more CTAs than exist
 };
 
+// One stage-2 chunk: up to rpc3 w_perm rows contiguous in memory.
+struct S2Chunk {
+  int src;   // first w_perm row, -1 for an invalid special slot
+  int w;     // first work index
+  short n;   // rows
+  short hrow;
+};
+constexpr int kFMaxChunks = 384;
+
 struct FusedSmem {
   uint64_t mbar[kFSlots];
   float part[kFSlots][kFChunkRows][16][kFMaxRows];
@@ -90,6 +99,8 @@ struct FusedSmem {
   uint32_t coarse[kFMaxRows][kHistCoarse];
   uint32_t hist[kFBins];
   unsigned long long cand[kFCand];
+  S2Chunk chunks[kFMaxChunks];
+  int s_nchunks;
   unsigned long long best[2];
   int scan[33];
   int s_bstar, s_above, s_cnt, s_ncand, s_cb, s_fb;
@@ -230,28 +241,28 @@ __device__ void fused_select(const float *sc, int K, int p, float vmin, float vm
 }
 
 // Stage-2 work walk: work index w of row-major (hidden row, probe, slot) items,
-// then the special tokens of each hidden row. Returns the w_perm row of w and
-// how many following work items are contiguous in w_perm (run length).
+// then the special tokens of each hidden row. Returns the w_perm row of w
+// (-1 if invalid) and how many following work items are contiguous in w_perm.
 struct S2Item {
-  long long src;  // w_perm row, -1 if invalid
+  int src;
   int run;
   int hrow;
 };
 
 __device__ __forceinline__ S2Item s2_item(const FusedArgs &a, const int *probes_sm, int r_lo,
-                                          long long w, long long w_end) {
-  const long long per_row = (long long)a.p * a.cap + a.n_special;
+                                          int w, int w_end) {
+  const int per_row = a.p * a.cap + a.n_special;
   S2Item it;
-  it.hrow = (int)(w / per_row);
-  const long long j = w - (long long)it.hrow * per_row;
-  if (j < (long long)a.p * a.cap) {
-    const int pi = (int)(j / a.cap), sl = (int)(j - (long long)pi * a.cap);
+  it.hrow = w / per_row;
+  const int j = w - it.hrow * per_row;
+  if (j < a.p * a.cap) {
+    const int pi = j / a.cap, sl = j - pi * a.cap;
     const int cl = probes_sm[(it.hrow - r_lo) * a.p + pi];
-    it.src = (long long)cl * a.cap + sl;
-    it.run = (int)min((long long)(a.cap - sl), w_end - w);
+    it.src = (cl >= 0 && cl < a.K) ? cl * a.cap + sl : -1;
+    it.run = min(a.cap - sl, w_end - w);
   } else {
-    const long long sp = a.special_slots[j - (long long)a.p * a.cap];
-    it.src = (sp >= 0 && sp < (long long)a.K * a.cap) ? sp : -1;
+    const int sp = a.special_slots[j - a.p * a.cap];
+    it.src = (sp >= 0 && sp < a.K * a.cap) ? sp : -1;
     it.run = 1;
   }
   return it;
@@ -406,11 +417,11 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   FH_STAMP(3);
 
   // ------------------------------------------------------------------- select
-  const long long per_row = (long long)a.p * a.cap + a.n_special;
-  const long long W = per_row * a.rows;
-  const long long w0 = W * b / G, w1 = W * (b + 1) / G;
-  const int r_lo = (int)(w0 / per_row);
-  const int r_hi = w1 > w0 ? (int)((w1 - 1) / per_row) : r_lo - 1;
+  const int per_row = a.p * a.cap + a.n_special;
+  const int W = per_row * a.rows;
+  const int w0 = (int)((long long)W * b / G), w1 = (int)((long long)W * (b + 1) / G);
+  const int r_lo = w0 / per_row;
+  const int r_hi = w1 > w0 ? (w1 - 1) / per_row : r_lo - 1;
   float *sc_sm = reinterpret_cast<float *>(ring);
   for (int hr = r_lo; hr <= r_hi; ++hr) {
     const uint32_t *h1g = hist_cur + (size_t)hr * kHistWords;
@@ -524,47 +535,69 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
                         : make_uint4(0, 0, 0, 0);
     vec_to_float<HT>(x, h3[r]);
   }
-  const char *wp = reinterpret_cast<const char *>(a.w_perm);
-  // Producer cursor (thread 0) and consumer cursor (all threads) walk the same
-  // chunk sequence; a chunk is at most rpc3 rows contiguous in w_perm.
-  long long w_issue = w0, w_cons = w0;
-  int n_issued = 0;
-  auto issue3 = [&](uint32_t gidx) {
-    const S2Item it = s2_item(a, probes_sm, r_lo, w_issue, w1);
-    const int n = min(it.run, rpc3);
-    const int s = gidx % kFSlots;
-    fence_proxy_async_smem();
-    if (it.src >= 0) {
-      mbar_expect_tx(&S.mbar[s], (uint32_t)(n * row3));
-      bulk_g2s(ring + (size_t)s * kFSlotBytes, wp + (size_t)it.src * row3, (uint32_t)(n * row3),
-               &S.mbar[s]);
-    } else {
-      mbar_expect_tx(&S.mbar[s], 0u);  // invalid special slot: empty chunk
+  // Chunk table of this CTA's stage-2 range (thread 0, 32-bit math).
+  if (tid == 0) {
+    int w = w0, nch = 0;
+    while (w < w1 && nch < kFMaxChunks) {
+      const S2Item it = s2_item(a, probes_sm, r_lo, w, w1);
+      const int n = min(it.run, rpc3);
+      S.chunks[nch].src = it.src;
+      S.chunks[nch].w = w;
+      S.chunks[nch].n = (short)n;
+      S.chunks[nch].hrow = (short)it.hrow;
+      ++nch;
+      w += n;
     }
-    w_issue += n;
-  };
+    S.s_nchunks = (w < w1) ? -1 : nch;  // -1: range needs more chunks than the table holds
+  }
   // Vocab ids of this CTA's stage-2 rows, fetched once (off the per-chunk path).
-  const int n_vid = (int)min((long long)kFVidCache, w1 - w0);
+  const int n_vid = min(kFVidCache, w1 - w0);
   for (int t = tid; t < n_vid; t += kFThreads) {
     const S2Item it = s2_item(a, probes_sm, r_lo, w0 + t, w0 + t + 1);
     vid_sm[t] = it.src >= 0 ? a.vocab_map[it.src] : 0;
   }
-  __syncthreads();  // ring free: selection done by every thread
+  __syncthreads();  // ring free: selection done by every thread; chunk table ready
+  const int nch = S.s_nchunks;
+  const char *wp = reinterpret_cast<const char *>(a.w_perm);
+  auto chunk_at = [&](int c, int &w_walk) -> S2Chunk {
+    if (nch >= 0) return S.chunks[c];
+    const S2Item it = s2_item(a, probes_sm, r_lo, w_walk, w1);  // overflow fallback
+    S2Chunk ch;
+    ch.src = it.src;
+    ch.w = w_walk;
+    ch.n = (short)min(it.run, rpc3);
+    ch.hrow = (short)it.hrow;
+    w_walk += ch.n;
+    return ch;
+  };
+  int w_issue = w0, w_cons = w0, c_issue = 0;
+  auto issue3 = [&](uint32_t gidx) {
+    const S2Chunk ch = chunk_at(c_issue++, w_issue);
+    const int s = gidx % kFSlots;
+    fence_proxy_async_smem();
+    if (ch.src >= 0) {
+      mbar_expect_tx(&S.mbar[s], (uint32_t)(ch.n * row3));
+      bulk_g2s(ring + (size_t)s * kFSlotBytes, wp + (size_t)ch.src * row3,
+               (uint32_t)(ch.n * row3), &S.mbar[s]);
+    } else {
+      mbar_expect_tx(&S.mbar[s], 0u);  // invalid row: empty chunk
+    }
+  };
+  const int n_chunks_total = nch >= 0 ? nch : 0x7FFFFFFF;
+  auto more_to_issue = [&]() { return nch >= 0 ? c_issue < nch : w_issue < w1; };
   if (tid == 0) {
     uint32_t gidx = gi;
-    while (n_issued < kFSlots && w_issue < w1) {
-      issue3(gidx++);
-      ++n_issued;
-    }
+    for (int k = 0; k < kFSlots && more_to_issue(); ++k) issue3(gidx++);
   }
-  while (w_cons < w1) {
-    const S2Item it = s2_item(a, probes_sm, r_lo, w_cons, w1);
-    const int n = min(it.run, rpc3);
+  for (int c = 0; c < n_chunks_total && w_cons < w1; ++c) {
+    int w_dummy = w_cons;
+    const S2Chunk ch = nch >= 0 ? S.chunks[c] : chunk_at(c, w_dummy);
+    const int n = ch.n;
     const int s = gi % kFSlots;
     if (!mbar_wait(&S.mbar[s], (gi / kFSlots) & 1, a.copy_polls) && lane == 0)
       atomicOr(&S.s_err, kErrCopyTimeout);
-    const int hr = it.hrow;
-    if (it.src >= 0 && g3 < RG3) {
+    const int hr = ch.hrow;
+    if (ch.src >= 0 && g3 < RG3) {
       const unsigned char *base = ring + (size_t)s * kFSlotBytes + (size_t)col3 * 16;
       for (int r = g3; r < n; r += RG3) {
         float w[8];
@@ -582,12 +615,11 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       }
     }
     __syncthreads();
-    if (it.src >= 0 && tid < n) {
+    if (ch.src >= 0 && tid < n) {
       float acc = 0.f;
       for (int q = 0; q < Q3; ++q) acc += S.part[s][tid][q][0];
-      const long long src = it.src + tid;
-      const long long wi = w_cons - w0 + tid;
-      const uint32_t vid = (uint32_t)(wi < n_vid ? vid_sm[wi] : a.vocab_map[src]);
+      const int wi = ch.w - w0 + tid;
+      const uint32_t vid = (uint32_t)(wi < n_vid ? vid_sm[wi] : a.vocab_map[ch.src + tid]);
       float key = acc;
       if (a.do_sample)
         key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)hr, vid);
@@ -595,7 +627,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     }
     w_cons += n;
     ++gi;
-    if (tid == 0 && w_issue < w1) issue3(gi + kFSlots - 1);
+    if (tid == 0 && more_to_issue()) issue3(gi + kFSlots - 1);
   }
   __syncthreads();
   FH_STAMP(5);
