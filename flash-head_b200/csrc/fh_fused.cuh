@@ -275,7 +275,7 @@ __device__ __forceinline__ void trace_stamp(int phase) {
   if (threadIdx.x == 0 && g_fh_trace) {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g_fh_trace[blockIdx.x * 8 + phase] = t;
+    g_fh_trace[blockIdx.x * 16 + phase] = t;
   }
 }
 #define FH_STAMP(p) trace_stamp(p)
@@ -443,6 +443,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         }
       }
     }
+    if (hr == r_lo) FH_STAMP(7);
     // Defaults keep every index in range even when the histogram is
     // incomplete (a timed-out barrier); the scan's first barrier publishes them.
     if (tid == 0) {
@@ -479,6 +480,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       __syncthreads();
     }
     need -= S.s_above;
+    if (hr == r_lo) FH_STAMP(8);
     const uint32_t prefix = (uint32_t)(cb * 256 + (S.s_fb & 255));
     const int cnt = S.s_cnt;
     int *probes_out = probes_sm + (hr - r_lo) * a.p;
@@ -500,6 +502,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         if (rank == need - 1) S.s_T = mine;
       }
       __syncthreads();
+      if (hr == r_lo) FH_STAMP(9);
       const unsigned long long T = S.s_T;
       block_ordered_compact(
           a.K, [&](int i) { return pack(sanitize(sc_sm[i]), (uint32_t)i) >= T; },
@@ -512,6 +515,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       fused_select(sc_sm, a.K, a.p, -INFINITY, -INFINITY, probes_out, S);
     }
   }
+  FH_STAMP(10);
   // Zero the histogram buffer the next call will use (this call never reads it).
   {
     const size_t n4 = (size_t)kFMaxRows * kHistWords / 4;
@@ -535,6 +539,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
                         : make_uint4(0, 0, 0, 0);
     vec_to_float<HT>(x, h3[r]);
   }
+  FH_STAMP(11);
   // Chunk table of this CTA's stage-2 range (thread 0, 32-bit math).
   if (tid == 0) {
     int w = w0, nch = 0;
@@ -583,6 +588,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       mbar_expect_tx(&S.mbar[s], 0u);  // invalid row: empty chunk
     }
   };
+  FH_STAMP(12);
   const int n_chunks_total = nch >= 0 ? nch : 0x7FFFFFFF;
   auto more_to_issue = [&]() { return nch >= 0 ? c_issue < nch : w_issue < w1; };
   if (tid == 0) {
