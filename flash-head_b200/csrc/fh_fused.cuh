@@ -1,29 +1,33 @@
 // One-kernel FlashHead decode step for a few hidden rows (R <= 4).
 //
-// A persistent cooperative grid of one 512-thread CTA per SM runs all three
-// stages with a single grid-wide dependency:
+// A persistent cooperative grid of one 512-thread CTA per SM runs the whole
+// step with one grid-wide barrier:
 //
 //  1. stage 1   CTA b streams its contiguous slice of centroid rows
-//               [b*K/G, (b+1)*K/G) through a 4-slot ring of shared-memory
+//               [b*K/G, (b+1)*K/G) through a 6-slot ring of shared-memory
 //               buffers filled by bulk asynchronous copies (TMA engine,
 //               completion on mbarriers) and scores them against the R hidden
-//               rows held in registers; scores go to global memory and
-//               their keys into global histograms (see 3).
-//  2. barrier   one arrive counter, bounded spin (a timeout sets an error
-//               bit and the kernel still runs to completion).
-//  3. select    stage 1 also built global two-level histograms of the
-//               score keys (256 coarse x 256 fine bins = bf16 resolution),
-//               so after the barrier every CTA finds the threshold bin from
-//               two 1 KB reads, ranks the few keys that share its 16-bit
-//               prefix exactly and compacts the selected ids from the
-//               L2-resident scores. Redundant selection costs no second
-//               grid-wide dependency.
-//  4. stage 2   the R * (p * cap + n_special) w_perm rows to score are split
-//               evenly across CTAs in (row, probe, slot) order; each CTA
-//               streams its contiguous runs through the same ring, packs
-//               (logit or Gumbel key, vocab id) words, and reduces them with a
-//               64-bit atomicMax. The last CTA to finish publishes the ids and
-//               resets the shared state words.
+//               rows held in registers. Each score's key goes into global
+//               two-level histograms (256 coarse x 256 fine bins: bf16
+//               resolution).
+//  2. barrier   one arrive counter, bounded spin (a timeout sets an error bit
+//               and the kernel still runs to completion).
+//  3. select    one warp per hidden row finds, from two 1 KB histogram reads,
+//               the bf16 bucket that holds the p-th largest score. Every CTA
+//               pushes the clusters it scored whose key lies above that
+//               bucket onto a global work queue; keys inside the bucket go
+//               to a small tie list that CTA r (for row r) ranks exactly
+//               (largest score, then smallest cluster id) once all CTAs have
+//               contributed, pushing the winners.
+//  4. stage 2   every CTA pops (row, cluster) items from the queue and streams
+//               the cluster's w_perm rows and vocab ids through two 64 KB
+//               slots, scoring them and keeping the best packed
+//               (logit or Gumbel key, vocab id) word per row; words meet in a
+//               64-bit atomicMax and the last CTA to finish publishes the ids.
+//
+// Histograms, queue and tie lists alternate between two buffers by a call
+// epoch; each call zeroes the buffers of the next call and the last CTA
+// resets the counters, so a workspace zero-filled once stays consistent.
 #pragma once
 
 #include "fh_kernels.cuh"
@@ -32,29 +36,47 @@ namespace fh {
 
 constexpr int kFThreads = 512;
 constexpr int kFWarps = kFThreads / 32;
-constexpr int kFSlots = 4;
-constexpr int kFSlotBytes = 24 * 1024;
-constexpr int kFChunkRows = 16;
+constexpr int kS1Slots = 6;
+constexpr int kS1SlotBytes = 24 * 1024;
+constexpr int kS3Slots = 2;
+constexpr int kS3SlotBytes = 64 * 1024;
+constexpr int kFChunkRows = 16;  // max centroid rows per stage-1 chunk
+constexpr int kS3MaxRows = 32;   // max w_perm rows per stage-2 chunk
 constexpr int kFBins = 512;
 constexpr int kFCand = 256;
 constexpr int kFMaxRows = 4;
 constexpr int kFMaxProbes = 4096;
+constexpr int kFMaxSpecial = 256;
+constexpr int kQueueCap = kFMaxRows * (kFMaxProbes + kFMaxSpecial);
+constexpr int kTieCap = 1024;
 
 // State words at the start of the workspace (uint32 index).
 constexpr int kSyncArrive = 1;
 constexpr int kSyncDone = 2;
 constexpr int kSyncError = 3;
 constexpr int kSyncEpoch = 4;
+constexpr int kSyncQTail = 5;
+constexpr int kSyncQHead = 6;
+constexpr int kSyncTieArrive = 7;
+constexpr int kSyncTieCount = 8;  // [8 + r]
 
-// Two-level key histograms per hidden row: 256 coarse bins (key >> 24) then
-// 65536 fine bins (key >> 16, i.e. bf16 resolution). Two buffers alternate
-// by call epoch; each call zeroes the buffer the next call will use.
 constexpr int kHistCoarse = 256;
 constexpr int kHistWords = kHistCoarse + 65536;
-constexpr size_t kHistBytes = 2ull * kFMaxRows * kHistWords * sizeof(uint32_t);
+// Per-epoch buffers (two of each).
+constexpr size_t kHistBufBytes = (size_t)kFMaxRows * kHistWords * sizeof(uint32_t);
+constexpr size_t kQueueBufBytes = (size_t)kQueueCap * sizeof(uint32_t);
+constexpr size_t kTieBufBytes = (size_t)kFMaxRows * kTieCap * sizeof(unsigned long long);
+constexpr size_t kEpochBufBytes = kHistBufBytes + kQueueBufBytes + kTieBufBytes;
+constexpr size_t kHistBytes = 2 * kEpochBufBytes;  // workspace bytes of all epoch buffers
 
 constexpr uint32_t kErrBarrierTimeout = 1u;
 constexpr uint32_t kErrCopyTimeout = 2u;
+constexpr uint32_t kErrQueueTimeout = 4u;
+
+// Queue item: bit 31 valid, bit 30 special token, bits 28-29 hidden row,
+// bits 0-23 cluster id (or special-token index).
+constexpr uint32_t kItemValid = 0x80000000u;
+constexpr uint32_t kItemSpecial = 0x40000000u;
 
 struct FusedArgs {
   const void *hidden;  // [R, D]
@@ -72,46 +94,55 @@ struct FusedArgs {
   int do_sample;
   float temperature;
   RngKey rng;
-  float *scores;       // [R, K] global scratch
+  float *scores;       // [R, K] global scratch (tie fallback)
   uint32_t *sync;      // workspace state words
-  uint32_t *hist;      // [2][kFMaxRows][kHistWords] key histograms
+  unsigned char *epoch_bufs;   // 2 x (histograms, queue, tie lists)
   unsigned long long *packed;  // [R]
   int64_t *out_ids;    // [R]
-  uint32_t barrier_polls;      // grid-barrier poll limit
+  uint32_t barrier_polls;      // grid-barrier / tie-list / queue poll limit
   uint32_t copy_polls;         // mbarrier poll limit
   int extra_arrivals;          // >0 only in the timeout test: wait for more CTAs than exist
 };
 
-// One stage-2 chunk: up to rpc3 w_perm rows contiguous in memory.
-struct S2Chunk {
-  int src;   // first w_perm row, -1 for an invalid special slot
-  int w;     // first work index
-  short n;   // rows
-  short hrow;
+struct S3Desc {
+  int src;   // first w_perm row; -1 invalid (empty chunk); -2 end of work
+  int n;     // rows
+  int row;   // hidden row
+  int vid_in_smem;
 };
-constexpr int kFMaxChunks = 384;
+
+struct RowThreshold {
+  uint32_t prefix;  // 16-bit key prefix of the bucket holding the p-th score
+  int need;         // keys of that bucket to select
+  int cnt;          // keys in that bucket
+};
 
 struct FusedSmem {
-  uint64_t mbar[kFSlots];
-  float part[kFSlots][kFChunkRows][16][kFMaxRows];
+  uint64_t mbar1[kS1Slots];
+  uint64_t mbar3[kS3Slots];
+  float part1[2][kFChunkRows][16][kFMaxRows];
+  float part3[kS3Slots][kS3MaxRows][16];
   float local[kFMaxRows][128];
   float scale[128];
-  uint32_t coarse[kFMaxRows][kHistCoarse];
+  uint32_t coarse[kFMaxRows * kHistCoarse];
+  __align__(16) int vid[kS3Slots][kS3MaxRows];
+  S3Desc desc[kS3Slots];
+  RowThreshold thr[kFMaxRows];
+  unsigned long long best[kFMaxRows];
+  unsigned long long tiek[kTieCap];
+  // generic refinement select (tie-list overflow fallback)
   uint32_t hist[kFBins];
   unsigned long long cand[kFCand];
-  S2Chunk chunks[kFMaxChunks];
-  int s_nchunks;
-  unsigned long long best[2];
   int scan[33];
-  int s_bstar, s_above, s_cnt, s_ncand, s_cb, s_fb;
+  int s_bstar, s_above, s_cnt, s_ncand;
   unsigned long long s_T, s_kmin, s_kmax;
   uint32_t s_err;
 };
 
-constexpr int kFVidCache = 4096;  // vocab ids of a CTA's stage-2 rows, prefetched
-constexpr size_t kFRingBytes = (size_t)kFSlots * kFSlotBytes;
-constexpr size_t kFSmemBytes =
-    kFRingBytes + sizeof(FusedSmem) + 2ull * kFMaxProbes * 4 + (size_t)kFVidCache * 4;
+constexpr size_t kFRingBytes = (size_t)kS1Slots * kS1SlotBytes > (size_t)kS3Slots * kS3SlotBytes
+                                   ? (size_t)kS1Slots * kS1SlotBytes
+                                   : (size_t)kS3Slots * kS3SlotBytes;
+constexpr size_t kFSmemBytes = kFRingBytes + sizeof(FusedSmem);
 
 template <typename T>
 __device__ __forceinline__ void vec_to_float(const uint4 &v, float *f);
@@ -240,33 +271,6 @@ __device__ void fused_select(const float *sc, int K, int p, float vmin, float vm
       S.scan);
 }
 
-// Stage-2 work walk: work index w of row-major (hidden row, probe, slot) items,
-// then the special tokens of each hidden row. Returns the w_perm row of w
-// (-1 if invalid) and how many following work items are contiguous in w_perm.
-struct S2Item {
-  int src;
-  int run;
-  int hrow;
-};
-
-__device__ __forceinline__ S2Item s2_item(const FusedArgs &a, const int *probes_sm, int r_lo,
-                                          int w, int w_end) {
-  const int per_row = a.p * a.cap + a.n_special;
-  S2Item it;
-  it.hrow = w / per_row;
-  const int j = w - it.hrow * per_row;
-  if (j < a.p * a.cap) {
-    const int pi = j / a.cap, sl = j - pi * a.cap;
-    const int cl = probes_sm[(it.hrow - r_lo) * a.p + pi];
-    it.src = (cl >= 0 && cl < a.K) ? cl * a.cap + sl : -1;
-    it.run = min(a.cap - sl, w_end - w);
-  } else {
-    const int sp = a.special_slots[j - a.p * a.cap];
-    it.src = (sp >= 0 && sp < a.K * a.cap) ? sp : -1;
-    it.run = 1;
-  }
-  return it;
-}
 
 #ifdef FH_TRACE
 // Profiling builds only: per-CTA %globaltimer stamps at phase boundaries.
@@ -283,44 +287,99 @@ __device__ __forceinline__ void trace_stamp(int phase) {
 #define FH_STAMP(p) ((void)0)
 #endif
 
+__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Warp-level search of a 256-bin histogram (highest bin first) for the bin
+// holding the need-th largest key: returns the bin, the count above it and
+// the bin's count (all lanes).
+__device__ __forceinline__ void warp_find_bin(const uint32_t *bins, int need, int &bin,
+                                              int &above, int &cnt) {
+  const int lane = threadIdx.x & 31;
+  // lane l owns bins 255-8l .. 248-8l (descending)
+  const uint4 lo = __ldcg(reinterpret_cast<const uint4 *>(bins + 248 - 8 * lane));
+  const uint4 hi = __ldcg(reinterpret_cast<const uint4 *>(bins + 252 - 8 * lane));
+  const uint32_t c[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
+  int mine = 0;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) mine += (int)c[u];
+  int incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const int before = incl - mine;
+  const unsigned m = __ballot_sync(0xFFFFFFFFu, before < need && need <= incl);
+  int b = 255, ab = 0, cn = 0;
+  if (m) {
+    const int src = __ffs(m) - 1;
+    if (lane == src) {
+      int cum = before;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (cum < need && need <= cum + (int)c[u]) {
+          b = 255 - 8 * lane - u;
+          ab = cum;
+          cn = (int)c[u];
+        }
+        cum += (int)c[u];
+      }
+    }
+    b = __shfl_sync(0xFFFFFFFFu, b, src);
+    ab = __shfl_sync(0xFFFFFFFFu, ab, src);
+    cn = __shfl_sync(0xFFFFFFFFu, cn, src);
+  }
+  bin = b;
+  above = ab;
+  cnt = cn;
+}
+
 template <typename HT, typename WT, int R>
 __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char *ring = smem;
   FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem + kFRingBytes);
-  int *probes_sm = reinterpret_cast<int *>(smem + kFRingBytes + sizeof(FusedSmem));
-  int *vid_sm = probes_sm + 2 * kFMaxProbes;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x;
   if (tid == 0) {
-    for (int s = 0; s < kFSlots; ++s) mbar_init(&S.mbar[s], 1);
+    for (int s = 0; s < kS1Slots; ++s) mbar_init(&S.mbar1[s], 1);
+    for (int s = 0; s < kS3Slots; ++s) mbar_init(&S.mbar3[s], 1);
     fence_mbar_init();
     S.s_err = 0u;
-    S.best[0] = S.best[1] = 0ull;
   }
+  if (tid < kFMaxRows) S.best[tid] = 0ull;
+  for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFThreads) S.coarse[i] = 0u;
   __syncthreads();
   FH_STAMP(0);
+
+  const uint32_t epoch = __ldcg(&a.sync[kSyncEpoch]);
+  unsigned char *buf_cur = a.epoch_bufs + (size_t)(epoch & 1u) * kEpochBufBytes;
+  unsigned char *buf_nxt = a.epoch_bufs + (size_t)((epoch + 1u) & 1u) * kEpochBufBytes;
+  uint32_t *hist_cur = reinterpret_cast<uint32_t *>(buf_cur);
+  uint32_t *queue = reinterpret_cast<uint32_t *>(buf_cur + kHistBufBytes);
+  unsigned long long *ties =
+      reinterpret_cast<unsigned long long *>(buf_cur + kHistBufBytes + kQueueBufBytes);
 
   // ------------------------------------------------------------------ stage 1
   const int c0 = (int)((long long)b * a.K / G), c1 = (int)((long long)(b + 1) * a.K / G);
   const int nc = c1 - c0;
   const int row1 = a.D * (int)sizeof(WT);
-  const int rpc1 = max(1, min(kFChunkRows, kFSlotBytes / row1));
+  const int rpc1 = max(1, min(kFChunkRows, kS1SlotBytes / row1));
   const int n1 = (nc + rpc1 - 1) / rpc1;
   const char *wsrc = reinterpret_cast<const char *>(a.cw) + (size_t)c0 * row1;
-  uint32_t gi = 0;  // running chunk counter over both stages (slot = gi % kFSlots)
-
   auto issue1 = [&](int i) {
-    const int s = i % kFSlots;
+    const int s = i % kS1Slots;
     const int rows = min(rpc1, nc - i * rpc1);
     const uint32_t bytes = (uint32_t)(rows * row1);
     fence_proxy_async_smem();
-    mbar_expect_tx(&S.mbar[s], bytes);
-    bulk_g2s(ring + (size_t)s * kFSlotBytes, wsrc + (size_t)i * rpc1 * row1, bytes, &S.mbar[s]);
+    mbar_expect_tx(&S.mbar1[s], bytes);
+    bulk_g2s(ring + (size_t)s * kS1SlotBytes, wsrc + (size_t)i * rpc1 * row1, bytes, &S.mbar1[s]);
   };
   if (tid == 0)
-    for (int i = 0; i < min(kFSlots, n1); ++i) issue1(i);
+    for (int i = 0; i < min(kS1Slots, n1); ++i) issue1(i);
   if (tid < nc) S.scale[tid] = a.cscale ? a.cscale[c0 + tid] : 1.f;
 
   constexpr int VE1 = Vec<WT>::kElems;
@@ -329,7 +388,6 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   float h1[R][VE1];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    // VE1 elements of hidden row r at column col1 (VE1 * 2 bytes)
     const char *hp = reinterpret_cast<const char *>(a.hidden) + (size_t)r * a.D * sizeof(HT) +
                      (size_t)col1 * VE1 * sizeof(HT);
 #pragma unroll
@@ -339,13 +397,13 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     }
   }
 
-  for (int i = 0; i < n1; ++i, ++gi) {
-    const int s = gi % kFSlots;
+  for (int i = 0; i < n1; ++i) {
+    const int s = i % kS1Slots;
     const int rows = min(rpc1, nc - i * rpc1);
-    if (!mbar_wait(&S.mbar[s], (gi / kFSlots) & 1, a.copy_polls) && lane == 0)
+    if (!mbar_wait(&S.mbar1[s], (i / kS1Slots) & 1, a.copy_polls) && lane == 0)
       atomicOr(&S.s_err, kErrCopyTimeout);
     if (g1 < RG1) {
-      const unsigned char *base = ring + (size_t)s * kFSlotBytes + (size_t)col1 * 16;
+      const unsigned char *base = ring + (size_t)s * kS1SlotBytes + (size_t)col1 * 16;
       for (int r = g1; r < rows; r += RG1) {
         float w[VE1];
         vec_to_float<WT>(lds128(base + (size_t)r * row1), w);
@@ -355,51 +413,38 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
 #pragma unroll
           for (int e = 0; e < VE1; ++e) acc = fmaf(w[e], h1[hr][e], acc);
           acc = warp_sum(acc);
-          if (lane == 0) S.part[s][r][q1][hr] = acc;
+          if (lane == 0) S.part1[i & 1][r][q1][hr] = acc;
         }
       }
     }
     __syncthreads();
     if (tid < rows * R) {
       const int r = tid / R, hr = tid - (tid / R) * R;
-      float acc = 0.f;
-      for (int q = 0; q < Q1; ++q) acc += S.part[s][r][q][hr];
-      const int k = c0 + i * rpc1 + r;
-      float sc = acc * S.scale[k - c0];
-      if (a.do_sample)
-        sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)hr, (uint32_t)k);
       if (hr < a.rows) {
+        float acc = 0.f;
+        for (int q = 0; q < Q1; ++q) acc += S.part1[i & 1][r][q][hr];
+        const int k = c0 + i * rpc1 + r;
+        float sc = acc * S.scale[k - c0];
+        if (a.do_sample)
+          sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)hr, (uint32_t)k);
         S.local[hr][k - c0] = sc;
         a.scores[(size_t)hr * a.K + k] = sc;
+        const uint32_t key = mono(sanitize(sc));
+        atomicAdd(&hist_cur[(size_t)hr * kHistWords + kHistCoarse + (key >> 16)], 1u);
+        atomicAdd(&S.coarse[hr * kHistCoarse + (key >> 24)], 1u);
       }
     }
-    if (tid == 0 && i + kFSlots < n1) issue1(i + kFSlots);
-  }
-  __syncthreads();
-  FH_STAMP(1);
-  // Publish this CTA's keys to the global two-level histograms of its rows:
-  // fine bins directly, coarse bins aggregated in shared memory first (they
-  // are few and hot).
-  const uint32_t epoch = __ldcg(&a.sync[kSyncEpoch]);
-  uint32_t *hist_cur = a.hist + (size_t)(epoch & 1u) * kFMaxRows * kHistWords;
-  uint32_t *hist_next = a.hist + (size_t)((epoch + 1u) & 1u) * kFMaxRows * kHistWords;
-  for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFThreads) (&S.coarse[0][0])[i] = 0u;
-  __syncthreads();
-  for (int i = tid; i < a.rows * nc; i += kFThreads) {
-    const int hr = i / nc, k = i - (i / nc) * nc;
-    const uint32_t key = mono(sanitize(S.local[hr][k]));
-    atomicAdd(&hist_cur[(size_t)hr * kHistWords + kHistCoarse + (key >> 16)], 1u);
-    atomicAdd(&S.coarse[hr][key >> 24], 1u);
+    if (tid == 0 && i + kS1Slots < n1) issue1(i + kS1Slots);
   }
   __syncthreads();
   for (int i = tid; i < a.rows * kHistCoarse; i += kFThreads) {
-    const uint32_t c = (&S.coarse[0][0])[i];
+    const uint32_t c = S.coarse[i];
     if (c) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], c);
   }
+  __syncthreads();
+  FH_STAMP(1);
 
   // ------------------------------------------------------------- grid barrier
-  __syncthreads();
-  FH_STAMP(2);
   if (tid == 0) {
     __threadfence();
     atomicAdd(&a.sync[kSyncArrive], 1u);
@@ -414,120 +459,132 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     __threadfence();
   }
   __syncthreads();
-  FH_STAMP(3);
+  FH_STAMP(2);
 
-  // ------------------------------------------------------------------- select
-  const int per_row = a.p * a.cap + a.n_special;
-  const int W = per_row * a.rows;
-  const int w0 = (int)((long long)W * b / G), w1 = (int)((long long)W * (b + 1) / G);
-  const int r_lo = w0 / per_row;
-  const int r_hi = w1 > w0 ? (w1 - 1) / per_row : r_lo - 1;
-  float *sc_sm = reinterpret_cast<float *>(ring);
-  for (int hr = r_lo; hr <= r_hi; ++hr) {
-    const uint32_t *h1g = hist_cur + (size_t)hr * kHistWords;
-    // All loads of this row's scores (and its coarse histogram) in flight at once.
-    const uint32_t coarse_v = tid < kHistCoarse ? __ldcg(&h1g[kHistCoarse - 1 - tid]) : 0u;
-    {
-      const float *src = a.scores + (size_t)hr * a.K;
-      for (int base = 0; base < a.K; base += kFThreads * 8) {
-        float v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = base + u * kFThreads + tid;
-          v[u] = i < a.K ? __ldcg(&src[i]) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = base + u * kFThreads + tid;
-          if (i < a.K) sc_sm[i] = v[u];
-        }
-      }
-    }
-    if (hr == r_lo) FH_STAMP(7);
-    // Defaults keep every index in range even when the histogram is
-    // incomplete (a timed-out barrier); the scan's first barrier publishes them.
-    if (tid == 0) {
-      S.s_cb = 0;
-      S.s_fb = 0;
-      S.s_cnt = 0;
-      S.s_above = 0;
-      S.s_T = ~0ull;
-    }
-    // coarse level: thread t owns bin 255 - t (highest first)
-    int need = a.p;
-    {
-      const int c = (int)coarse_v;
-      int total;
-      const int before = block_exclusive_scan(c, S.scan, &total);
-      if (before < need && need <= before + c) {
-        S.s_cb = kHistCoarse - 1 - tid;
-        S.s_above = before;
-      }
-      __syncthreads();
-    }
-    need -= S.s_above;
-    const int cb = min(max(S.s_cb, 0), kHistCoarse - 1);
-    {
-      const int f = tid < 256 ? (int)__ldcg(&h1g[kHistCoarse + cb * 256 + 255 - tid]) : 0;
-      int total;
-      const int before = block_exclusive_scan(f, S.scan, &total);
-      if (before < need && need <= before + f) {
-        S.s_fb = 255 - tid;
-        S.s_above = before;
-        S.s_cnt = f;
-      }
-      if (tid == 0) S.s_ncand = 0;
-      __syncthreads();
-    }
-    need -= S.s_above;
-    if (hr == r_lo) FH_STAMP(8);
-    const uint32_t prefix = (uint32_t)(cb * 256 + (S.s_fb & 255));
-    const int cnt = S.s_cnt;
-    int *probes_out = probes_sm + (hr - r_lo) * a.p;
-    if (cnt <= kFCand) {
-      // exact ranking of the keys that share the threshold's 16-bit prefix
-      for (int i = tid; i < a.K; i += kFThreads) {
-        const float v = sanitize(sc_sm[i]);
-        if ((mono(v) >> 16) == prefix) {
-          const int pos = atomicAdd(&S.s_ncand, 1);
-          if (pos < kFCand) S.cand[pos] = pack(v, (uint32_t)i);
-        }
-      }
-      __syncthreads();
-      const int nc2 = min(cnt, kFCand);
-      if (tid < nc2) {
-        const unsigned long long mine = S.cand[tid];
-        int rank = 0;
-        for (int j = 0; j < nc2; ++j) rank += S.cand[j] > mine;
-        if (rank == need - 1) S.s_T = mine;
-      }
-      __syncthreads();
-      if (hr == r_lo) FH_STAMP(9);
-      const unsigned long long T = S.s_T;
-      block_ordered_compact(
-          a.K, [&](int i) { return pack(sanitize(sc_sm[i]), (uint32_t)i) >= T; },
-          [&](int pos, int i) {
-            if (pos < a.p) probes_out[pos] = i;
-          },
-          S.scan);
-    } else {
-      // many keys share the threshold's bf16 prefix: full refinement
-      fused_select(sc_sm, a.K, a.p, -INFINITY, -INFINITY, probes_out, S);
+  // --------------------------------------------- thresholds: warp r, row r
+  if (warp < a.rows) {
+    const uint32_t *h = hist_cur + (size_t)warp * kHistWords;
+    int cb, above1, cnt1, fb, above2, cnt2;
+    warp_find_bin(h, a.p, cb, above1, cnt1);
+    warp_find_bin(h + kHistCoarse + cb * 256, a.p - above1, fb, above2, cnt2);
+    if (lane == 0) {
+      S.thr[warp].prefix = (uint32_t)(cb * 256 + fb);
+      S.thr[warp].need = a.p - above1 - above2;
+      S.thr[warp].cnt = cnt2;
     }
   }
-  FH_STAMP(10);
-  // Zero the histogram buffer the next call will use (this call never reads it).
+  __syncthreads();
+
+  // ------------------- push own clusters above the bucket; bucket -> tie list
+  for (int base = 0; base < a.rows * nc; base += kFThreads) {
+    const int i = base + tid;
+    bool push = false;
+    uint32_t item = 0;
+    if (i < a.rows * nc) {
+      const int hr = i / nc, k = i - (i / nc) * nc;
+      const float v = sanitize(S.local[hr][k]);
+      const uint32_t pre = mono(v) >> 16;
+      const uint32_t P = S.thr[hr].prefix;
+      if (pre > P) {
+        push = true;
+        item = kItemValid | ((uint32_t)hr << 28) | (uint32_t)(c0 + k);
+      } else if (pre == P) {
+        const uint32_t t = atomicAdd(&a.sync[kSyncTieCount + hr], 1u);
+        if (t < (uint32_t)kTieCap) ties[(size_t)hr * kTieCap + t] = pack(v, (uint32_t)(c0 + k));
+      }
+    }
+    const unsigned m = __ballot_sync(0xFFFFFFFFu, push);
+    if (m) {
+      const int leader = __ffs(m) - 1;
+      uint32_t slot = 0;
+      if (lane == leader) slot = atomicAdd(&a.sync[kSyncQTail], (uint32_t)__popc(m));
+      slot = __shfl_sync(0xFFFFFFFFu, slot, leader) + __popc(m & ((1u << lane) - 1u));
+      if (push && slot < (uint32_t)kQueueCap) st_release_gpu(&queue[slot], item);
+    }
+  }
+  // special tokens of row b are pushed by CTA b
+  if (b < a.rows) {
+    for (int base = 0; base < a.n_special; base += kFThreads) {
+      const int t = base + tid;
+      const bool push = t < a.n_special;
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, push);
+      if (m) {
+        const int leader = __ffs(m) - 1;
+        uint32_t slot = 0;
+        if (lane == leader) slot = atomicAdd(&a.sync[kSyncQTail], (uint32_t)__popc(m));
+        slot = __shfl_sync(0xFFFFFFFFu, slot, leader) + __popc(m & ((1u << lane) - 1u));
+        if (push && slot < (uint32_t)kQueueCap)
+          st_release_gpu(&queue[slot], kItemValid | kItemSpecial | ((uint32_t)b << 28) | (uint32_t)t);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    atomicAdd(&a.sync[kSyncTieArrive], 1u);
+  }
+  // Zero this CTA's share of the buffers the next call will use.
   {
-    const size_t n4 = (size_t)kFMaxRows * kHistWords / 4;
-    uint4 *z = reinterpret_cast<uint4 *>(hist_next);
+    const size_t n4 = kEpochBufBytes / 16;
+    uint4 *z = reinterpret_cast<uint4 *>(buf_nxt);
     for (size_t i = (size_t)b * n4 / G + tid; i < (size_t)(b + 1) * n4 / G; i += kFThreads)
       z[i] = make_uint4(0, 0, 0, 0);
   }
+  FH_STAMP(3);
 
+  // ------------------------------------- tie resolution: CTA r for row r
+  if (b < a.rows) {
+    const int hr = b;
+    if (tid == 0) {
+      uint32_t polls = 0;
+      while (ld_acquire_gpu(&a.sync[kSyncTieArrive]) < (uint32_t)G) {
+        if (++polls >= a.barrier_polls) {
+          atomicOr(&S.s_err, kErrQueueTimeout);
+          break;
+        }
+      }
+      __threadfence();
+    }
+    __syncthreads();
+    const int need = S.thr[hr].need;
+    const int cnt = (int)min(__ldcg(&a.sync[kSyncTieCount + hr]), (uint32_t)S.thr[hr].cnt);
+    const uint32_t P = S.thr[hr].prefix;
+    if (cnt <= kTieCap) {
+      for (int t = tid; t < cnt; t += kFThreads) S.tiek[t] = __ldcg(&ties[(size_t)hr * kTieCap + t]);
+      __syncthreads();
+      for (int t = tid; t < cnt; t += kFThreads) {
+        const unsigned long long mine = S.tiek[t];
+        int rank = 0;
+        for (int j = 0; j < cnt; ++j) rank += S.tiek[j] > mine;
+        if (rank < need) {
+          const uint32_t slot = atomicAdd(&a.sync[kSyncQTail], 1u);
+          if (slot < (uint32_t)kQueueCap)
+            st_release_gpu(&queue[slot], kItemValid | ((uint32_t)hr << 28) | packed_id(mine));
+        }
+      }
+    } else {
+      // Too many keys share the bucket: exact select over the whole row.
+      float *sc = reinterpret_cast<float *>(ring);
+      int *sel = reinterpret_cast<int *>(ring + (size_t)a.K * sizeof(float));
+      for (int i = tid; i < a.K; i += kFThreads) sc[i] = __ldcg(&a.scores[(size_t)hr * a.K + i]);
+      __syncthreads();
+      fused_select(sc, a.K, a.p, -INFINITY, -INFINITY, sel, S);
+      for (int t = tid; t < a.p; t += kFThreads) {
+        const int k = sel[t];
+        if (k >= 0 && k < a.K && (mono(sanitize(sc[k])) >> 16) == P) {
+          const uint32_t slot = atomicAdd(&a.sync[kSyncQTail], 1u);
+          if (slot < (uint32_t)kQueueCap)
+            st_release_gpu(&queue[slot], kItemValid | ((uint32_t)hr << 28) | (uint32_t)k);
+        }
+      }
+    }
+    __syncthreads();
+  }
   FH_STAMP(4);
+
   // ------------------------------------------------------------------ stage 2
   const int row3 = a.D * (int)sizeof(HT);
-  const int rpc3 = max(1, min(kFChunkRows, kFSlotBytes / row3));
+  const int rpc3 = max(1, min(min(a.cap, kS3MaxRows), kS3SlotBytes / row3));
   const int NV3 = row3 / 16, Q3 = NV3 / 32, RG3 = kFWarps / Q3;
   const int g3 = warp / Q3, q3 = warp % Q3, col3 = q3 * 32 + lane;
   float h3[R][8];
@@ -539,107 +596,107 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
                         : make_uint4(0, 0, 0, 0);
     vec_to_float<HT>(x, h3[r]);
   }
-  FH_STAMP(11);
-  // Chunk table of this CTA's stage-2 range (thread 0, 32-bit math).
-  if (tid == 0) {
-    int w = w0, nch = 0;
-    while (w < w1 && nch < kFMaxChunks) {
-      const S2Item it = s2_item(a, probes_sm, r_lo, w, w1);
-      const int n = min(it.run, rpc3);
-      S.chunks[nch].src = it.src;
-      S.chunks[nch].w = w;
-      S.chunks[nch].n = (short)n;
-      S.chunks[nch].hrow = (short)it.hrow;
-      ++nch;
-      w += n;
-    }
-    S.s_nchunks = (w < w1) ? -1 : nch;  // -1: range needs more chunks than the table holds
-  }
-  // Vocab ids of this CTA's stage-2 rows, fetched once (off the per-chunk path).
-  const int n_vid = min(kFVidCache, w1 - w0);
-  for (int t = tid; t < n_vid; t += kFThreads) {
-    const S2Item it = s2_item(a, probes_sm, r_lo, w0 + t, w0 + t + 1);
-    vid_sm[t] = it.src >= 0 ? a.vocab_map[it.src] : 0;
-  }
-  __syncthreads();  // ring free: selection done by every thread; chunk table ready
-  const int nch = S.s_nchunks;
+  const uint32_t total = (uint32_t)(a.rows * (a.p + a.n_special));
   const char *wp = reinterpret_cast<const char *>(a.w_perm);
-  auto chunk_at = [&](int c, int &w_walk) -> S2Chunk {
-    if (nch >= 0) return S.chunks[c];
-    const S2Item it = s2_item(a, probes_sm, r_lo, w_walk, w1);  // overflow fallback
-    S2Chunk ch;
-    ch.src = it.src;
-    ch.w = w_walk;
-    ch.n = (short)min(it.run, rpc3);
-    ch.hrow = (short)it.hrow;
-    w_walk += ch.n;
-    return ch;
-  };
-  int w_issue = w0, w_cons = w0, c_issue = 0;
-  auto issue3 = [&](uint32_t gidx) {
-    const S2Chunk ch = chunk_at(c_issue++, w_issue);
-    const int s = gidx % kFSlots;
+  // Producer state (thread 0 only): current item and its next chunk.
+  uint32_t cur_item = 0;
+  int cur_chunk = 0, cur_chunks = 0;
+  auto produce = [&](int s) {
+    S3Desc d;
+    d.src = -2;
+    d.n = 0;
+    d.row = 0;
+    d.vid_in_smem = 0;
+    if (cur_chunk >= cur_chunks) {
+      const uint32_t idx = atomicAdd(&a.sync[kSyncQHead], 1u);
+      cur_chunks = 0;
+      cur_chunk = 0;
+      if (idx < total && idx < (uint32_t)kQueueCap) {
+        uint32_t v = 0, polls = 0;
+        while (!((v = ld_acquire_gpu(&queue[idx])) & kItemValid)) {
+          if (++polls >= a.barrier_polls) {
+            atomicOr(&S.s_err, kErrQueueTimeout);
+            break;
+          }
+        }
+        if (v & kItemValid) {
+          cur_item = v;
+          cur_chunks = (v & kItemSpecial) ? 1 : (a.cap + rpc3 - 1) / rpc3;
+        }
+      }
+    }
+    if (cur_chunk < cur_chunks) {
+      d.row = (int)((cur_item >> 28) & 3u);
+      const int payload = (int)(cur_item & 0x00FFFFFFu);
+      if (cur_item & kItemSpecial) {
+        const int sp = payload < a.n_special ? a.special_slots[payload] : -1;
+        d.src = (sp >= 0 && sp < a.K * a.cap) ? sp : -1;
+        d.n = 1;
+      } else {
+        const int start = cur_chunk * rpc3;
+        d.src = payload < a.K ? payload * a.cap + start : -1;
+        d.n = min(rpc3, a.cap - start);
+      }
+      ++cur_chunk;
+    }
+    S.desc[s] = d;
     fence_proxy_async_smem();
-    if (ch.src >= 0) {
-      mbar_expect_tx(&S.mbar[s], (uint32_t)(ch.n * row3));
-      bulk_g2s(ring + (size_t)s * kFSlotBytes, wp + (size_t)ch.src * row3,
-               (uint32_t)(ch.n * row3), &S.mbar[s]);
+    if (d.src >= 0) {
+      const int *vsrc = a.vocab_map + d.src;
+      const bool vid_bulk = ((reinterpret_cast<uintptr_t>(vsrc) & 15u) == 0) && (d.n % 4 == 0);
+      S.desc[s].vid_in_smem = vid_bulk ? 1 : 0;
+      mbar_expect_tx(&S.mbar3[s], (uint32_t)(d.n * row3) + (vid_bulk ? (uint32_t)(d.n * 4) : 0u));
+      bulk_g2s(ring + (size_t)s * kS3SlotBytes, wp + (size_t)d.src * row3, (uint32_t)(d.n * row3),
+               &S.mbar3[s]);
+      if (vid_bulk) bulk_g2s(&S.vid[s][0], vsrc, (uint32_t)(d.n * 4), &S.mbar3[s]);
     } else {
-      mbar_expect_tx(&S.mbar[s], 0u);  // invalid row: empty chunk
+      mbar_expect_tx(&S.mbar3[s], 0u);  // invalid row or end of work: no data
     }
   };
-  FH_STAMP(12);
-  const int n_chunks_total = nch >= 0 ? nch : 0x7FFFFFFF;
-  auto more_to_issue = [&]() { return nch >= 0 ? c_issue < nch : w_issue < w1; };
-  if (tid == 0) {
-    uint32_t gidx = gi;
-    for (int k = 0; k < kFSlots && more_to_issue(); ++k) issue3(gidx++);
-  }
-  for (int c = 0; c < n_chunks_total && w_cons < w1; ++c) {
-    int w_dummy = w_cons;
-    const S2Chunk ch = nch >= 0 ? S.chunks[c] : chunk_at(c, w_dummy);
-    const int n = ch.n;
-    const int s = gi % kFSlots;
-    if (!mbar_wait(&S.mbar[s], (gi / kFSlots) & 1, a.copy_polls) && lane == 0)
+  __syncthreads();  // ring free for stage 2 (tie fallback used it)
+  if (tid == 0)
+    for (int s = 0; s < kS3Slots; ++s) produce(s);
+  for (int c = 0;; ++c) {
+    const int s = c % kS3Slots;
+    if (!mbar_wait(&S.mbar3[s], (c / kS3Slots) & 1, a.copy_polls) && lane == 0)
       atomicOr(&S.s_err, kErrCopyTimeout);
-    const int hr = ch.hrow;
-    if (ch.src >= 0 && g3 < RG3) {
-      const unsigned char *base = ring + (size_t)s * kFSlotBytes + (size_t)col3 * 16;
-      for (int r = g3; r < n; r += RG3) {
+    const S3Desc d = S.desc[s];
+    if (d.src == -2) break;
+    if (d.src >= 0 && g3 < RG3) {
+      const unsigned char *base = ring + (size_t)s * kS3SlotBytes + (size_t)col3 * 16;
+      for (int r = g3; r < d.n; r += RG3) {
         float w[8];
         vec_to_float<HT>(lds128(base + (size_t)r * row3), w);
         float acc = 0.f;
 #pragma unroll
         for (int hh = 0; hh < R; ++hh) {
-          if (hh == hr) {
+          if (hh == d.row) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc = fmaf(w[e], h3[hh][e], acc);
           }
         }
         acc = warp_sum(acc);
-        if (lane == 0) S.part[s][r][q3][0] = acc;
+        if (lane == 0) S.part3[s][r][q3] = acc;
       }
     }
     __syncthreads();
-    if (ch.src >= 0 && tid < n) {
+    if (d.src >= 0 && tid < d.n) {
       float acc = 0.f;
-      for (int q = 0; q < Q3; ++q) acc += S.part[s][tid][q][0];
-      const int wi = ch.w - w0 + tid;
-      const uint32_t vid = (uint32_t)(wi < n_vid ? vid_sm[wi] : a.vocab_map[ch.src + tid]);
+      for (int q = 0; q < Q3; ++q) acc += S.part3[s][tid][q];
+      const uint32_t vid = (uint32_t)(d.vid_in_smem ? S.vid[s][tid] : a.vocab_map[d.src + tid]);
       float key = acc;
       if (a.do_sample)
-        key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)hr, vid);
-      atomicMax(&S.best[hr - r_lo], pack(key, vid));
+        key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)d.row, vid);
+      atomicMax(&S.best[d.row], pack(key, vid));
     }
-    w_cons += n;
-    ++gi;
-    if (tid == 0 && more_to_issue()) issue3(gi + kFSlots - 1);
+    __syncthreads();  // slot s and its descriptor are free
+    if (tid == 0) produce(s);
   }
   __syncthreads();
   FH_STAMP(5);
 
   // --------------------------------------------------------------- reduction
-  if (tid <= r_hi - r_lo && S.best[tid] != 0ull) atomicMax(&a.packed[r_lo + tid], S.best[tid]);
+  if (tid < a.rows && S.best[tid] != 0ull) atomicMax(&a.packed[tid], S.best[tid]);
   if (tid == 0 && S.s_err) atomicOr(&a.sync[kSyncError], S.s_err);
   __syncthreads();
   __shared__ uint32_t s_last;
@@ -655,9 +712,13 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       const unsigned long long wv = atomicExch(&a.packed[tid], 0ull);
       a.out_ids[tid] = wv ? (int64_t)packed_id(wv) : (int64_t)0xFFFFFFFFll;
     }
+    if (tid < kFMaxRows) a.sync[kSyncTieCount + tid] = 0u;
     if (tid == 0) {
       a.sync[kSyncArrive] = 0u;
       a.sync[kSyncDone] = 0u;
+      a.sync[kSyncQTail] = 0u;
+      a.sync[kSyncQHead] = 0u;
+      a.sync[kSyncTieArrive] = 0u;
       a.sync[kSyncEpoch] = epoch + 1u;
     }
   }

@@ -164,7 +164,7 @@ struct Workspace {
   int32_t *probes;              // [rows, p]
   unsigned long long *packed;   // [rows]
   unsigned *counter;            // [1]
-  uint32_t *hist;               // one-kernel key histograms
+  unsigned char *epoch_bufs;    // one-kernel histograms, queue, tie lists
   size_t bytes;                 // bytes needed for `rows`
 };
 
@@ -186,7 +186,7 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   const size_t scores = round_up((size_t)rows * w.score_stride * sizeof(float), 256);
   w.bytes = state + probes + scores + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
-  w.hist = reinterpret_cast<uint32_t *>(p + 256);
+  w.epoch_bufs = reinterpret_cast<unsigned char *>(p + 256);
   w.packed = reinterpret_cast<unsigned long long *>(p + 256 + fh::kHistBytes);
   const size_t top = (ws_bytes / 256) * 256;
   const size_t probes_off = top >= probes ? top - probes : 0;
@@ -353,7 +353,8 @@ bool fused_ok(const fh_head_desc &d, int rows, bool sample, int grid) {
   const int nv3 = d.hidden * 2 / 16;
   if (nv1 % 32 || nv1 > 512 || nv3 % 32 || nv3 > 512) return false;
   if (d.n_clusters > 128 * grid || d.n_clusters > fh::kSelMaxItems) return false;
-  if (d.n_probes > fh::kFMaxProbes || d.cluster_size > fh::kFChunkRows) return false;
+  if (d.n_probes > fh::kFMaxProbes || d.cluster_size > fh::kS3MaxRows) return false;
+  if (d.n_special > fh::kFMaxSpecial || d.n_clusters >= (1 << 24)) return false;
   return true;
 }
 
@@ -380,7 +381,7 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
   a.rng = rng_key(seed, offset);
   a.scores = w.scores;
   a.sync = reinterpret_cast<uint32_t *>(w.counter);
-  a.hist = w.hist;
+  a.epoch_bufs = w.epoch_bufs;
   a.packed = w.packed;
   a.out_ids = out_ids;
   const bool test_timeout = (d.flags & FH_FLAG_TEST_TIMEOUT) != 0;
