@@ -13,21 +13,22 @@
 //  2. barrier   one arrive counter, bounded spin (a timeout sets an error bit
 //               and the kernel still runs to completion).
 //  3. select    one warp per hidden row finds, from two 1 KB histogram reads,
-//               the bf16 bucket that holds the p-th largest score. Every CTA
-//               pushes the clusters it scored whose key lies above that
-//               bucket onto a global work queue; keys inside the bucket go
-//               to a small tie list that CTA r (for row r) ranks exactly
-//               (largest score, then smallest cluster id) once all CTAs have
-//               contributed, pushing the winners.
-//  4. stage 2   every CTA pops (row, cluster) items from the queue and streams
-//               the cluster's w_perm rows and vocab ids through two 64 KB
-//               slots, scoring them and keeping the best packed
-//               (logit or Gumbel key, vocab id) word per row; words meet in a
-//               64-bit atomicMax and the last CTA to finish publishes the ids.
+//               the bf16 bucket that holds the p-th largest score. Each CTA
+//               keeps the clusters it scored whose key lies above that bucket;
+//               keys inside the bucket (a handful) are published to a small
+//               tie list, and only the CTAs owning such keys wait for the
+//               bucket's count (known from the histogram) to be reached, then
+//               rank their keys exactly (largest score, then smallest id).
+//  4. stage 2   every CTA streams the w_perm rows and vocab ids of its own
+//               selected clusters (and, for CTA r, row r's special tokens)
+//               through four 32 KB slots, scoring them and keeping the best
+//               packed (logit or Gumbel key, vocab id) word per row; words
+//               meet in a 64-bit atomicMax and the last CTA to finish
+//               publishes the ids.
 //
-// Histograms, queue and tie lists alternate between two buffers by a call
-// epoch; each call zeroes the buffers of the next call and the last CTA
-// resets the counters, so a workspace zero-filled once stays consistent.
+// Histograms and tie lists alternate between two buffers by a call epoch;
+// each call zeroes the buffers of the next call and the last CTA resets the
+// counters, so a workspace zero-filled once stays consistent.
 #pragma once
 
 #include "fh_kernels.cuh"
@@ -38,8 +39,8 @@ constexpr int kFThreads = 512;
 constexpr int kFWarps = kFThreads / 32;
 constexpr int kS1Slots = 6;
 constexpr int kS1SlotBytes = 24 * 1024;
-constexpr int kS3Slots = 2;
-constexpr int kS3SlotBytes = 64 * 1024;
+constexpr int kS3Slots = 4;
+constexpr int kS3SlotBytes = 32 * 1024;
 constexpr int kFChunkRows = 16;  // max centroid rows per stage-1 chunk
 constexpr int kS3MaxRows = 32;   // max w_perm rows per stage-2 chunk
 constexpr int kFBins = 512;
@@ -47,35 +48,30 @@ constexpr int kFCand = 256;
 constexpr int kFMaxRows = 4;
 constexpr int kFMaxProbes = 4096;
 constexpr int kFMaxSpecial = 256;
-constexpr int kQueueCap = kFMaxRows * (kFMaxProbes + kFMaxSpecial);
 constexpr int kTieCap = 1024;
+constexpr int kWorkCap = 1024;  // stage-2 items of one CTA (own clusters + specials)
 
 // State words at the start of the workspace (uint32 index).
 constexpr int kSyncArrive = 1;
 constexpr int kSyncDone = 2;
 constexpr int kSyncError = 3;
 constexpr int kSyncEpoch = 4;
-constexpr int kSyncQTail = 5;
-constexpr int kSyncQHead = 6;
-constexpr int kSyncTieArrive = 7;
 constexpr int kSyncTieCount = 8;  // [8 + r]
 
 constexpr int kHistCoarse = 256;
 constexpr int kHistWords = kHistCoarse + 65536;
 // Per-epoch buffers (two of each).
 constexpr size_t kHistBufBytes = (size_t)kFMaxRows * kHistWords * sizeof(uint32_t);
-constexpr size_t kQueueBufBytes = (size_t)kQueueCap * sizeof(uint32_t);
 constexpr size_t kTieBufBytes = (size_t)kFMaxRows * kTieCap * sizeof(unsigned long long);
-constexpr size_t kEpochBufBytes = kHistBufBytes + kQueueBufBytes + kTieBufBytes;
+constexpr size_t kEpochBufBytes = kHistBufBytes + kTieBufBytes;
 constexpr size_t kHistBytes = 2 * kEpochBufBytes;  // workspace bytes of all epoch buffers
 
 constexpr uint32_t kErrBarrierTimeout = 1u;
 constexpr uint32_t kErrCopyTimeout = 2u;
-constexpr uint32_t kErrQueueTimeout = 4u;
+constexpr uint32_t kErrTieTimeout = 4u;
 
-// Queue item: bit 31 valid, bit 30 special token, bits 28-29 hidden row,
-// bits 0-23 cluster id (or special-token index).
-constexpr uint32_t kItemValid = 0x80000000u;
+// Stage-2 work item: bit 30 special token, bits 28-29 hidden row, bits 0-23
+// cluster id (or special-token index).
 constexpr uint32_t kItemSpecial = 0x40000000u;
 
 struct FusedArgs {
@@ -96,10 +92,10 @@ struct FusedArgs {
   RngKey rng;
   float *scores;       // [R, K] global scratch (tie fallback)
   uint32_t *sync;      // workspace state words
-  unsigned char *epoch_bufs;   // 2 x (histograms, queue, tie lists)
+  unsigned char *epoch_bufs;   // 2 x (histograms, tie lists)
   unsigned long long *packed;  // [R]
   int64_t *out_ids;    // [R]
-  uint32_t barrier_polls;      // grid-barrier / tie-list / queue poll limit
+  uint32_t barrier_polls;      // grid-barrier / tie-list poll limit
   uint32_t copy_polls;         // mbarrier poll limit
   int extra_arrivals;          // >0 only in the timeout test: wait for more CTAs than exist
 };
@@ -130,6 +126,10 @@ struct FusedSmem {
   RowThreshold thr[kFMaxRows];
   unsigned long long best[kFMaxRows];
   unsigned long long tiek[kTieCap];
+  uint32_t work[kWorkCap];
+  unsigned long long mytie[64];  // this CTA's keys in a threshold bucket
+  int mytie_row[64];
+  int n_work, n_mytie;
   // generic refinement select (tie-list overflow fallback)
   uint32_t hist[kFBins];
   unsigned long long cand[kFCand];
@@ -349,6 +349,8 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     for (int s = 0; s < kS3Slots; ++s) mbar_init(&S.mbar3[s], 1);
     fence_mbar_init();
     S.s_err = 0u;
+    S.n_work = 0;
+    S.n_mytie = 0;
   }
   if (tid < kFMaxRows) S.best[tid] = 0ull;
   for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFThreads) S.coarse[i] = 0u;
@@ -359,9 +361,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   unsigned char *buf_cur = a.epoch_bufs + (size_t)(epoch & 1u) * kEpochBufBytes;
   unsigned char *buf_nxt = a.epoch_bufs + (size_t)((epoch + 1u) & 1u) * kEpochBufBytes;
   uint32_t *hist_cur = reinterpret_cast<uint32_t *>(buf_cur);
-  uint32_t *queue = reinterpret_cast<uint32_t *>(buf_cur + kHistBufBytes);
-  unsigned long long *ties =
-      reinterpret_cast<unsigned long long *>(buf_cur + kHistBufBytes + kQueueBufBytes);
+  unsigned long long *ties = reinterpret_cast<unsigned long long *>(buf_cur + kHistBufBytes);
 
   // ------------------------------------------------------------------ stage 1
   const int c0 = (int)((long long)b * a.K / G), c1 = (int)((long long)(b + 1) * a.K / G);
@@ -437,6 +437,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     if (tid == 0 && i + kS1Slots < n1) issue1(i + kS1Slots);
   }
   __syncthreads();
+  FH_STAMP(7);
   for (int i = tid; i < a.rows * kHistCoarse; i += kFThreads) {
     const uint32_t c = S.coarse[i];
     if (c) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], c);
@@ -447,6 +448,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   // ------------------------------------------------------------- grid barrier
   if (tid == 0) {
     __threadfence();
+    FH_STAMP(8);
     atomicAdd(&a.sync[kSyncArrive], 1u);
     const uint32_t target = (uint32_t)(G + a.extra_arrivals);
     uint32_t polls = 0;
@@ -474,55 +476,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     }
   }
   __syncthreads();
-
-  // ------------------- push own clusters above the bucket; bucket -> tie list
-  for (int base = 0; base < a.rows * nc; base += kFThreads) {
-    const int i = base + tid;
-    bool push = false;
-    uint32_t item = 0;
-    if (i < a.rows * nc) {
-      const int hr = i / nc, k = i - (i / nc) * nc;
-      const float v = sanitize(S.local[hr][k]);
-      const uint32_t pre = mono(v) >> 16;
-      const uint32_t P = S.thr[hr].prefix;
-      if (pre > P) {
-        push = true;
-        item = kItemValid | ((uint32_t)hr << 28) | (uint32_t)(c0 + k);
-      } else if (pre == P) {
-        const uint32_t t = atomicAdd(&a.sync[kSyncTieCount + hr], 1u);
-        if (t < (uint32_t)kTieCap) ties[(size_t)hr * kTieCap + t] = pack(v, (uint32_t)(c0 + k));
-      }
-    }
-    const unsigned m = __ballot_sync(0xFFFFFFFFu, push);
-    if (m) {
-      const int leader = __ffs(m) - 1;
-      uint32_t slot = 0;
-      if (lane == leader) slot = atomicAdd(&a.sync[kSyncQTail], (uint32_t)__popc(m));
-      slot = __shfl_sync(0xFFFFFFFFu, slot, leader) + __popc(m & ((1u << lane) - 1u));
-      if (push && slot < (uint32_t)kQueueCap) st_release_gpu(&queue[slot], item);
-    }
-  }
-  // special tokens of row b are pushed by CTA b
-  if (b < a.rows) {
-    for (int base = 0; base < a.n_special; base += kFThreads) {
-      const int t = base + tid;
-      const bool push = t < a.n_special;
-      const unsigned m = __ballot_sync(0xFFFFFFFFu, push);
-      if (m) {
-        const int leader = __ffs(m) - 1;
-        uint32_t slot = 0;
-        if (lane == leader) slot = atomicAdd(&a.sync[kSyncQTail], (uint32_t)__popc(m));
-        slot = __shfl_sync(0xFFFFFFFFu, slot, leader) + __popc(m & ((1u << lane) - 1u));
-        if (push && slot < (uint32_t)kQueueCap)
-          st_release_gpu(&queue[slot], kItemValid | kItemSpecial | ((uint32_t)b << 28) | (uint32_t)t);
-      }
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    atomicAdd(&a.sync[kSyncTieArrive], 1u);
-  }
+  FH_STAMP(9);
   // Zero this CTA's share of the buffers the next call will use.
   {
     const size_t n4 = kEpochBufBytes / 16;
@@ -530,61 +484,41 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     for (size_t i = (size_t)b * n4 / G + tid; i < (size_t)(b + 1) * n4 / G; i += kFThreads)
       z[i] = make_uint4(0, 0, 0, 0);
   }
-  FH_STAMP(3);
 
-  // ------------------------------------- tie resolution: CTA r for row r
-  if (b < a.rows) {
-    const int hr = b;
-    if (tid == 0) {
-      uint32_t polls = 0;
-      while (ld_acquire_gpu(&a.sync[kSyncTieArrive]) < (uint32_t)G) {
-        if (++polls >= a.barrier_polls) {
-          atomicOr(&S.s_err, kErrQueueTimeout);
-          break;
-        }
-      }
-      __threadfence();
-    }
-    __syncthreads();
-    const int need = S.thr[hr].need;
-    const int cnt = (int)min(__ldcg(&a.sync[kSyncTieCount + hr]), (uint32_t)S.thr[hr].cnt);
+  // ------------- own clusters above the bucket -> work list; bucket -> ties
+  for (int i = tid; i < a.rows * nc; i += kFThreads) {
+    const int hr = i / nc, k = i - (i / nc) * nc;
+    const float v = sanitize(S.local[hr][k]);
+    const uint32_t pre = mono(v) >> 16;
     const uint32_t P = S.thr[hr].prefix;
-    if (cnt <= kTieCap) {
-      for (int t = tid; t < cnt; t += kFThreads) S.tiek[t] = __ldcg(&ties[(size_t)hr * kTieCap + t]);
-      __syncthreads();
-      for (int t = tid; t < cnt; t += kFThreads) {
-        const unsigned long long mine = S.tiek[t];
-        int rank = 0;
-        for (int j = 0; j < cnt; ++j) rank += S.tiek[j] > mine;
-        if (rank < need) {
-          const uint32_t slot = atomicAdd(&a.sync[kSyncQTail], 1u);
-          if (slot < (uint32_t)kQueueCap)
-            st_release_gpu(&queue[slot], kItemValid | ((uint32_t)hr << 28) | packed_id(mine));
-        }
-      }
-    } else {
-      // Too many keys share the bucket: exact select over the whole row.
-      float *sc = reinterpret_cast<float *>(ring);
-      int *sel = reinterpret_cast<int *>(ring + (size_t)a.K * sizeof(float));
-      for (int i = tid; i < a.K; i += kFThreads) sc[i] = __ldcg(&a.scores[(size_t)hr * a.K + i]);
-      __syncthreads();
-      fused_select(sc, a.K, a.p, -INFINITY, -INFINITY, sel, S);
-      for (int t = tid; t < a.p; t += kFThreads) {
-        const int k = sel[t];
-        if (k >= 0 && k < a.K && (mono(sanitize(sc[k])) >> 16) == P) {
-          const uint32_t slot = atomicAdd(&a.sync[kSyncQTail], 1u);
-          if (slot < (uint32_t)kQueueCap)
-            st_release_gpu(&queue[slot], kItemValid | ((uint32_t)hr << 28) | (uint32_t)k);
-        }
+    if (pre > P) {
+      const int w = atomicAdd(&S.n_work, 1);
+      if (w < kWorkCap) S.work[w] = ((uint32_t)hr << 28) | (uint32_t)(c0 + k);
+    } else if (pre == P) {
+      const unsigned long long key = pack(v, (uint32_t)(c0 + k));
+      const uint32_t t = atomicAdd(&a.sync[kSyncTieCount + hr], 1u);
+      if (t < (uint32_t)kTieCap) ties[(size_t)hr * kTieCap + t] = key;
+      const int m = atomicAdd(&S.n_mytie, 1);
+      if (m < 64) {
+        S.mytie[m] = key;
+        S.mytie_row[m] = hr;
       }
     }
-    __syncthreads();
   }
-  FH_STAMP(4);
+  // special tokens of row b are scored by CTA b
+  if (b < a.rows)
+    for (int t = tid; t < a.n_special; t += kFThreads) {
+      const int w = atomicAdd(&S.n_work, 1);
+      if (w < kWorkCap) S.work[w] = kItemSpecial | ((uint32_t)b << 28) | (uint32_t)t;
+    }
+  __syncthreads();
+  FH_STAMP(10);
 
   // ------------------------------------------------------------------ stage 2
   const int row3 = a.D * (int)sizeof(HT);
-  const int rpc3 = max(1, min(min(a.cap, kS3MaxRows), kS3SlotBytes / row3));
+  int rpc3 = min(min(a.cap, kS3MaxRows), kS3SlotBytes / row3);
+  if (rpc3 >= 4) rpc3 &= ~3;  // multiples of 4 rows keep the vocab-id copies 16-byte sized
+  rpc3 = max(1, rpc3);
   const int NV3 = row3 / 16, Q3 = NV3 / 32, RG3 = kFWarps / Q3;
   const int g3 = warp / Q3, q3 = warp % Q3, col3 = q3 * 32 + lane;
   float h3[R][8];
@@ -596,48 +530,36 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
                         : make_uint4(0, 0, 0, 0);
     vec_to_float<HT>(x, h3[r]);
   }
-  const uint32_t total = (uint32_t)(a.rows * (a.p + a.n_special));
   const char *wp = reinterpret_cast<const char *>(a.w_perm);
-  // Producer state (thread 0 only): current item and its next chunk.
-  uint32_t cur_item = 0;
-  int cur_chunk = 0, cur_chunks = 0;
+  // Producer state (thread 0 only): next work item and its next chunk.
+  int p_item = 0, p_chunk = 0;
   auto produce = [&](int s) {
     S3Desc d;
     d.src = -2;
     d.n = 0;
     d.row = 0;
     d.vid_in_smem = 0;
-    if (cur_chunk >= cur_chunks) {
-      const uint32_t idx = atomicAdd(&a.sync[kSyncQHead], 1u);
-      cur_chunks = 0;
-      cur_chunk = 0;
-      if (idx < total && idx < (uint32_t)kQueueCap) {
-        uint32_t v = 0, polls = 0;
-        while (!((v = ld_acquire_gpu(&queue[idx])) & kItemValid)) {
-          if (++polls >= a.barrier_polls) {
-            atomicOr(&S.s_err, kErrQueueTimeout);
-            break;
-          }
-        }
-        if (v & kItemValid) {
-          cur_item = v;
-          cur_chunks = (v & kItemSpecial) ? 1 : (a.cap + rpc3 - 1) / rpc3;
-        }
-      }
-    }
-    if (cur_chunk < cur_chunks) {
-      d.row = (int)((cur_item >> 28) & 3u);
-      const int payload = (int)(cur_item & 0x00FFFFFFu);
-      if (cur_item & kItemSpecial) {
+    const int nw = min(S.n_work, kWorkCap);
+    if (p_item < nw) {
+      const uint32_t item = S.work[p_item];
+      d.row = (int)((item >> 28) & 3u);
+      const int payload = (int)(item & 0x00FFFFFFu);
+      if (item & kItemSpecial) {
         const int sp = payload < a.n_special ? a.special_slots[payload] : -1;
         d.src = (sp >= 0 && sp < a.K * a.cap) ? sp : -1;
         d.n = 1;
+        ++p_item;
       } else {
-        const int start = cur_chunk * rpc3;
+        const int start = p_chunk * rpc3;
         d.src = payload < a.K ? payload * a.cap + start : -1;
         d.n = min(rpc3, a.cap - start);
+        if (start + rpc3 >= a.cap) {
+          ++p_item;
+          p_chunk = 0;
+        } else {
+          ++p_chunk;
+        }
       }
-      ++cur_chunk;
     }
     S.desc[s] = d;
     fence_proxy_async_smem();
@@ -653,14 +575,65 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       mbar_expect_tx(&S.mbar3[s], 0u);  // invalid row or end of work: no data
     }
   };
-  __syncthreads();  // ring free for stage 2 (tie fallback used it)
+  // Start streaming the certain clusters, then settle this CTA's bucket keys;
+  // slots are only marked end-of-work once the work list is final.
+  int n_prod = 0;  // thread 0: chunks produced so far (chunk i uses slot i % kS3Slots)
   if (tid == 0)
-    for (int s = 0; s < kS3Slots; ++s) produce(s);
+    while (n_prod < kS3Slots && p_item < min(S.n_work, kWorkCap)) produce(n_prod++ % kS3Slots);
+  {
+    const int nmt = min(S.n_mytie, 64);
+    if (nmt > 0) {
+      // wait until every key of the bucket (count from the histogram) is listed
+      if (tid == 0) {
+        for (int hr = 0; hr < a.rows; ++hr) {
+          bool mine = false;
+          for (int m = 0; m < nmt; ++m) mine |= S.mytie_row[m] == hr;
+          if (!mine) continue;
+          const uint32_t want = (uint32_t)min(S.thr[hr].cnt, kTieCap);
+          uint32_t polls = 0;
+          while (ld_acquire_gpu(&a.sync[kSyncTieCount + hr]) < want) {
+            if (++polls >= a.barrier_polls) {
+              atomicOr(&S.s_err, kErrTieTimeout);
+              break;
+            }
+          }
+        }
+        __threadfence();
+      }
+      __syncthreads();
+      for (int m = 0; m < nmt; ++m) {
+        const int hr = S.mytie_row[m];
+        const int cnt = min(S.thr[hr].cnt, kTieCap);
+        const unsigned long long mine = S.mytie[m];
+        int rank = 0;
+        for (int t = tid; t < cnt; t += kFThreads)
+          rank += __ldcg(&ties[(size_t)hr * kTieCap + t]) > mine;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rank += __shfl_xor_sync(0xFFFFFFFFu, rank, o);
+        if (lane == 0) S.scan[warp] = rank;
+        __syncthreads();
+        if (tid == 0) {
+          int tot = 0;
+          for (int w = 0; w < kFWarps; ++w) tot += S.scan[w];
+          if (tot < S.thr[hr].need) {
+            const int w = atomicAdd(&S.n_work, 1);
+            if (w < kWorkCap) S.work[w] = ((uint32_t)hr << 28) | packed_id(mine);
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+  FH_STAMP(4);
+  __syncthreads();
+  if (tid == 0)
+    while (n_prod < kS3Slots) produce(n_prod++ % kS3Slots);
   for (int c = 0;; ++c) {
     const int s = c % kS3Slots;
     if (!mbar_wait(&S.mbar3[s], (c / kS3Slots) & 1, a.copy_polls) && lane == 0)
       atomicOr(&S.s_err, kErrCopyTimeout);
     const S3Desc d = S.desc[s];
+    if (c == 0) FH_STAMP(11);
     if (d.src == -2) break;
     if (d.src >= 0 && g3 < RG3) {
       const unsigned char *base = ring + (size_t)s * kS3SlotBytes + (size_t)col3 * 16;
@@ -690,7 +663,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       atomicMax(&S.best[d.row], pack(key, vid));
     }
     __syncthreads();  // slot s and its descriptor are free
-    if (tid == 0) produce(s);
+    if (tid == 0) produce(n_prod++ % kS3Slots);
   }
   __syncthreads();
   FH_STAMP(5);
@@ -716,9 +689,6 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     if (tid == 0) {
       a.sync[kSyncArrive] = 0u;
       a.sync[kSyncDone] = 0u;
-      a.sync[kSyncQTail] = 0u;
-      a.sync[kSyncQHead] = 0u;
-      a.sync[kSyncTieArrive] = 0u;
       a.sync[kSyncEpoch] = epoch + 1u;
     }
   }
