@@ -438,6 +438,33 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   }
   __syncthreads();
   FH_STAMP(7);
+  // Speculative L2 prefetch of stage-2 rows. HBM would sit idle through the
+  // barrier and the threshold search, so each CTA pulls the w_perm rows of
+  // its clusters that are likely to be selected: score above its own
+  // mean + z * std, where z is the normal quantile of the selection rate
+  // minus a margin. A wrong guess only costs bandwidth that was idle.
+  if (!a.do_sample && warp < a.rows && nc > 1) {
+    float sum = 0.f, sq = 0.f;
+    for (int i = lane; i < nc; i += 32) {
+      const float v = S.local[warp][i];
+      if (isfinite(v)) {
+        sum += v;
+        sq += v * v;
+      }
+    }
+    sum = warp_sum(sum);
+    sq = warp_sum(sq);
+    const float mean = sum / nc;
+    const float sd = sqrtf(fmaxf(sq / nc - mean * mean, 0.f));
+    const float frac = fminf(0.5f, (float)a.p / (float)a.K);
+    const float z = -normcdfinvf(frac) - 0.25f;
+    const float t_est = mean + z * sd;
+    const size_t cluster_bytes = (size_t)a.cap * a.D * sizeof(HT);
+    for (int i = lane; i < nc; i += 32)
+      if (S.local[warp][i] > t_est && cluster_bytes % 16 == 0)
+        bulk_prefetch_l2(reinterpret_cast<const char *>(a.w_perm) + (size_t)(c0 + i) * cluster_bytes,
+                         (uint32_t)cluster_bytes);
+  }
   for (int i = tid; i < a.rows * kHistCoarse; i += kFThreads) {
     const uint32_t c = S.coarse[i];
     if (c) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], c);
