@@ -283,8 +283,15 @@ __device__ __forceinline__ void trace_stamp(int phase) {
   }
 }
 #define FH_STAMP(p) trace_stamp(p)
+// clock64 accumulators (thread 0): tick() returns cycles since the last tick
+#define FH_TICK_DECL long long fh_t0 = clock64(); long long fh_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#define FH_TICK(k) do { const long long _t = clock64(); fh_acc[k] += _t - fh_t0; fh_t0 = _t; } while (0)
+#define FH_TICK_FLUSH() do { if (threadIdx.x == 0 && g_fh_trace) for (int _k = 0; _k < 8; ++_k) g_fh_trace[gridDim.x * 16 + blockIdx.x * 8 + _k] = fh_acc[_k]; } while (0)
 #else
 #define FH_STAMP(p) ((void)0)
+#define FH_TICK_DECL
+#define FH_TICK(k) ((void)0)
+#define FH_TICK_FLUSH() ((void)0)
 #endif
 
 __device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
@@ -397,11 +404,16 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     }
   }
 
+  FH_TICK_DECL
   for (int i = 0; i < n1; ++i) {
     const int s = i % kS1Slots;
     const int rows = min(rpc1, nc - i * rpc1);
+    FH_TICK(7);
     if (!mbar_wait(&S.mbar1[s], (i / kS1Slots) & 1, a.copy_polls) && lane == 0)
       atomicOr(&S.s_err, kErrCopyTimeout);
+    if (i == 0) FH_STAMP(13);
+    if (i == n1 - 1) FH_STAMP(14);
+    FH_TICK(0);
     if (g1 < RG1) {
       const unsigned char *base = ring + (size_t)s * kS1SlotBytes + (size_t)col1 * 16;
       for (int r = g1; r < rows; r += RG1) {
@@ -417,7 +429,9 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         }
       }
     }
+    FH_TICK(1);
     __syncthreads();
+    FH_TICK(2);
     if (tid < rows * R) {
       const int r = tid / R, hr = tid - (tid / R) * R;
       if (hr < a.rows) {
@@ -435,6 +449,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       }
     }
     if (tid == 0 && i + kS1Slots < n1) issue1(i + kS1Slots);
+    FH_TICK(3);
   }
   __syncthreads();
   FH_STAMP(7);
@@ -655,10 +670,12 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   __syncthreads();
   if (tid == 0)
     while (n_prod < kS3Slots) produce(n_prod++ % kS3Slots);
+  FH_TICK(7);
   for (int c = 0;; ++c) {
     const int s = c % kS3Slots;
     if (!mbar_wait(&S.mbar3[s], (c / kS3Slots) & 1, a.copy_polls) && lane == 0)
       atomicOr(&S.s_err, kErrCopyTimeout);
+    FH_TICK(4);
     const S3Desc d = S.desc[s];
     if (c == 0) FH_STAMP(11);
     if (d.src == -2) break;
@@ -679,6 +696,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         if (lane == 0) S.part3[s][r][q3] = acc;
       }
     }
+    FH_TICK(5);
     __syncthreads();
     if (d.src >= 0 && tid < d.n) {
       float acc = 0.f;
@@ -691,7 +709,9 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     }
     __syncthreads();  // slot s and its descriptor are free
     if (tid == 0) produce(n_prod++ % kS3Slots);
+    FH_TICK(6);
   }
+  FH_TICK_FLUSH();
   __syncthreads();
   FH_STAMP(5);
 
