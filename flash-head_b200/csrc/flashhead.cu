@@ -641,6 +641,92 @@ FH_API int fh_dense_next_token(const fh_head *head, const void *hidden, int rows
 }
 
 // ---------------------------------------------------------------------------
+// Greedy step with library-owned scratch (no workspace argument, no
+// allocation): a file-scope device array, laid out for the three-kernel path
+// as counter | packed[4] | probes[4][4096] | scores[4][16384].
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocProbesOff = 512;
+constexpr size_t kNoAllocScoresOff =
+    kNoAllocProbesOff + (size_t)FH_NOALLOC_MAX_ROWS * FH_NOALLOC_MAX_PROBES * sizeof(int32_t);
+constexpr size_t kNoAllocBytes =
+    kNoAllocScoresOff + (size_t)FH_NOALLOC_MAX_ROWS * FH_NOALLOC_MAX_CLUSTERS * sizeof(float);
+static_assert(kNoAllocBytes == FH_NOALLOC_SCRATCH_BYTES, "scratch size out of sync with the header");
+static_assert(FH_NOALLOC_MAX_CLUSTERS % 64 == 0, "score rows are padded to 64 clusters");
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+std::mutex g_noalloc_mutex;
+void *g_noalloc_addr[128];
+
+// Device address of g_noalloc_scratch on the current device, looked up once.
+int noalloc_scratch(void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "current device");
+  if (dev < 0 || dev >= 128) return fail(FH_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "address of the fixed scratch array");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return FH_OK;
+}
+}  // namespace
+
+extern "C" FH_API int fh_get_next_token_noalloc(const fh_head *head, const void *hidden,
+                                                int rows, int64_t *out_ids, fh_stream_t stream) {
+  if (!head) return fail(FH_ERR_INVALID_ARGUMENT, "null head");
+  if (rows < 0) return fail(FH_ERR_INVALID_ARGUMENT, "rows=%d < 0", rows);
+  if (rows == 0) return FH_OK;
+  if (rows > FH_NOALLOC_MAX_ROWS)
+    return fail(FH_ERR_UNSUPPORTED, "rows=%d exceeds the fixed scratch limit of %d rows", rows,
+                FH_NOALLOC_MAX_ROWS);
+  if (head->d.n_clusters > FH_NOALLOC_MAX_CLUSTERS || head->d.n_probes > FH_NOALLOC_MAX_PROBES)
+    return fail(FH_ERR_UNSUPPORTED,
+                "n_clusters=%d / n_probes=%d exceed the fixed scratch limits (%d / %d)",
+                head->d.n_clusters, head->d.n_probes, FH_NOALLOC_MAX_CLUSTERS,
+                FH_NOALLOC_MAX_PROBES);
+  if (!hidden || !out_ids) return fail(FH_ERR_INVALID_ARGUMENT, "null hidden/output pointer");
+  if (!aligned16(hidden))
+    return fail(FH_ERR_INVALID_ARGUMENT, "hidden states must be 16-byte aligned");
+  void *base = nullptr;
+  int st = noalloc_scratch(&base);
+  if (st != FH_OK) return st;
+  char *p = reinterpret_cast<char *>(base);
+  Workspace w;
+  w.counter = reinterpret_cast<unsigned *>(p);
+  w.packed = reinterpret_cast<unsigned long long *>(p + 256);
+  w.probes = reinterpret_cast<int32_t *>(p + kNoAllocProbesOff);
+  w.scores = reinterpret_cast<float *>(p + kNoAllocScoresOff);
+  w.score_stride = (int)round_up((size_t)head->d.n_clusters, 64);
+  w.epoch_bufs = nullptr;
+  w.bytes = kNoAllocBytes;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // k_scores zeroes the accumulator and the counter before stage 2 uses them.
+  st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
+  if (st != FH_OK) return st;
+  fh::Stage2Args a = stage2_args(head->d, hidden, rows);
+  a.probes = w.probes;
+  a.probe_stride = head->d.n_probes;
+  a.P = head->d.n_probes;
+  a.cluster_base = 0;
+  a.packed = w.packed;
+  a.counter = w.counter;
+  a.out_ids = out_ids;
+  a.wait_prior = 1;
+  const int items = rows * (a.P + a.n_special);
+  FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kGreedy>(head->d.weight_dtype, a, items, s, true)),
+                  "stage-2 launch");
+  return FH_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Stateless kernels with the reference's layout (fused.py)
 // ---------------------------------------------------------------------------
 static int check_stateless(const void *hs, int T, int D, const void *w_perm, const int64_t *ci,

@@ -148,6 +148,31 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
                              size_t workspace_bytes, fh_stream_t stream);
 
 /*
+ * Greedy next token WITHOUT a workspace argument; nothing is allocated. No
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they need a token, e.g. code running while a CUDA graph
+ * is being captured, a latency-critical thread that must not enter the
+ * allocator, or a host runtime whose fixed memory pool forbids cudaMalloc.
+ *
+ * Its scratch is a fixed array inside this library (FH_NOALLOC_SCRATCH_BYTES
+ * bytes of device memory that every GPU loading the library holds until the
+ * process exits). Limits: rows <= FH_NOALLOC_MAX_ROWS, n_clusters <=
+ * FH_NOALLOC_MAX_CLUSTERS, n_probes <= FH_NOALLOC_MAX_PROBES; larger requests
+ * return FH_ERR_UNSUPPORTED. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current: make that
+ * first call before capturing a CUDA graph. Every call uses the same array
+ * and clears what must start at zero itself; calls that may run at the same
+ * time on the GPU (other streams, other threads) race on it, so the caller
+ * must serialise them. Results equal fh_get_next_token's three-kernel path.
+ */
+#define FH_NOALLOC_MAX_ROWS 4
+#define FH_NOALLOC_MAX_CLUSTERS 16384
+#define FH_NOALLOC_MAX_PROBES 4096
+#define FH_NOALLOC_SCRATCH_BYTES 328192
+FH_API int fh_get_next_token_noalloc(const fh_head *head, const void *hidden, int rows,
+                                     int64_t *out_ids, fh_stream_t stream);
+
+/*
  * Sampled next token: probes drawn without replacement with probabilities
  * softmax(h.C/T) over the raw centroids, then one token drawn from
  * softmax(logit/T) over the candidates (flash_head.py:202-211, :326-328).
