@@ -4,14 +4,18 @@
 // step with one grid-wide barrier:
 //
 //  1. stage 1   CTA b streams its contiguous slice of centroid rows
-//               [b*K/G, (b+1)*K/G) through a 6-slot ring of shared-memory
-//               buffers filled by bulk asynchronous copies (TMA engine,
-//               completion on mbarriers) and scores them against the R hidden
-//               rows held in registers. Each score's key goes into global
-//               two-level histograms (256 coarse x 256 fine bins: bf16
-//               resolution).
+//               [b*K/G, (b+1)*K/G) as 16-row tiles through a 128 KB ring of
+//               shared-memory slots filled by bulk asynchronous copies (TMA
+//               engine, completion on mbarriers; one copy per tile when 16 rows
+//               fit a slot). Each tile is scored on the tensor cores with
+//               mma.m16n8k16 fragments (fp8 rows converted exactly to f16),
+//               the d-range split over the 16 warps and reduced once per tile.
+//               Each score's key goes into global two-level histograms
+//               (256 coarse x 256 fine bins: bf16 resolution).
 //  2. barrier   one arrive counter, bounded spin (a timeout sets an error bit
-//               and the kernel still runs to completion).
+//               and the kernel still runs to completion). Before arriving, each
+//               CTA prefetches into L2 the w_perm rows of its clusters that are
+//               likely to be selected, so HBM works through the barrier.
 //  3. select    one warp per hidden row finds, from two 1 KB histogram reads,
 //               the bf16 bucket that holds the p-th largest score. Each CTA
 //               keeps the clusters it scored whose key lies above that bucket;
@@ -19,12 +23,13 @@
 //               tie list, and only the CTAs owning such keys wait for the
 //               bucket's count (known from the histogram) to be reached, then
 //               rank their keys exactly (largest score, then smallest id).
-//  4. stage 2   every CTA streams the w_perm rows and vocab ids of its own
-//               selected clusters (and, for CTA r, row r's special tokens)
-//               through four 32 KB slots, scoring them and keeping the best
-//               packed (logit or Gumbel key, vocab id) word per row; words
-//               meet in a 64-bit atomicMax and the last CTA to finish
-//               publishes the ids.
+//  4. stage 2   every CTA streams the w_perm rows (and vocab ids) of its own
+//               selected clusters, and CTA r row r's special tokens, through
+//               the same ring (a whole 16-row cluster per copy when it fits a
+//               slot), scores them with mma fragments, and keeps the best
+//               packed (logit or Gumbel key, vocab id) word per row; words meet
+//               in a 64-bit atomicMax and the last CTA to finish publishes the
+//               ids.
 //
 // Histograms and tie lists alternate between two buffers by a call epoch;
 // each call zeroes the buffers of the next call and the last CTA resets the
@@ -37,19 +42,15 @@ namespace fh {
 
 constexpr int kFThreads = 512;
 constexpr int kFWarps = kFThreads / 32;
-constexpr int kS1Slots = 6;
-constexpr int kS1SlotBytes = 24 * 1024;
-constexpr int kS3Slots = 4;
-constexpr int kS3SlotBytes = 32 * 1024;
-constexpr int kFChunkRows = 16;  // max centroid rows per stage-1 chunk
-constexpr int kS3MaxRows = 32;   // max w_perm rows per stage-2 chunk
-constexpr int kFBins = 512;
-constexpr int kFCand = 256;
+constexpr int kRingBytes = 128 * 1024;
+constexpr int kMaxSlots = 4;
+constexpr int kTileRows = 16;
 constexpr int kFMaxRows = 4;
 constexpr int kFMaxProbes = 4096;
 constexpr int kFMaxSpecial = 256;
 constexpr int kTieCap = 1024;
 constexpr int kWorkCap = 1024;  // stage-2 items of one CTA (own clusters + specials)
+constexpr int kS3MaxRows = 16;  // w_perm rows per stage-2 tile (cluster size limit)
 
 // State words at the start of the workspace (uint32 index).
 constexpr int kSyncArrive = 1;
@@ -90,7 +91,7 @@ struct FusedArgs {
   int do_sample;
   float temperature;
   RngKey rng;
-  float *scores;       // [R, K] global scratch (tie fallback)
+  float *scores;       // [R, K] global scratch (exact ranking of large buckets)
   uint32_t *sync;      // workspace state words
   unsigned char *epoch_bufs;   // 2 x (histograms, tie lists)
   unsigned long long *packed;  // [R]
@@ -100,177 +101,172 @@ struct FusedArgs {
   int extra_arrivals;          // >0 only in the timeout test: wait for more CTAs than exist
 };
 
-struct S3Desc {
-  int src;   // first w_perm row; -1 invalid (empty chunk); -2 end of work
-  int n;     // rows
-  int row;   // hidden row
-  int vid_in_smem;
-};
-
 struct RowThreshold {
   uint32_t prefix;  // 16-bit key prefix of the bucket holding the p-th score
   int need;         // keys of that bucket to select
   int cnt;          // keys in that bucket
 };
 
+// One chunk of a stage-2 tile: rows [src, src + n) of w_perm, bytes
+// [dc * chunk row bytes, ...) of each row.
+struct S2Chunk {
+  int src;    // first w_perm row; -1 invalid (empty chunk); -2 end of work
+  int n;      // rows (1..16)
+  int row;    // hidden row
+  int dc;     // d-chunk index within the rows
+  int last;   // last d-chunk of this tile
+  int vid_in_smem;
+};
+
 struct FusedSmem {
-  uint64_t mbar1[kS1Slots];
-  uint64_t mbar3[kS3Slots];
-  float part1[2][kFChunkRows][16][kFMaxRows];
-  float part3[kS3Slots][kS3MaxRows][16];
+  uint64_t mbar[kMaxSlots];
+  float part[2][kFWarps][kTileRows][kFMaxRows];  // per-warp partial tile results
   float local[kFMaxRows][128];
   float scale[128];
   uint32_t coarse[kFMaxRows * kHistCoarse];
-  __align__(16) int vid[kS3Slots][kS3MaxRows];
-  S3Desc desc[kS3Slots];
+  __align__(16) int vid[kMaxSlots][kTileRows];
+  S2Chunk desc[kMaxSlots];
   RowThreshold thr[kFMaxRows];
   unsigned long long best[kFMaxRows];
-  unsigned long long tiek[kTieCap];
   uint32_t work[kWorkCap];
-  unsigned long long mytie[64];  // this CTA's keys in a threshold bucket
-  int mytie_row[64];
-  int n_work, n_mytie;
-  // generic refinement select (tie-list overflow fallback)
-  uint32_t hist[kFBins];
-  unsigned long long cand[kFCand];
-  int scan[33];
-  int s_bstar, s_above, s_cnt, s_ncand;
-  unsigned long long s_T, s_kmin, s_kmax;
+  int n_work;
+  int bucket_keys[kFMaxRows];  // this CTA's keys inside row r's threshold bucket
   uint32_t s_err;
+  uint32_t s_last;
 };
 
-constexpr size_t kFRingBytes = (size_t)kS1Slots * kS1SlotBytes > (size_t)kS3Slots * kS3SlotBytes
-                                   ? (size_t)kS1Slots * kS1SlotBytes
-                                   : (size_t)kS3Slots * kS3SlotBytes;
-constexpr size_t kFSmemBytes = kFRingBytes + sizeof(FusedSmem);
+constexpr size_t kFSmemBase = (kRingBytes + sizeof(FusedSmem) + 127) / 128 * 128;
+constexpr size_t kFSmemMax = 226 * 1024;
+
+// Dynamic shared memory of k_fused_step: ring, FusedSmem, the hidden rows as
+// stage-2 B operands [R][D] (16-bit) and, for fp8 stage-1 rows, as f16
+// stage-1 B operands [R][D].
+__host__ __device__ __forceinline__ size_t fused_smem_bytes(int R, int D, int wt_bytes) {
+  return kFSmemBase + (size_t)R * D * 2 * (wt_bytes == 1 ? 2 : 1);
+}
+
+// Ring geometry of one stage for rows of rb bytes: slots of 32 KB when a
+// 16-row tile fits, else 64 KB; a tile row is cut into chunks of cb bytes
+// when 16 full rows do not fit a slot. Rows sit in a slot at pitch
+// (one bulk copy per tile when the tile is one chunk, else one per row).
+struct RingGeom {
+  int slot_bytes, n_slots, cb, ndc, pitch;
+};
+__host__ __device__ __forceinline__ RingGeom ring_geom(int rb) {
+  RingGeom g;
+  g.slot_bytes = kTileRows * rb <= 32 * 1024 ? 32 * 1024 : 64 * 1024;
+  g.n_slots = kRingBytes / g.slot_bytes;
+  g.cb = rb < g.slot_bytes / kTileRows ? rb : g.slot_bytes / kTileRows;
+  g.ndc = (rb + g.cb - 1) / g.cb;
+  g.pitch = g.ndc == 1 ? rb : g.cb;
+  return g;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core tile GEMV: mma.m16n8k16 with f32 accumulators.
+//
+// Fragment use (lane = 4g + t): the lane loads 16 contiguous bytes of tile
+// rows g and g + 8 and the matching slice of the hidden row that feeds
+// column g. Because a dot product may take its k indices in any order as long
+// as A and B agree, k-step j of a 64-byte row group uses, for lane t,
+// elements (16t + 4j + u) of an fp8 group (4 steps) or (8t + 4j + u) of a
+// 16-bit group (2 steps), u = 0..3: slots {2t, 2t+1} take u = 0, 1 and
+// slots {2t+8, 2t+9} take u = 2, 3.
+//
+// Bank conflicts: tile rows lie at a pitch that is a multiple of 128 bytes,
+// so rows g and g + 1 (one quarter-warp of 16-byte loads) would hit the same
+// banks. Odd g therefore read the neighbouring 64-byte group (q ^ 1) of their
+// rows, and B column n carries the hidden slice of parity n & 1: column
+// 2r + (g & 1) of row g is the dot product of row g with hidden row r, exact
+// over the full row because q -> q ^ 1 permutes the groups of a chunk.
+// ---------------------------------------------------------------------------
+template <typename MT>
+__device__ __forceinline__ void mma16816(float *c, const uint32_t *a, const uint32_t *b);
+template <>
+__device__ __forceinline__ void mma16816<__half>(float *c, const uint32_t *a, const uint32_t *b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float *c, const uint32_t *a,
+                                                        const uint32_t *b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint32_t v16) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v16, __NV_E4M3);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// MMA operand type for stage-1 rows of type WT: f16 for fp8 and f16 rows,
+// bf16 for bf16 rows.
+template <typename WT>
+struct S1Mma {
+  using T = __half;
+};
+template <>
+struct S1Mma<__nv_bfloat16> {
+  using T = __nv_bfloat16;
+};
+
+// f16 copy of a hidden row for fp8 stage-1 groups: 16-byte granule gr of
+// 64-element group q is stored at granule gr ^ (q & 1), so the two granules a
+// lane reads (2t, 2t + 1) for groups q and q ^ 1 fall in different banks.
+__device__ __forceinline__ int fp8_hidden_slot(int e) {
+  const int q = e >> 6, gr = (e >> 3) & 7;
+  return (q << 6) | ((gr ^ (q & 1)) << 3) | (e & 7);
+}
+
+// One 64-byte group of a tile for this lane: rows g / g + 8 at ra / rb
+// (shared memory), hidden slice at h0 (and h1 for fp8: the second granule).
+template <typename WT, typename MT>
+__device__ __forceinline__ void tile_group(float *c, const unsigned char *ra,
+                                           const unsigned char *rb, const MT *h0,
+                                           const MT *h1) {
+  const uint4 a0 = lds128(ra), b0 = lds128(rb);
+  if constexpr (sizeof(WT) == 1) {
+    const uint4 x0 = lds128(h0), x1 = lds128(h1);
+    const uint32_t wa[4] = {a0.x, a0.y, a0.z, a0.w}, wb[4] = {b0.x, b0.y, b0.z, b0.w};
+    const uint32_t hh[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t a[4] = {fp8x2_to_f16x2(wa[j] & 0xFFFFu), fp8x2_to_f16x2(wb[j] & 0xFFFFu),
+                             fp8x2_to_f16x2(wa[j] >> 16), fp8x2_to_f16x2(wb[j] >> 16)};
+      const uint32_t b[2] = {hh[2 * j], hh[2 * j + 1]};
+      mma16816<MT>(c, a, b);
+    }
+  } else {
+    const uint4 x0 = lds128(h0);
+    {
+      const uint32_t a[4] = {a0.x, b0.x, a0.y, b0.y};
+      const uint32_t b[2] = {x0.x, x0.y};
+      mma16816<MT>(c, a, b);
+    }
+    {
+      const uint32_t a[4] = {a0.z, b0.z, a0.w, b0.w};
+      const uint32_t b[2] = {x0.z, x0.w};
+      mma16816<MT>(c, a, b);
+    }
+  }
+}
 
 template <typename T>
-__device__ __forceinline__ void vec_to_float(const uint4 &v, float *f);
+__device__ __forceinline__ T f2t(float x);
 template <>
-__device__ __forceinline__ void vec_to_float<__nv_bfloat16>(const uint4 &v, float *f) {
-  Vec<__nv_bfloat16>::to_float(v, f);
-}
-template <>
-__device__ __forceinline__ void vec_to_float<__half>(const uint4 &v, float *f) {
-  Vec<__half>::to_float(v, f);
+__device__ __forceinline__ __half f2t<__half>(float x) {
+  return __float2half_rn(x);
 }
 template <>
-__device__ __forceinline__ void vec_to_float<__nv_fp8_e4m3>(const uint4 &v, float *f) {
-  Vec<__nv_fp8_e4m3>::to_float(v, f);
+__device__ __forceinline__ __nv_bfloat16 f2t<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
 }
-
-// ---------------------------------------------------------------------------
-// Block-wide top-p selection over K scores in shared memory (512 threads).
-// Same rule as k_select: the p largest (score, -id) keys; output ascending ids.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ int fsel_bin_value(float s, float vmin, float scale) {
-  const float f = (s - vmin) * scale;
-  const int b = f >= (float)(kFBins - 1) ? kFBins - 1 : (int)f;
-  return b < 0 ? 0 : b;
-}
-
-__device__ void fused_select(const float *sc, int K, int p, float vmin, float vmax, int *out,
-                             FusedSmem &S) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float vscale = (float)kFBins / (vmax - vmin);
-  const bool value_ok = vmax > vmin && isfinite(vscale) && vscale > 0.f;
-  auto key_of = [&](int i) { return pack(sanitize(sc[i]), (uint32_t)i); };
-
-  unsigned long long alo = 0ull, ahi = ~0ull, T = 0ull;
-  int need = p;
-  for (int level = 0; level < kSelMaxLevels; ++level) {
-    const bool vm = value_ok && level == 0;
-    const unsigned long long range = ahi - alo;
-    const int shift = range == 0ull ? 0 : max(0, 64 - __clzll((long long)range) - 9);
-    for (int i = tid; i < kFBins; i += kFThreads) S.hist[i] = 0u;
-    __syncthreads();
-    for (int i = tid; i < K; i += kFThreads) {
-      const unsigned long long k = key_of(i);
-      if (k < alo || k > ahi) continue;
-      const int b = vm ? fsel_bin_value(unmono((uint32_t)(k >> 32)), vmin, vscale)
-                       : (int)((k - alo) >> shift);
-      atomicAdd(&S.hist[b], 1u);
-    }
-    __syncthreads();
-    const int mybin = kFBins - 1 - tid;  // thread t owns bin 511 - t (highest first)
-    const int c = (int)S.hist[mybin];
-    int total;
-    const int before = block_exclusive_scan(c, S.scan, &total);
-    if (before < need && need <= before + c) {
-      S.s_bstar = mybin;
-      S.s_above = before;
-      S.s_cnt = c;
-    }
-    __syncthreads();
-    const int bstar = S.s_bstar, cnt = S.s_cnt;
-    need -= S.s_above;
-    unsigned long long kmin = ~0ull, kmax = 0ull;
-    for (int i = tid; i < K; i += kFThreads) {
-      const unsigned long long k = key_of(i);
-      if (k < alo || k > ahi) continue;
-      const int b = vm ? fsel_bin_value(unmono((uint32_t)(k >> 32)), vmin, vscale)
-                       : (int)((k - alo) >> shift);
-      if (b == bstar) {
-        kmin = k < kmin ? k : kmin;
-        kmax = k > kmax ? k : kmax;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long x = __shfl_xor_sync(0xFFFFFFFFu, kmin, o);
-      const unsigned long long y = __shfl_xor_sync(0xFFFFFFFFu, kmax, o);
-      kmin = x < kmin ? x : kmin;
-      kmax = y > kmax ? y : kmax;
-    }
-    if (tid == 0) {
-      S.s_kmin = ~0ull;
-      S.s_kmax = 0ull;
-      S.s_ncand = 0;
-    }
-    __syncthreads();
-    if (lane == 0) {
-      atomicMin(&S.s_kmin, kmin);
-      atomicMax(&S.s_kmax, kmax);
-    }
-    __syncthreads();
-    alo = S.s_kmin;
-    ahi = S.s_kmax;
-    if (cnt == need) {
-      T = alo;
-      break;
-    }
-    if (cnt <= kFCand) {
-      for (int i = tid; i < K; i += kFThreads) {
-        const unsigned long long k = key_of(i);
-        if (k >= alo && k <= ahi) {
-          const int pos = atomicAdd(&S.s_ncand, 1);
-          if (pos < kFCand) S.cand[pos] = k;
-        }
-      }
-      __syncthreads();
-      const int nc = min(cnt, kFCand);
-      if (tid < nc) {
-        const unsigned long long mine = S.cand[tid];
-        int rank = 0;
-        for (int j = 0; j < nc; ++j) rank += S.cand[j] > mine;
-        if (rank == need - 1) S.s_T = mine;
-      }
-      __syncthreads();
-      T = S.s_T;
-      break;
-    }
-    __syncthreads();
-    (void)warp;
-  }
-  // Compaction in id order.
-  block_ordered_compact(
-      K, [&](int i) { return key_of(i) >= T; },
-      [&](int pos, int i) {
-        if (pos < p) out[pos] = i;
-      },
-      S.scan);
-}
-
 
 #ifdef FH_TRACE
 // Profiling builds only: per-CTA %globaltimer stamps at phase boundaries.
@@ -294,9 +290,6 @@ __device__ __forceinline__ void trace_stamp(int phase) {
 #define FH_TICK_FLUSH() ((void)0)
 #endif
 
-__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // Warp-level search of a 256-bin histogram (highest bin first) for the bin
 // holding the need-th largest key: returns the bin, the count above it and
@@ -345,21 +338,30 @@ __device__ __forceinline__ void warp_find_bin(const uint32_t *bins, int need, in
 
 template <typename HT, typename WT, int R>
 __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
-  extern __shared__ __align__(1024) unsigned char smem[];
+  using M1 = typename S1Mma<WT>::T;  // stage-1 mma operand type
+  constexpr bool kFp8 = sizeof(WT) == 1;
+  extern __shared__ __align__(128) unsigned char smem[];
   unsigned char *ring = smem;
-  FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem + kFRingBytes);
+  FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem + kRingBytes);
+  HT *hB3 = reinterpret_cast<HT *>(smem + kFSmemBase);  // [R][D] stage-2 B operand
+  // stage-1 B operand: a swizzled f16 copy for fp8 rows, else the same array
+  M1 *hB1 = kFp8 ? reinterpret_cast<M1 *>(smem + kFSmemBase + (size_t)R * a.D * 2)
+                 : reinterpret_cast<M1 *>(hB3);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x;
+  const int gq = lane >> 2, tq = lane & 3, odd = gq & 1;  // mma fragment coordinates
+  uint32_t phase = 0u;  // parity of the next completion of each slot's mbarrier
   if (tid == 0) {
-    for (int s = 0; s < kS1Slots; ++s) mbar_init(&S.mbar1[s], 1);
-    for (int s = 0; s < kS3Slots; ++s) mbar_init(&S.mbar3[s], 1);
+    for (int s = 0; s < kMaxSlots; ++s) mbar_init(&S.mbar[s], 1);
     fence_mbar_init();
     S.s_err = 0u;
     S.n_work = 0;
-    S.n_mytie = 0;
   }
-  if (tid < kFMaxRows) S.best[tid] = 0ull;
+  if (tid < kFMaxRows) {
+    S.best[tid] = 0ull;
+    S.bucket_keys[tid] = 0;
+  }
   for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFThreads) S.coarse[i] = 0u;
   __syncthreads();
   FH_STAMP(0);
@@ -373,86 +375,115 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   // ------------------------------------------------------------------ stage 1
   const int c0 = (int)((long long)b * a.K / G), c1 = (int)((long long)(b + 1) * a.K / G);
   const int nc = c1 - c0;
-  const int row1 = a.D * (int)sizeof(WT);
-  const int rpc1 = max(1, min(kFChunkRows, kS1SlotBytes / row1));
-  const int n1 = (nc + rpc1 - 1) / rpc1;
-  const char *wsrc = reinterpret_cast<const char *>(a.cw) + (size_t)c0 * row1;
-  auto issue1 = [&](int i) {
-    const int s = i % kS1Slots;
-    const int rows = min(rpc1, nc - i * rpc1);
-    const uint32_t bytes = (uint32_t)(rows * row1);
+  const int rb1 = a.D * (int)sizeof(WT);  // bytes per centroid row
+  const RingGeom g1 = ring_geom(rb1);
+  const int ntile1 = (nc + kTileRows - 1) / kTileRows;
+  const int n1 = ntile1 * g1.ndc;
+  const char *wsrc = reinterpret_cast<const char *>(a.cw) + (size_t)c0 * rb1;
+  auto issue1 = [&](int c) {
+    const int s = c % g1.n_slots, tile = c / g1.ndc, dc = c - tile * g1.ndc;
+    const int tr = min(kTileRows, nc - tile * kTileRows);
+    const int cb = min(g1.cb, rb1 - dc * g1.cb);
     fence_proxy_async_smem();
-    mbar_expect_tx(&S.mbar1[s], bytes);
-    bulk_g2s(ring + (size_t)s * kS1SlotBytes, wsrc + (size_t)i * rpc1 * row1, bytes, &S.mbar1[s]);
+    mbar_expect_tx(&S.mbar[s], (uint32_t)(tr * cb));
+    unsigned char *dst = ring + (size_t)s * g1.slot_bytes;
+    const char *src = wsrc + (size_t)tile * kTileRows * rb1 + (size_t)dc * g1.cb;
+    if (g1.ndc == 1) {
+      bulk_g2s(dst, src, (uint32_t)(tr * rb1), &S.mbar[s]);
+    } else {
+      for (int r = 0; r < tr; ++r)
+        bulk_g2s(dst + (size_t)r * g1.pitch, src + (size_t)r * rb1, (uint32_t)cb, &S.mbar[s]);
+    }
   };
   if (tid == 0)
-    for (int i = 0; i < min(kS1Slots, n1); ++i) issue1(i);
+    for (int c = 0; c < min(g1.n_slots, n1); ++c) issue1(c);
   if (tid < nc) S.scale[tid] = a.cscale ? a.cscale[c0 + tid] : 1.f;
-
-  constexpr int VE1 = Vec<WT>::kElems;
-  const int NV1 = row1 / 16, Q1 = NV1 / 32, RG1 = kFWarps / Q1;
-  const int g1 = warp / Q1, q1 = warp % Q1, col1 = q1 * 32 + lane;
-  float h1[R][VE1];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const char *hp = reinterpret_cast<const char *>(a.hidden) + (size_t)r * a.D * sizeof(HT) +
-                     (size_t)col1 * VE1 * sizeof(HT);
-#pragma unroll
-    for (int v = 0; v < VE1 / 8; ++v) {
-      const uint4 x = (r < a.rows && g1 < RG1) ? ldg_keep(hp + v * 16) : make_uint4(0, 0, 0, 0);
-      vec_to_float<HT>(x, &h1[r][v * 8]);
-    }
+  // hidden rows as mma B operands (16-bit) in shared memory
+  for (int i = tid; i < R * a.D; i += kFThreads) {
+    const int r = i / a.D, e = i - r * a.D;
+    float v = 0.f;
+    if (r < a.rows) v = (float)reinterpret_cast<const HT *>(a.hidden)[i];
+    hB3[i] = f2t<HT>(v);
+    if (kFp8) hB1[(size_t)r * a.D + fp8_hidden_slot(e)] = f2t<M1>(v);
   }
+  __syncthreads();
 
   FH_TICK_DECL
-  for (int i = 0; i < n1; ++i) {
-    const int s = i % kS1Slots;
-    const int rows = min(rpc1, nc - i * rpc1);
-    FH_TICK(7);
-    if (!mbar_wait(&S.mbar1[s], (i / kS1Slots) & 1, a.copy_polls) && lane == 0)
-      atomicOr(&S.s_err, kErrCopyTimeout);
-    if (i == 0) FH_STAMP(13);
-    if (i == n1 - 1) FH_STAMP(14);
-    FH_TICK(0);
-    if (g1 < RG1) {
-      const unsigned char *base = ring + (size_t)s * kS1SlotBytes + (size_t)col1 * 16;
-      for (int r = g1; r < rows; r += RG1) {
-        float w[VE1];
-        vec_to_float<WT>(lds128(base + (size_t)r * row1), w);
-#pragma unroll
-        for (int hr = 0; hr < R; ++hr) {
-          float acc = 0.f;
-#pragma unroll
-          for (int e = 0; e < VE1; ++e) acc = fmaf(w[e], h1[hr][e], acc);
-          acc = warp_sum(acc);
-          if (lane == 0) S.part1[i & 1][r][q1][hr] = acc;
+  {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int hrow = (gq >> 1) < R ? (gq >> 1) : 0;  // hidden row feeding column gq
+    const M1 *hrow1 = hB1 + (size_t)hrow * a.D;
+    for (int c = 0; c < n1; ++c) {
+      const int s = c % g1.n_slots, tile = c / g1.ndc, dc = c - tile * g1.ndc;
+      const int tr = min(kTileRows, nc - tile * kTileRows);
+      const int cb = min(g1.cb, rb1 - dc * g1.cb);
+      FH_TICK(7);
+      if (!mbar_wait(&S.mbar[s], (phase >> s) & 1u, a.copy_polls) && lane == 0)
+        atomicOr(&S.s_err, kErrCopyTimeout);
+      phase ^= 1u << s;
+      FH_TICK(0);
+      const unsigned char *slot = ring + (size_t)s * g1.slot_bytes;
+      const int ng = cb / 64;
+      const int qbase = dc * (g1.cb / 64);  // first 64-byte group of this chunk in the row
+      for (int grp = warp; grp < ng; grp += kFWarps) {
+        const int q = grp ^ odd;
+        const unsigned char *ra = slot + (size_t)gq * g1.pitch + q * 64 + tq * 16;
+        if constexpr (kFp8) {
+          const M1 *hg = hrow1 + (size_t)(qbase + q) * 64;
+          const int sw = (qbase + q) & 1;
+          tile_group<WT, M1>(acc, ra, ra + 8 * g1.pitch, hg + (((2 * tq) ^ sw) << 3),
+                             hg + (((2 * tq + 1) ^ sw) << 3));
+        } else {
+          const M1 *hg = hrow1 + (size_t)(qbase + q) * 32 + tq * 8;
+          tile_group<WT, M1>(acc, ra, ra + 8 * g1.pitch, hg, hg);
         }
       }
-    }
-    FH_TICK(1);
-    __syncthreads();
-    FH_TICK(2);
-    if (tid < rows * R) {
-      const int r = tid / R, hr = tid - (tid / R) * R;
-      if (hr < a.rows) {
-        float acc = 0.f;
-        for (int q = 0; q < Q1; ++q) acc += S.part1[i & 1][r][q][hr];
-        const int k = c0 + i * rpc1 + r;
-        float sc = acc * S.scale[k - c0];
-        if (a.do_sample)
-          sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)hr, (uint32_t)k);
-        S.local[hr][k - c0] = sc;
-        a.scores[(size_t)hr * a.K + k] = sc;
-        const uint32_t key = mono(sanitize(sc));
-        atomicAdd(&hist_cur[(size_t)hr * kHistWords + kHistCoarse + (key >> 16)], 1u);
-        atomicAdd(&S.coarse[hr * kHistCoarse + (key >> 24)], 1u);
+      const bool last = dc == g1.ndc - 1;
+      if (last) {
+        // lane (g, t): row g (and g + 8) against hidden row t in c[odd] (c[2 + odd])
+        const int par = tile & 1;
+        if (tq < R) {
+          S.part[par][warp][gq][tq] = acc[odd];
+          S.part[par][warp][gq + 8][tq] = acc[2 + odd];
+        }
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
       }
+      FH_TICK(1);
+      __syncthreads();
+      FH_TICK(2);
+      if (tid == 0 && c + g1.n_slots < n1) issue1(c + g1.n_slots);
+      if (last && tid < kTileRows * kFWarps) {
+        // tile reduction: thread = (row, warp); a 16-lane shuffle tree per row
+        const int row = tid >> 4, w = tid & 15, par = tile & 1;
+#pragma unroll
+        for (int col = 0; col < R; ++col) {
+          float v = S.part[par][w][row][col];
+          v += __shfl_xor_sync(0xFFFFFFFFu, v, 8);
+          v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+          v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+          v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+          if (w == 0 && row < tr && col < a.rows) {
+            const int k = c0 + tile * kTileRows + row;
+            float sc = v * S.scale[k - c0];
+            if (a.do_sample)
+              sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)col, (uint32_t)k);
+            S.local[col][k - c0] = sc;
+            a.scores[(size_t)col * a.K + k] = sc;
+            const uint32_t key = mono(sanitize(sc));
+            atomicAdd(&hist_cur[(size_t)col * kHistWords + kHistCoarse + (key >> 16)], 1u);
+            atomicAdd(&S.coarse[col * kHistCoarse + (key >> 24)], 1u);
+          }
+        }
+      }
+      FH_TICK(3);
     }
-    if (tid == 0 && i + kS1Slots < n1) issue1(i + kS1Slots);
-    FH_TICK(3);
   }
   __syncthreads();
   FH_STAMP(7);
+  for (int i = tid; i < a.rows * kHistCoarse; i += kFThreads) {
+    const uint32_t cc = S.coarse[i];
+    if (cc) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], cc);
+  }
   // Speculative L2 prefetch of stage-2 rows. HBM would sit idle through the
   // barrier and the threshold search, so each CTA pulls the w_perm rows of
   // its clusters that are likely to be selected: score above its own
@@ -479,10 +510,6 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       if (S.local[warp][i] > t_est && cluster_bytes % 16 == 0)
         bulk_prefetch_l2(reinterpret_cast<const char *>(a.w_perm) + (size_t)(c0 + i) * cluster_bytes,
                          (uint32_t)cluster_bytes);
-  }
-  for (int i = tid; i < a.rows * kHistCoarse; i += kFThreads) {
-    const uint32_t c = S.coarse[i];
-    if (c) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], c);
   }
   __syncthreads();
   FH_STAMP(1);
@@ -537,13 +564,10 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       const int w = atomicAdd(&S.n_work, 1);
       if (w < kWorkCap) S.work[w] = ((uint32_t)hr << 28) | (uint32_t)(c0 + k);
     } else if (pre == P) {
-      const unsigned long long key = pack(v, (uint32_t)(c0 + k));
-      const uint32_t t = atomicAdd(&a.sync[kSyncTieCount + hr], 1u);
-      if (t < (uint32_t)kTieCap) ties[(size_t)hr * kTieCap + t] = key;
-      const int m = atomicAdd(&S.n_mytie, 1);
-      if (m < 64) {
-        S.mytie[m] = key;
-        S.mytie_row[m] = hr;
+      atomicAdd(&S.bucket_keys[hr], 1);
+      if (S.thr[hr].cnt <= kTieCap) {
+        const uint32_t t = atomicAdd(&a.sync[kSyncTieCount + hr], 1u);
+        if (t < (uint32_t)kTieCap) ties[(size_t)hr * kTieCap + t] = pack(v, (uint32_t)(c0 + k));
       }
     }
   }
@@ -557,29 +581,18 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   FH_STAMP(10);
 
   // ------------------------------------------------------------------ stage 2
-  const int row3 = a.D * (int)sizeof(HT);
-  int rpc3 = min(min(a.cap, kS3MaxRows), kS3SlotBytes / row3);
-  if (rpc3 >= 4) rpc3 &= ~3;  // multiples of 4 rows keep the vocab-id copies 16-byte sized
-  rpc3 = max(1, rpc3);
-  const int NV3 = row3 / 16, Q3 = NV3 / 32, RG3 = kFWarps / Q3;
-  const int g3 = warp / Q3, q3 = warp % Q3, col3 = q3 * 32 + lane;
-  float h3[R][8];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const uint4 x = (r < a.rows && g3 < RG3)
-                        ? ldg_keep(reinterpret_cast<const char *>(a.hidden) +
-                                   (size_t)r * row3 + (size_t)col3 * 16)
-                        : make_uint4(0, 0, 0, 0);
-    vec_to_float<HT>(x, h3[r]);
-  }
+  const int rb3 = a.D * (int)sizeof(HT);
+  const RingGeom g3 = ring_geom(rb3);
   const char *wp = reinterpret_cast<const char *>(a.w_perm);
-  // Producer state (thread 0 only): next work item and its next chunk.
-  int p_item = 0, p_chunk = 0;
+  // Producer state (thread 0 only): next work item and its next d-chunk.
+  int p_item = 0, p_dc = 0;
   auto produce = [&](int s) {
-    S3Desc d;
+    S2Chunk d;
     d.src = -2;
     d.n = 0;
     d.row = 0;
+    d.dc = 0;
+    d.last = 1;
     d.vid_in_smem = 0;
     const int nw = min(S.n_work, kWorkCap);
     if (p_item < nw) {
@@ -590,126 +603,155 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         const int sp = payload < a.n_special ? a.special_slots[payload] : -1;
         d.src = (sp >= 0 && sp < a.K * a.cap) ? sp : -1;
         d.n = 1;
-        ++p_item;
       } else {
-        const int start = p_chunk * rpc3;
-        d.src = payload < a.K ? payload * a.cap + start : -1;
-        d.n = min(rpc3, a.cap - start);
-        if (start + rpc3 >= a.cap) {
-          ++p_item;
-          p_chunk = 0;
-        } else {
-          ++p_chunk;
-        }
+        d.src = payload < a.K ? payload * a.cap : -1;
+        d.n = a.cap;
+      }
+      d.dc = p_dc;
+      d.last = p_dc == g3.ndc - 1;
+      if (d.last) {
+        ++p_item;
+        p_dc = 0;
+      } else {
+        ++p_dc;
       }
     }
-    S.desc[s] = d;
-    fence_proxy_async_smem();
     if (d.src >= 0) {
+      const int cb = min(g3.cb, rb3 - d.dc * g3.cb);
       const int *vsrc = a.vocab_map + d.src;
-      const bool vid_bulk = ((reinterpret_cast<uintptr_t>(vsrc) & 15u) == 0) && (d.n % 4 == 0);
-      S.desc[s].vid_in_smem = vid_bulk ? 1 : 0;
-      mbar_expect_tx(&S.mbar3[s], (uint32_t)(d.n * row3) + (vid_bulk ? (uint32_t)(d.n * 4) : 0u));
-      bulk_g2s(ring + (size_t)s * kS3SlotBytes, wp + (size_t)d.src * row3, (uint32_t)(d.n * row3),
-               &S.mbar3[s]);
-      if (vid_bulk) bulk_g2s(&S.vid[s][0], vsrc, (uint32_t)(d.n * 4), &S.mbar3[s]);
+      const bool vid_bulk =
+          d.last && ((reinterpret_cast<uintptr_t>(vsrc) & 15u) == 0) && (d.n % 4 == 0);
+      d.vid_in_smem = vid_bulk ? 1 : 0;
+      S.desc[s] = d;
+      fence_proxy_async_smem();
+      mbar_expect_tx(&S.mbar[s], (uint32_t)(d.n * cb) + (vid_bulk ? (uint32_t)(d.n * 4) : 0u));
+      unsigned char *dst = ring + (size_t)s * g3.slot_bytes;
+      const char *src = wp + (size_t)d.src * rb3 + (size_t)d.dc * g3.cb;
+      if (g3.ndc == 1) {
+        bulk_g2s(dst, src, (uint32_t)(d.n * rb3), &S.mbar[s]);
+      } else {
+        for (int r = 0; r < d.n; ++r)
+          bulk_g2s(dst + (size_t)r * g3.pitch, src + (size_t)r * rb3, (uint32_t)cb, &S.mbar[s]);
+      }
+      if (vid_bulk) bulk_g2s(&S.vid[s][0], vsrc, (uint32_t)(d.n * 4), &S.mbar[s]);
     } else {
-      mbar_expect_tx(&S.mbar3[s], 0u);  // invalid row or end of work: no data
+      S.desc[s] = d;
+      mbar_expect_tx(&S.mbar[s], 0u);  // invalid row or end of work: no data
     }
   };
   // Start streaming the certain clusters, then settle this CTA's bucket keys;
-  // slots are only marked end-of-work once the work list is final.
-  int n_prod = 0;  // thread 0: chunks produced so far (chunk i uses slot i % kS3Slots)
+  // slots are only marked end-of-work once the work list is final. Chunk i of
+  // stage 2 uses slot i % n_slots.
+  int n_prod = 0;  // thread 0: next chunk to produce
   if (tid == 0)
-    while (n_prod < kS3Slots && p_item < min(S.n_work, kWorkCap)) produce(n_prod++ % kS3Slots);
-  {
-    const int nmt = min(S.n_mytie, 64);
-    if (nmt > 0) {
-      // wait until every key of the bucket (count from the histogram) is listed
-      if (tid == 0) {
-        for (int hr = 0; hr < a.rows; ++hr) {
-          bool mine = false;
-          for (int m = 0; m < nmt; ++m) mine |= S.mytie_row[m] == hr;
-          if (!mine) continue;
-          const uint32_t want = (uint32_t)min(S.thr[hr].cnt, kTieCap);
-          uint32_t polls = 0;
-          while (ld_acquire_gpu(&a.sync[kSyncTieCount + hr]) < want) {
-            if (++polls >= a.barrier_polls) {
-              atomicOr(&S.s_err, kErrTieTimeout);
-              break;
-            }
+    while (n_prod < g3.n_slots && p_item < min(S.n_work, kWorkCap)) produce(n_prod++ % g3.n_slots);
+  // Rank this CTA's bucket keys exactly, one warp per key, against the full
+  // bucket: the published tie list (complete once its count reaches the
+  // histogram's), or, for a bucket larger than the list, the scores row itself.
+  bool any_bucket = false;
+  for (int hr = 0; hr < a.rows; ++hr) any_bucket |= S.bucket_keys[hr] > 0;
+  if (any_bucket) {
+    if (tid == 0) {
+      for (int hr = 0; hr < a.rows; ++hr) {
+        if (S.bucket_keys[hr] == 0 || S.thr[hr].cnt > kTieCap) continue;
+        const uint32_t want = (uint32_t)S.thr[hr].cnt;
+        uint32_t polls = 0;
+        while (ld_acquire_gpu(&a.sync[kSyncTieCount + hr]) < want) {
+          if (++polls >= a.barrier_polls) {
+            atomicOr(&S.s_err, kErrTieTimeout);
+            break;
           }
         }
-        __threadfence();
       }
-      __syncthreads();
-      for (int m = 0; m < nmt; ++m) {
-        const int hr = S.mytie_row[m];
-        const int cnt = min(S.thr[hr].cnt, kTieCap);
-        const unsigned long long mine = S.mytie[m];
-        int rank = 0;
-        for (int t = tid; t < cnt; t += kFThreads)
-          rank += __ldcg(&ties[(size_t)hr * kTieCap + t]) > mine;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) rank += __shfl_xor_sync(0xFFFFFFFFu, rank, o);
-        if (lane == 0) S.scan[warp] = rank;
-        __syncthreads();
-        if (tid == 0) {
-          int tot = 0;
-          for (int w = 0; w < kFWarps; ++w) tot += S.scan[w];
-          if (tot < S.thr[hr].need) {
-            const int w = atomicAdd(&S.n_work, 1);
-            if (w < kWorkCap) S.work[w] = ((uint32_t)hr << 28) | packed_id(mine);
-          }
+      __threadfence();
+    }
+    __syncthreads();
+    for (int i = warp; i < a.rows * nc; i += kFWarps) {
+      const int hr = i / nc, k = i - (i / nc) * nc;
+      const float v = sanitize(S.local[hr][k]);
+      const uint32_t P = S.thr[hr].prefix;
+      if ((mono(v) >> 16) != P) continue;  // warp-uniform
+      const unsigned long long mine = pack(v, (uint32_t)(c0 + k));
+      const int cnt = S.thr[hr].cnt;
+      int rank = 0;
+      if (cnt <= kTieCap) {
+        for (int t = lane; t < cnt; t += 32) rank += __ldcg(&ties[(size_t)hr * kTieCap + t]) > mine;
+      } else {
+        for (int t = lane; t < a.K; t += 32) {
+          const float u = sanitize(__ldcg(&a.scores[(size_t)hr * a.K + t]));
+          rank += (mono(u) >> 16) == P && pack(u, (uint32_t)t) > mine;
         }
-        __syncthreads();
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) rank += __shfl_xor_sync(0xFFFFFFFFu, rank, o);
+      if (lane == 0 && rank < S.thr[hr].need) {
+        const int w = atomicAdd(&S.n_work, 1);
+        if (w < kWorkCap) S.work[w] = ((uint32_t)hr << 28) | (uint32_t)(c0 + k);
       }
     }
   }
   FH_STAMP(4);
   __syncthreads();
   if (tid == 0)
-    while (n_prod < kS3Slots) produce(n_prod++ % kS3Slots);
+    while (n_prod < g3.n_slots) produce(n_prod++ % g3.n_slots);
   FH_TICK(7);
-  for (int c = 0;; ++c) {
-    const int s = c % kS3Slots;
-    if (!mbar_wait(&S.mbar3[s], (c / kS3Slots) & 1, a.copy_polls) && lane == 0)
-      atomicOr(&S.s_err, kErrCopyTimeout);
-    FH_TICK(4);
-    const S3Desc d = S.desc[s];
-    if (c == 0) FH_STAMP(11);
-    if (d.src == -2) break;
-    if (d.src >= 0 && g3 < RG3) {
-      const unsigned char *base = ring + (size_t)s * kS3SlotBytes + (size_t)col3 * 16;
-      for (int r = g3; r < d.n; r += RG3) {
-        float w[8];
-        vec_to_float<HT>(lds128(base + (size_t)r * row3), w);
-        float acc = 0.f;
-#pragma unroll
-        for (int hh = 0; hh < R; ++hh) {
-          if (hh == d.row) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc = fmaf(w[e], h3[hh][e], acc);
-          }
+  {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int tile = 0;
+    for (int c = 0;; ++c) {
+      const int s = c % g3.n_slots;
+      if (!mbar_wait(&S.mbar[s], (phase >> s) & 1u, a.copy_polls) && lane == 0)
+        atomicOr(&S.s_err, kErrCopyTimeout);
+      phase ^= 1u << s;
+      FH_TICK(4);
+      const S2Chunk d = S.desc[s];
+      if (c == 0) FH_STAMP(11);
+      if (d.src == -2) break;
+      if (d.src >= 0) {
+        const int cb = min(g3.cb, rb3 - d.dc * g3.cb);
+        const unsigned char *slot = ring + (size_t)s * g3.slot_bytes;
+        const int ng = cb / 64;
+        const HT *hrow3 = hB3 + (size_t)d.row * a.D + (size_t)d.dc * (g3.cb / 2) + tq * 8;
+        for (int grp = warp; grp < ng; grp += kFWarps) {
+          const int q = grp ^ odd;
+          const unsigned char *ra = slot + (size_t)gq * g3.pitch + q * 64 + tq * 16;
+          tile_group<HT, HT>(acc, ra, ra + 8 * g3.pitch, hrow3 + q * 32, hrow3 + q * 32);
         }
-        acc = warp_sum(acc);
-        if (lane == 0) S.part3[s][r][q3] = acc;
       }
+      // vocab id of tile row tid >> 4, read before the slot is refilled
+      uint32_t vid = 0u;
+      if (d.last && d.src >= 0 && tid < kTileRows * kFWarps && (tid & 15) == 0 &&
+          (tid >> 4) < d.n)
+        vid = (uint32_t)(d.vid_in_smem ? S.vid[s][tid >> 4] : __ldg(&a.vocab_map[d.src + (tid >> 4)]));
+      if (d.last) {
+        // every B column pair holds hidden row d.row: lanes t == 0 carry rows g, g + 8
+        const int par = tile & 1;
+        if (tq == 0) {
+          S.part[par][warp][gq][0] = acc[odd];
+          S.part[par][warp][gq + 8][0] = acc[2 + odd];
+        }
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+      }
+      FH_TICK(5);
+      __syncthreads();  // slot s is free; partials of a finished tile are visible
+      if (tid == 0) produce(n_prod++ % g3.n_slots);
+      if (d.last && d.src >= 0 && tid < kTileRows * kFWarps) {
+        const int row = tid >> 4, w = tid & 15, par = tile & 1;
+        float v = S.part[par][w][row][0];
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, 8);
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+        if (w == 0 && row < d.n) {
+          float key = v;
+          if (a.do_sample)
+            key = v / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)d.row, vid);
+          atomicMax(&S.best[d.row], pack(key, vid));
+        }
+      }
+      if (d.last) ++tile;
+      FH_TICK(6);
     }
-    FH_TICK(5);
-    __syncthreads();
-    if (d.src >= 0 && tid < d.n) {
-      float acc = 0.f;
-      for (int q = 0; q < Q3; ++q) acc += S.part3[s][tid][q];
-      const uint32_t vid = (uint32_t)(d.vid_in_smem ? S.vid[s][tid] : a.vocab_map[d.src + tid]);
-      float key = acc;
-      if (a.do_sample)
-        key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)d.row, vid);
-      atomicMax(&S.best[d.row], pack(key, vid));
-    }
-    __syncthreads();  // slot s and its descriptor are free
-    if (tid == 0) produce(n_prod++ % kS3Slots);
-    FH_TICK(6);
   }
   FH_TICK_FLUSH();
   __syncthreads();
@@ -719,14 +761,13 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   if (tid < a.rows && S.best[tid] != 0ull) atomicMax(&a.packed[tid], S.best[tid]);
   if (tid == 0 && S.s_err) atomicOr(&a.sync[kSyncError], S.s_err);
   __syncthreads();
-  __shared__ uint32_t s_last;
   if (tid == 0) {
     __threadfence();
-    s_last = atomicAdd(&a.sync[kSyncDone], 1u) == (uint32_t)G - 1;
+    S.s_last = atomicAdd(&a.sync[kSyncDone], 1u) == (uint32_t)G - 1;
   }
   __syncthreads();
   FH_STAMP(6);
-  if (s_last) {
+  if (S.s_last) {
     __threadfence();
     if (tid < a.rows) {
       const unsigned long long wv = atomicExch(&a.packed[tid], 0ull);

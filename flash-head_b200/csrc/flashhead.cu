@@ -112,7 +112,7 @@ cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream
     std::lock_guard<std::mutex> lock(g_attr_mutex);
     if (!attr_done[dev]) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fh::kFSmemBytes);
+                               (int)fh::kFSmemMax);
       if (e != cudaSuccess) return e;
       attr_done[dev] = true;
     }
@@ -121,7 +121,7 @@ cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(fh::kFThreads);
-  cfg.dynamicSmemBytes = fh::kFSmemBytes;
+  cfg.dynamicSmemBytes = fh::fused_smem_bytes(R, a.D, (int)sizeof(WT));
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
@@ -349,9 +349,11 @@ bool fused_ok(const fh_head_desc &d, int rows, bool sample, int grid) {
   if (d.flags & FH_FLAG_NO_FUSED) return false;
   if (rows < 1 || rows > fh::kFMaxRows || grid < rows || d.cluster_base != 0) return false;
   const int wdt = sample ? d.sample_dtype : d.score_dtype;
-  const int nv1 = d.hidden * (wdt == FH_FP8_E4M3 ? 1 : 2) / 16;
-  const int nv3 = d.hidden * 2 / 16;
-  if (nv1 % 32 || nv1 > 512 || nv3 % 32 || nv3 > 512) return false;
+  // rows of whole 128-byte group pairs; hidden rows (16-bit) in shared memory
+  const int wt_bytes = wdt == FH_FP8_E4M3 ? 1 : 2;
+  if ((d.hidden * wt_bytes) % 128 != 0 || (d.hidden * 2) % 128 != 0) return false;
+  const int R = rows <= 1 ? 1 : rows <= 2 ? 2 : 4;
+  if (fh::fused_smem_bytes(R, d.hidden, wt_bytes) > fh::kFSmemMax) return false;
   if (d.n_clusters > 128 * grid || d.n_clusters > fh::kSelMaxItems) return false;
   if (d.n_probes > fh::kFMaxProbes || d.cluster_size > fh::kS3MaxRows) return false;
   if (d.n_special > fh::kFMaxSpecial || d.n_clusters >= (1 << 24)) return false;

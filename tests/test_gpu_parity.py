@@ -431,6 +431,26 @@ def test_fused_step_shapes(K, cap, D, p):
         assert nh.workspace_error() == 0
 
 
+def test_fused_step_bucket_larger_than_tie_list(llama1b_heads):
+    """A zero hidden row ties all 8016 cluster scores in one bf16 bucket, far
+    more keys than the one-kernel step's 1024-entry tie list: the bucket is
+    ranked against the scores row instead, so the probes are clusters 0..p-1
+    (equal scores, smallest ids first) and the token is the smallest vocab id
+    among them, exactly as the oracle and the three-kernel path pick it."""
+    from flash_head.synthetic import make_hidden
+    fh = llama1b_heads["fp8"]
+    nh, twin = _native_pair(fh)
+    ov = OracleView(fh)
+    H = make_hidden(2, fh._D, seed=123, device="cuda")
+    H[0].zero_()
+    fused = nh.next_token(H).cpu().numpy()
+    three = twin.next_token(H).cpu().numpy()
+    want0 = ov.greedy_given_probes(np.zeros(fh._D, np.float32), np.arange(fh.n_probes))
+    assert fused[0] == three[0] == want0
+    check_greedy_rows(fh, H[1:], fused[1:], nh.top_clusters(H[1:]).cpu().numpy())
+    assert nh.workspace_error() == 0
+
+
 def test_fused_step_special_tokens(golden_small):
     """Fused path (D=64 is below its minimum, so use a D=512 head) with specials."""
     from flash_head.synthetic import make_hidden
