@@ -16,40 +16,47 @@
 //               and the kernel still runs to completion). Before arriving, each
 //               CTA prefetches into L2 the w_perm rows of its clusters that are
 //               likely to be selected, so HBM works through the barrier.
-//  3. select    one warp per hidden row finds, from two 1 KB histogram reads,
-//               the bf16 bucket that holds the p-th largest score. Each CTA
-//               keeps the clusters it scored whose key lies above that bucket;
-//               keys inside the bucket (a handful) are published to a small
-//               tie list, and only the CTAs owning such keys wait for the
-//               bucket's count (known from the histogram) to be reached, then
-//               rank their keys exactly (largest score, then smallest id).
-//  4. stage 2   every CTA streams the w_perm rows (and vocab ids) of its own
-//               selected clusters, and CTA r row r's special tokens, through
-//               the same ring (a whole 16-row cluster per copy when it fits a
-//               slot), scores them with mma fragments, and keeps the best
-//               packed (logit or Gumbel key, vocab id) word per row; words meet
-//               in a 64-bit atomicMax and the last CTA to finish publishes the
-//               ids.
+//  3. select    every CTA copies the full score rows (32 KB per row at
+//               K = 8016) from L2 into shared memory while one warp per hidden
+//               row finds, from two 1 KB histogram reads, the bf16 bucket that
+//               holds the p-th largest score. The exact threshold key inside
+//               that bucket (largest score, then smallest id) is ranked from
+//               the bucket's few keys, or by a 6-pass radix select over the
+//               row when the bucket is large. Every CTA thus knows the whole
+//               selection without waiting on any other CTA.
+//  4. stage 2   the step's items (per row: the p selected clusters in id order,
+//               then the special tokens) are split into G equal contiguous
+//               ranges; CTA b streams the w_perm rows (and vocab ids) of its
+//               range through the same ring (a whole 16-row cluster per copy
+//               when it fits a slot), scores them with mma fragments, and keeps
+//               the best packed (logit or Gumbel key, vocab id) word per row;
+//               words meet in a 64-bit atomicMax and the last CTA to finish
+//               publishes the ids.
 //
-// Histograms and tie lists alternate between two buffers by a call epoch;
-// each call zeroes the buffers of the next call and the last CTA resets the
-// counters, so a workspace zero-filled once stays consistent.
+// Histograms alternate between two buffers by a call epoch; each call zeroes
+// the buffers of the next call and the last CTA resets the counters, so a
+// workspace zero-filled once stays consistent.
 #pragma once
 
 #include "fh_kernels.cuh"
 
 namespace fh {
 
-constexpr int kFThreads = 512;
+constexpr int kFThreads = 512;             // 16 compute warps
 constexpr int kFWarps = kFThreads / 32;
+constexpr int kFBlock = kFThreads + 32;    // + one producer / reducer warp
+// Named barriers between the compute warps and the producer warp.
+constexpr int kBarSlot0 = 1;  // 1..4: slot s consumed (and a finished tile's partials written)
+constexpr int kBarPart0 = 5;  // 5..6: partial buffer (tile & 1) reduced, free again
+constexpr int kMaxChunks = 160;  // 128-cluster chunks of a score row
 constexpr int kRingBytes = 128 * 1024;
 constexpr int kMaxSlots = 4;
 constexpr int kTileRows = 16;
 constexpr int kFMaxRows = 4;
 constexpr int kFMaxProbes = 4096;
 constexpr int kFMaxSpecial = 256;
-constexpr int kTieCap = 1024;
-constexpr int kWorkCap = 1024;  // stage-2 items of one CTA (own clusters + specials)
+constexpr int kBktCap = 64;     // bucket keys ranked directly; larger buckets: radix select
+constexpr int kWorkCap = 1024;  // stage-2 items of one CTA
 constexpr int kS3MaxRows = 16;  // w_perm rows per stage-2 tile (cluster size limit)
 
 // State words at the start of the workspace (uint32 index).
@@ -57,19 +64,15 @@ constexpr int kSyncArrive = 1;
 constexpr int kSyncDone = 2;
 constexpr int kSyncError = 3;
 constexpr int kSyncEpoch = 4;
-constexpr int kSyncTieCount = 8;  // [8 + r]
 
 constexpr int kHistCoarse = 256;
 constexpr int kHistWords = kHistCoarse + 65536;
-// Per-epoch buffers (two of each).
-constexpr size_t kHistBufBytes = (size_t)kFMaxRows * kHistWords * sizeof(uint32_t);
-constexpr size_t kTieBufBytes = (size_t)kFMaxRows * kTieCap * sizeof(unsigned long long);
-constexpr size_t kEpochBufBytes = kHistBufBytes + kTieBufBytes;
+// Per-epoch histogram buffers (two).
+constexpr size_t kEpochBufBytes = (size_t)kFMaxRows * kHistWords * sizeof(uint32_t);
 constexpr size_t kHistBytes = 2 * kEpochBufBytes;  // workspace bytes of all epoch buffers
 
 constexpr uint32_t kErrBarrierTimeout = 1u;
 constexpr uint32_t kErrCopyTimeout = 2u;
-constexpr uint32_t kErrTieTimeout = 4u;
 
 // Stage-2 work item: bit 30 special token, bits 28-29 hidden row, bits 0-23
 // cluster id (or special-token index).
@@ -91,12 +94,13 @@ struct FusedArgs {
   int do_sample;
   float temperature;
   RngKey rng;
-  float *scores;       // [R, K] global scratch (exact ranking of large buckets)
+  float *scores;       // [R, score_stride] global scratch: every CTA reads all scores
+  int score_stride;    // multiple of 4
   uint32_t *sync;      // workspace state words
-  unsigned char *epoch_bufs;   // 2 x (histograms, tie lists)
+  unsigned char *epoch_bufs;   // 2 x histograms
   unsigned long long *packed;  // [R]
   int64_t *out_ids;    // [R]
-  uint32_t barrier_polls;      // grid-barrier / tie-list poll limit
+  uint32_t barrier_polls;      // grid-barrier poll limit
   uint32_t copy_polls;         // mbarrier poll limit
   int extra_arrivals;          // >0 only in the timeout test: wait for more CTAs than exist
 };
@@ -120,7 +124,7 @@ struct S2Chunk {
 
 struct FusedSmem {
   uint64_t mbar[kMaxSlots];
-  float part[2][kFWarps][kTileRows][kFMaxRows];  // per-warp partial tile results
+  __align__(16) float part[2][kTileRows][kFMaxRows][kFWarps];  // per-warp partial tile results
   float local[kFMaxRows][128];
   float scale[128];
   uint32_t coarse[kFMaxRows * kHistCoarse];
@@ -128,9 +132,15 @@ struct FusedSmem {
   S2Chunk desc[kMaxSlots];
   RowThreshold thr[kFMaxRows];
   unsigned long long best[kFMaxRows];
+  unsigned long long tkey[kFMaxRows];          // selection: key >= tkey[r]
+  unsigned long long bkt[kFMaxRows][kBktCap];  // keys of row r's threshold bucket
+  int bkt_n[kFMaxRows];
+  __align__(16) uint32_t rhist[256];           // radix-select digit histogram
+  int rsel_bin, rsel_above;
+  int chunk_sel[kFMaxRows][kMaxChunks];        // selected keys per 128-cluster chunk
+  int chunk_off[kFMaxRows][kMaxChunks];        // their first position in id order
   uint32_t work[kWorkCap];
   int n_work;
-  int bucket_keys[kFMaxRows];  // this CTA's keys inside row r's threshold bucket
   uint32_t s_err;
   uint32_t s_last;
 };
@@ -226,8 +236,9 @@ __device__ __forceinline__ int fp8_hidden_slot(int e) {
 
 // One 64-byte group of a tile for this lane: rows g / g + 8 at ra / rb
 // (shared memory), hidden slice at h0 (and h1 for fp8: the second granule).
+// Even k-steps accumulate into c0, odd ones into c1 (two independent chains).
 template <typename WT, typename MT>
-__device__ __forceinline__ void tile_group(float *c, const unsigned char *ra,
+__device__ __forceinline__ void tile_group(float *c0, float *c1, const unsigned char *ra,
                                            const unsigned char *rb, const MT *h0,
                                            const MT *h1) {
   const uint4 a0 = lds128(ra), b0 = lds128(rb);
@@ -240,21 +251,31 @@ __device__ __forceinline__ void tile_group(float *c, const unsigned char *ra,
       const uint32_t a[4] = {fp8x2_to_f16x2(wa[j] & 0xFFFFu), fp8x2_to_f16x2(wb[j] & 0xFFFFu),
                              fp8x2_to_f16x2(wa[j] >> 16), fp8x2_to_f16x2(wb[j] >> 16)};
       const uint32_t b[2] = {hh[2 * j], hh[2 * j + 1]};
-      mma16816<MT>(c, a, b);
+      mma16816<MT>((j & 1) ? c1 : c0, a, b);
     }
   } else {
     const uint4 x0 = lds128(h0);
     {
       const uint32_t a[4] = {a0.x, b0.x, a0.y, b0.y};
       const uint32_t b[2] = {x0.x, x0.y};
-      mma16816<MT>(c, a, b);
+      mma16816<MT>(c0, a, b);
     }
     {
       const uint32_t a[4] = {a0.z, b0.z, a0.w, b0.w};
       const uint32_t b[2] = {x0.z, x0.w};
-      mma16816<MT>(c, a, b);
+      mma16816<MT>(c1, a, b);
     }
   }
+}
+
+// Named barriers (warp-aligned: every lane of a warp calls them together).
+__device__ __forceinline__ void nbar_arrive(int id, int n) {
+  __syncwarp();
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void nbar_sync(int id, int n) {
+  __syncwarp();
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 template <typename T>
@@ -275,16 +296,18 @@ __device__ __forceinline__ void trace_stamp(int phase) {
   if (threadIdx.x == 0 && g_fh_trace) {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g_fh_trace[blockIdx.x * 16 + phase] = t;
+    g_fh_trace[blockIdx.x * 24 + phase] = t;
   }
 }
 #define FH_STAMP(p) trace_stamp(p)
+#define FH_STAMP_P(p) do { if (threadIdx.x == kFThreads && g_fh_trace) { unsigned long long _t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(_t)); g_fh_trace[blockIdx.x * 24 + (p)] = _t; } } while (0)
 // clock64 accumulators (thread 0): tick() returns cycles since the last tick
 #define FH_TICK_DECL long long fh_t0 = clock64(); long long fh_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #define FH_TICK(k) do { const long long _t = clock64(); fh_acc[k] += _t - fh_t0; fh_t0 = _t; } while (0)
-#define FH_TICK_FLUSH() do { if (threadIdx.x == 0 && g_fh_trace) for (int _k = 0; _k < 8; ++_k) g_fh_trace[gridDim.x * 16 + blockIdx.x * 8 + _k] = fh_acc[_k]; } while (0)
+#define FH_TICK_FLUSH() do { if (threadIdx.x == 0 && g_fh_trace) for (int _k = 0; _k < 8; ++_k) g_fh_trace[gridDim.x * 24 + blockIdx.x * 8 + _k] = fh_acc[_k]; } while (0)
 #else
 #define FH_STAMP(p) ((void)0)
+#define FH_STAMP_P(p) ((void)0)
 #define FH_TICK_DECL
 #define FH_TICK(k) ((void)0)
 #define FH_TICK_FLUSH() ((void)0)
@@ -294,12 +317,15 @@ __device__ __forceinline__ void trace_stamp(int phase) {
 // Warp-level search of a 256-bin histogram (highest bin first) for the bin
 // holding the need-th largest key: returns the bin, the count above it and
 // the bin's count (all lanes).
+template <bool kGlobal>
 __device__ __forceinline__ void warp_find_bin(const uint32_t *bins, int need, int &bin,
                                               int &above, int &cnt) {
   const int lane = threadIdx.x & 31;
   // lane l owns bins 255-8l .. 248-8l (descending)
-  const uint4 lo = __ldcg(reinterpret_cast<const uint4 *>(bins + 248 - 8 * lane));
-  const uint4 hi = __ldcg(reinterpret_cast<const uint4 *>(bins + 252 - 8 * lane));
+  const uint4 *plo = reinterpret_cast<const uint4 *>(bins + 248 - 8 * lane);
+  const uint4 *phi = reinterpret_cast<const uint4 *>(bins + 252 - 8 * lane);
+  const uint4 lo = kGlobal ? __ldcg(plo) : *plo;
+  const uint4 hi = kGlobal ? __ldcg(phi) : *phi;
   const uint32_t c[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
   int mine = 0;
 #pragma unroll
@@ -337,7 +363,7 @@ __device__ __forceinline__ void warp_find_bin(const uint32_t *bins, int need, in
 }
 
 template <typename HT, typename WT, int R>
-__global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
+__global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   using M1 = typename S1Mma<WT>::T;  // stage-1 mma operand type
   constexpr bool kFp8 = sizeof(WT) == 1;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -349,9 +375,10 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
                  : reinterpret_cast<M1 *>(hB3);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool producer = warp == kFWarps;  // TMA issue + tile reductions
   const int G = gridDim.x, b = blockIdx.x;
   const int gq = lane >> 2, tq = lane & 3, odd = gq & 1;  // mma fragment coordinates
-  uint32_t phase = 0u;  // parity of the next completion of each slot's mbarrier
+  uint32_t phase = 0u;  // compute warps: parity of each slot's next mbarrier completion
   if (tid == 0) {
     for (int s = 0; s < kMaxSlots; ++s) mbar_init(&S.mbar[s], 1);
     fence_mbar_init();
@@ -360,9 +387,9 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   }
   if (tid < kFMaxRows) {
     S.best[tid] = 0ull;
-    S.bucket_keys[tid] = 0;
+    S.bkt_n[tid] = 0;
   }
-  for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFThreads) S.coarse[i] = 0u;
+  for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFBlock) S.coarse[i] = 0u;
   __syncthreads();
   FH_STAMP(0);
 
@@ -370,7 +397,6 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   unsigned char *buf_cur = a.epoch_bufs + (size_t)(epoch & 1u) * kEpochBufBytes;
   unsigned char *buf_nxt = a.epoch_bufs + (size_t)((epoch + 1u) & 1u) * kEpochBufBytes;
   uint32_t *hist_cur = reinterpret_cast<uint32_t *>(buf_cur);
-  unsigned long long *ties = reinterpret_cast<unsigned long long *>(buf_cur + kHistBufBytes);
 
   // ------------------------------------------------------------------ stage 1
   const int c0 = (int)((long long)b * a.K / G), c1 = (int)((long long)(b + 1) * a.K / G);
@@ -395,27 +421,52 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         bulk_g2s(dst + (size_t)r * g1.pitch, src + (size_t)r * rb1, (uint32_t)cb, &S.mbar[s]);
     }
   };
-  if (tid == 0)
-    for (int c = 0; c < min(g1.n_slots, n1); ++c) issue1(c);
-  if (tid < nc) S.scale[tid] = a.cscale ? a.cscale[c0 + tid] : 1.f;
-  // hidden rows as mma B operands (16-bit) in shared memory
-  for (int i = tid; i < R * a.D; i += kFThreads) {
-    const int r = i / a.D, e = i - r * a.D;
-    float v = 0.f;
-    if (r < a.rows) v = (float)reinterpret_cast<const HT *>(a.hidden)[i];
-    hB3[i] = f2t<HT>(v);
-    if (kFp8) hB1[(size_t)r * a.D + fp8_hidden_slot(e)] = f2t<M1>(v);
+  if (producer) {
+    if (lane == 0)
+      for (int c = 0; c < min(g1.n_slots, n1); ++c) issue1(c);
+    FH_STAMP_P(15);
+  } else {
+    if (tid < nc) S.scale[tid] = a.cscale ? a.cscale[c0 + tid] : 1.f;
+    // hidden rows as mma B operands (16-bit) in shared memory, 16 bytes per
+    // thread and load (one round trip for R * D <= 4096)
+    for (int i = tid; i < R * a.D / 8; i += kFThreads) {
+      const int e0 = i * 8, r = e0 / a.D, e = e0 - r * a.D;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < a.rows) v = __ldg(reinterpret_cast<const uint4 *>(a.hidden) + i);
+      reinterpret_cast<uint4 *>(hB3)[i] = v;
+      if constexpr (kFp8) {
+        float f[8];
+        Vec<HT>::to_float(v, f);
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const __half2 h2 = __floats2half2_rn(f[2 * u], f[2 * u + 1]);
+          w[u] = *reinterpret_cast<const uint32_t *>(&h2);
+        }
+        *reinterpret_cast<uint4 *>(hB1 + (size_t)r * a.D + fp8_hidden_slot(e)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    // Zero this CTA's share of the histograms the next call will use.
+    constexpr int n4 = (int)(kEpochBufBytes / 16);
+    uint4 *z = reinterpret_cast<uint4 *>(buf_nxt);
+    const int z1 = (int)((long long)(b + 1) * n4 / G);
+    for (int i = (int)((long long)b * n4 / G) + tid; i < z1; i += kFThreads)
+      z[i] = make_uint4(0, 0, 0, 0);
+    FH_STAMP(16);
   }
   __syncthreads();
+  FH_STAMP(17);
 
   FH_TICK_DECL
-  {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (!producer) {
+    // Compute warps: stream the tiles; partials of a tile go to
+    // part[tile & 1] once the producer has reduced tile - 2 from it.
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
     const int hrow = (gq >> 1) < R ? (gq >> 1) : 0;  // hidden row feeding column gq
     const M1 *hrow1 = hB1 + (size_t)hrow * a.D;
     for (int c = 0; c < n1; ++c) {
       const int s = c % g1.n_slots, tile = c / g1.ndc, dc = c - tile * g1.ndc;
-      const int tr = min(kTileRows, nc - tile * kTileRows);
       const int cb = min(g1.cb, rb1 - dc * g1.cb);
       FH_TICK(7);
       if (!mbar_wait(&S.mbar[s], (phase >> s) & 1u, a.copy_polls) && lane == 0)
@@ -431,85 +482,66 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         if constexpr (kFp8) {
           const M1 *hg = hrow1 + (size_t)(qbase + q) * 64;
           const int sw = (qbase + q) & 1;
-          tile_group<WT, M1>(acc, ra, ra + 8 * g1.pitch, hg + (((2 * tq) ^ sw) << 3),
+          tile_group<WT, M1>(acc0, acc1, ra, ra + 8 * g1.pitch, hg + (((2 * tq) ^ sw) << 3),
                              hg + (((2 * tq + 1) ^ sw) << 3));
         } else {
           const M1 *hg = hrow1 + (size_t)(qbase + q) * 32 + tq * 8;
-          tile_group<WT, M1>(acc, ra, ra + 8 * g1.pitch, hg, hg);
+          tile_group<WT, M1>(acc0, acc1, ra, ra + 8 * g1.pitch, hg, hg);
         }
-      }
-      const bool last = dc == g1.ndc - 1;
-      if (last) {
-        // lane (g, t): row g (and g + 8) against hidden row t in c[odd] (c[2 + odd])
-        const int par = tile & 1;
-        if (tq < R) {
-          S.part[par][warp][gq][tq] = acc[odd];
-          S.part[par][warp][gq + 8][tq] = acc[2 + odd];
-        }
-        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
       }
       FH_TICK(1);
-      __syncthreads();
-      FH_TICK(2);
-      if (tid == 0 && c + g1.n_slots < n1) issue1(c + g1.n_slots);
-      if (last && tid < kTileRows * kFWarps) {
-        // tile reduction: thread = (row, warp); a 16-lane shuffle tree per row
-        const int row = tid >> 4, w = tid & 15, par = tile & 1;
+      if (dc == g1.ndc - 1) {
+        // lane (g, t): row g (and g + 8) against hidden row t in c[odd] (c[2 + odd])
+        const int par = tile & 1;
+        if (tile >= 2) nbar_sync(kBarPart0 + par, kFBlock);
+        if (tq < R) {
+          S.part[par][gq][tq][warp] = acc0[odd] + acc1[odd];
+          S.part[par][gq + 8][tq][warp] = acc0[2 + odd] + acc1[2 + odd];
+        }
 #pragma unroll
-        for (int col = 0; col < R; ++col) {
-          float v = S.part[par][w][row][col];
-          v += __shfl_xor_sync(0xFFFFFFFFu, v, 8);
-          v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
-          v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
-          v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
-          if (w == 0 && row < tr && col < a.rows) {
+        for (int u = 0; u < 4; ++u) acc0[u] = acc1[u] = 0.f;
+      }
+      FH_TICK(2);
+      nbar_arrive(kBarSlot0 + s, kFBlock);
+    }
+    for (int t = max(ntile1 - 2, 0); t < ntile1; ++t) nbar_sync(kBarPart0 + (t & 1), kFBlock);
+  } else {
+    // Producer warp: refill each slot once it is consumed; reduce each
+    // finished tile over the 16 warps, then score it into the histograms.
+    for (int c = 0; c < n1; ++c) {
+      const int s = c % g1.n_slots, tile = c / g1.ndc, dc = c - tile * g1.ndc;
+      nbar_sync(kBarSlot0 + s, kFBlock);
+      if (lane == 0 && c + g1.n_slots < n1) issue1(c + g1.n_slots);
+      if (dc == g1.ndc - 1) {
+        const int par = tile & 1, tr = min(kTileRows, nc - tile * kTileRows);
+        for (int qd = lane; qd < kTileRows * R; qd += 32) {
+          const int row = qd & (kTileRows - 1), col = qd / kTileRows;
+          const float4 *pp = reinterpret_cast<const float4 *>(&S.part[par][row][col][0]);
+          const float4 x0 = pp[0], x1 = pp[1], x2 = pp[2], x3 = pp[3];
+          const float v = ((x0.x + x0.y) + (x0.z + x0.w)) + ((x1.x + x1.y) + (x1.z + x1.w)) +
+                          (((x2.x + x2.y) + (x2.z + x2.w)) + ((x3.x + x3.y) + (x3.z + x3.w)));
+          if (row < tr && col < a.rows) {
             const int k = c0 + tile * kTileRows + row;
             float sc = v * S.scale[k - c0];
             if (a.do_sample)
               sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)col, (uint32_t)k);
             S.local[col][k - c0] = sc;
-            a.scores[(size_t)col * a.K + k] = sc;
+            a.scores[(size_t)col * a.score_stride + k] = sc;
             const uint32_t key = mono(sanitize(sc));
             atomicAdd(&hist_cur[(size_t)col * kHistWords + kHistCoarse + (key >> 16)], 1u);
             atomicAdd(&S.coarse[col * kHistCoarse + (key >> 24)], 1u);
           }
         }
+        __syncwarp();
+        nbar_arrive(kBarPart0 + par, kFBlock);
       }
-      FH_TICK(3);
     }
   }
   __syncthreads();
   FH_STAMP(7);
-  for (int i = tid; i < a.rows * kHistCoarse; i += kFThreads) {
+  for (int i = tid; i < a.rows * kHistCoarse; i += kFBlock) {
     const uint32_t cc = S.coarse[i];
     if (cc) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], cc);
-  }
-  // Speculative L2 prefetch of stage-2 rows. HBM would sit idle through the
-  // barrier and the threshold search, so each CTA pulls the w_perm rows of
-  // its clusters that are likely to be selected: score above its own
-  // mean + z * std, where z is the normal quantile of the selection rate
-  // minus a margin. A wrong guess only costs bandwidth that was idle.
-  if (!a.do_sample && warp < a.rows && nc > 1) {
-    float sum = 0.f, sq = 0.f;
-    for (int i = lane; i < nc; i += 32) {
-      const float v = S.local[warp][i];
-      if (isfinite(v)) {
-        sum += v;
-        sq += v * v;
-      }
-    }
-    sum = warp_sum(sum);
-    sq = warp_sum(sq);
-    const float mean = sum / nc;
-    const float sd = sqrtf(fmaxf(sq / nc - mean * mean, 0.f));
-    const float frac = fminf(0.5f, (float)a.p / (float)a.K);
-    const float z = -normcdfinvf(frac) - 0.25f;
-    const float t_est = mean + z * sd;
-    const size_t cluster_bytes = (size_t)a.cap * a.D * sizeof(HT);
-    for (int i = lane; i < nc; i += 32)
-      if (S.local[warp][i] > t_est && cluster_bytes % 16 == 0)
-        bulk_prefetch_l2(reinterpret_cast<const char *>(a.w_perm) + (size_t)(c0 + i) * cluster_bytes,
-                         (uint32_t)cluster_bytes);
   }
   __syncthreads();
   FH_STAMP(1);
@@ -519,6 +551,37 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     __threadfence();
     FH_STAMP(8);
     atomicAdd(&a.sync[kSyncArrive], 1u);
+  }
+  // Speculative L2 prefetch of stage-2 rows while the grid meets. HBM would
+  // sit idle through the barrier and the selection, so the producer warp
+  // pulls the w_perm rows of this CTA's clusters that are likely to be
+  // selected: score above its own mean + z * std, where z is the normal
+  // quantile of the selection rate minus a margin. A wrong guess only costs
+  // bandwidth that was idle.
+  if (producer && !a.do_sample && nc > 1) {
+    const size_t cluster_bytes = (size_t)a.cap * a.D * sizeof(HT);
+    for (int r = 0; r < a.rows; ++r) {
+      float sum = 0.f, sq = 0.f;
+      for (int i = lane; i < nc; i += 32) {
+        const float v = S.local[r][i];
+        if (isfinite(v)) {
+          sum += v;
+          sq += v * v;
+        }
+      }
+      sum = warp_sum(sum);
+      sq = warp_sum(sq);
+      const float mean = sum / nc;
+      const float sd = sqrtf(fmaxf(sq / nc - mean * mean, 0.f));
+      const float frac = fminf(0.5f, (float)a.p / (float)a.K);
+      const float t_est = mean + (-normcdfinvf(frac) - 0.25f) * sd;
+      for (int i = lane; i < nc; i += 32)
+        if (S.local[r][i] > t_est && cluster_bytes % 16 == 0)
+          bulk_prefetch_l2(reinterpret_cast<const char *>(a.w_perm) + (size_t)(c0 + i) * cluster_bytes,
+                           (uint32_t)cluster_bytes);
+    }
+  }
+  if (tid == 0) {
     const uint32_t target = (uint32_t)(G + a.extra_arrivals);
     uint32_t polls = 0;
     while (ld_acquire_gpu(&a.sync[kSyncArrive]) < target) {
@@ -532,12 +595,33 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   __syncthreads();
   FH_STAMP(2);
 
-  // --------------------------------------------- thresholds: warp r, row r
-  if (warp < a.rows) {
+  // ---------------------------------------------------------------- select
+  // Warps kFMaxRows.. of the compute warps copy the score rows into the ring
+  // (stage 1 is done with it) while warp r finds row r's threshold bucket.
+  float *sc_s = reinterpret_cast<float *>(ring);  // [rows][Kp]
+  const int Kp = (a.K + 3) & ~3;
+  if (warp >= kFMaxRows && !producer) {
+    const int nv = a.rows * (Kp / 4), t0 = tid - kFMaxRows * 32;
+    constexpr int nt = kFThreads - kFMaxRows * 32;
+    for (int i = t0; i < nv; i += 4 * nt) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = i + u * nt;
+        if (j < nv) {
+          const int r = j / (Kp / 4), cc = j - r * (Kp / 4);
+          v[u] = __ldcg(reinterpret_cast<const float4 *>(a.scores + (size_t)r * a.score_stride) + cc);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i + u * nt < nv) reinterpret_cast<float4 *>(sc_s)[i + u * nt] = v[u];
+    }
+  } else if (warp < a.rows) {
     const uint32_t *h = hist_cur + (size_t)warp * kHistWords;
     int cb, above1, cnt1, fb, above2, cnt2;
-    warp_find_bin(h, a.p, cb, above1, cnt1);
-    warp_find_bin(h + kHistCoarse + cb * 256, a.p - above1, fb, above2, cnt2);
+    warp_find_bin<true>(h, a.p, cb, above1, cnt1);
+    warp_find_bin<true>(h + kHistCoarse + cb * 256, a.p - above1, fb, above2, cnt2);
     if (lane == 0) {
       S.thr[warp].prefix = (uint32_t)(cb * 256 + fb);
       S.thr[warp].need = a.p - above1 - above2;
@@ -546,37 +630,202 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   }
   __syncthreads();
   FH_STAMP(9);
-  // Zero this CTA's share of the buffers the next call will use.
-  {
-    const size_t n4 = kEpochBufBytes / 16;
-    uint4 *z = reinterpret_cast<uint4 *>(buf_nxt);
-    for (size_t i = (size_t)b * n4 / G + tid; i < (size_t)(b + 1) * n4 / G; i += kFThreads)
-      z[i] = make_uint4(0, 0, 0, 0);
-  }
-
-  // ------------- own clusters above the bucket -> work list; bucket -> ties
-  for (int i = tid; i < a.rows * nc; i += kFThreads) {
-    const int hr = i / nc, k = i - (i / nc) * nc;
-    const float v = sanitize(S.local[hr][k]);
-    const uint32_t pre = mono(v) >> 16;
-    const uint32_t P = S.thr[hr].prefix;
-    if (pre > P) {
-      const int w = atomicAdd(&S.n_work, 1);
-      if (w < kWorkCap) S.work[w] = ((uint32_t)hr << 28) | (uint32_t)(c0 + k);
-    } else if (pre == P) {
-      atomicAdd(&S.bucket_keys[hr], 1);
-      if (S.thr[hr].cnt <= kTieCap) {
-        const uint32_t t = atomicAdd(&a.sync[kSyncTieCount + hr], 1u);
-        if (t < (uint32_t)kTieCap) ties[(size_t)hr * kTieCap + t] = pack(v, (uint32_t)(c0 + k));
+  // Pass A, 128-cluster chunks over the compute warps: keys above the
+  // threshold bucket per chunk, and the bucket's keys (when any is needed).
+  const int nch = (a.K + 127) >> 7;
+  if (!producer) {
+    for (int r = 0; r < a.rows; ++r) {
+      const uint32_t P = S.thr[r].prefix;
+      const uint32_t thrA = P >= 0xFFFFu ? 0xFFFFFFFFu : (P + 1u) << 16;
+      const uint32_t bktLo = P << 16;
+      const bool want = S.thr[r].need > 0;
+      const float4 *row4 = reinterpret_cast<const float4 *>(sc_s + r * Kp);
+      for (int ch = warp; ch < nch; ch += kFWarps) {
+        const int k0 = (ch << 7) + 4 * lane;
+        int above = 0;
+        uint32_t inb = 0u;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (k0 < a.K) {
+          const float4 v4 = row4[k0 >> 2];
+          v[0] = v4.x;
+          v[1] = v4.y;
+          v[2] = v4.z;
+          v[3] = v4.w;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t m = mono(sanitize(v[u]));
+            const bool ok = k0 + u < a.K;
+            above += ok && m >= thrA;
+            inb |= (uint32_t)(ok && m - bktLo < 65536u) << u;
+          }
+        }
+        above = __reduce_add_sync(0xFFFFFFFFu, above);
+        if (lane == 0) S.chunk_sel[r][ch] = above;
+        if (want && __any_sync(0xFFFFFFFFu, inb != 0u)) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if ((inb >> u) & 1u) {
+              const int m = atomicAdd(&S.bkt_n[r], 1);
+              if (m < kBktCap) S.bkt[r][m] = pack(sanitize(v[u]), (uint32_t)(k0 + u));
+            }
+        }
       }
     }
   }
-  // special tokens of row b are scored by CTA b
-  if (b < a.rows)
-    for (int t = tid; t < a.n_special; t += kFThreads) {
-      const int w = atomicAdd(&S.n_work, 1);
-      if (w < kWorkCap) S.work[w] = kItemSpecial | ((uint32_t)b << 28) | (uint32_t)t;
+  __syncthreads();
+  FH_STAMP(12);
+  // Threshold key of row r: keys above the bucket, plus the `need` largest
+  // keys of the bucket. Small buckets: the key of rank need - 1 (warp r).
+  if (warp < a.rows) {
+    const RowThreshold t = S.thr[warp];
+    const int n = S.bkt_n[warp];
+    unsigned long long T = t.prefix >= 0xFFFFu ? ~0ull : (unsigned long long)(t.prefix + 1u) << 48;
+    if (t.need > 0 && n <= kBktCap) {
+      T = (unsigned long long)t.prefix << 48;  // fewer keys than needed: take the whole bucket
+      for (int j = lane; j < n; j += 32) {
+        const unsigned long long mine = S.bkt[warp][j];
+        int rank = 0;
+        for (int m = 0; m < n; ++m) rank += S.bkt[warp][m] > mine;
+        if (rank == t.need - 1) S.tkey[warp] = mine;
+      }
+      __syncwarp();
+      if (lane == 0 && t.need <= n) T = S.tkey[warp];
     }
+    __syncwarp();
+    if (lane == 0) S.tkey[warp] = T;
+  }
+  __syncthreads();
+  FH_STAMP(4);
+  // Large buckets: radix select of the need-th largest key, 8 bits per pass
+  // over the 48 key bits below the bucket prefix.
+  for (int r = 0; r < a.rows; ++r) {
+    if (S.thr[r].need <= 0 || S.bkt_n[r] <= kBktCap) continue;  // block-uniform
+    unsigned long long pre = (unsigned long long)S.thr[r].prefix << 48;
+    int need = S.thr[r].need;
+    for (int shift = 40; shift >= 0; shift -= 8) {
+      for (int i = tid; i < 256; i += kFBlock) S.rhist[i] = 0u;
+      __syncthreads();
+      const unsigned long long hi_sel = pre >> (shift + 8);
+      for (int k = tid; k < a.K; k += kFBlock) {
+        const unsigned long long key = pack(sanitize(sc_s[r * Kp + k]), (uint32_t)k);
+        if ((key >> (shift + 8)) == hi_sel) atomicAdd(&S.rhist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        int bin, above, cnt;
+        warp_find_bin<false>(S.rhist, need, bin, above, cnt);
+        if (lane == 0) {
+          S.rsel_bin = bin;
+          S.rsel_above = above;
+        }
+      }
+      __syncthreads();
+      pre |= (unsigned long long)S.rsel_bin << shift;
+      need -= S.rsel_above;
+      __syncthreads();  // rsel_* and rhist are reused by the next pass
+    }
+    if (tid == 0) S.tkey[r] = pre;
+    __syncthreads();
+  }
+  FH_STAMP(13);
+  // Selected keys (key >= tkey[r]) per chunk: the keys above the bucket plus
+  // the listed bucket winners, or a recount for a large bucket.
+  const int per_row = a.p + a.n_special;
+  const int total = a.rows * per_row;
+  const int lo = (int)((long long)b * total / G), hi = (int)((long long)(b + 1) * total / G);
+  const int n_items = min(hi - lo, kWorkCap);  // the host keeps hi - lo <= kWorkCap
+  for (int r = 0; r < a.rows; ++r) {
+    const unsigned long long T = S.tkey[r];
+    if (S.thr[r].need <= 0) continue;
+    if (S.bkt_n[r] <= kBktCap) {
+      for (int m = tid; m < S.bkt_n[r]; m += kFBlock) {
+        const unsigned long long key = S.bkt[r][m];
+        if (key >= T) atomicAdd(&S.chunk_sel[r][(int)(0xFFFFFFFFu - (uint32_t)key) >> 7], 1);
+      }
+    } else if (!producer) {
+      const float4 *row4 = reinterpret_cast<const float4 *>(sc_s + r * Kp);
+      for (int ch = warp; ch < nch; ch += kFWarps) {
+        const int k0 = (ch << 7) + 4 * lane;
+        int cnt = 0;
+        if (k0 < a.K) {
+          const float4 v4 = row4[k0 >> 2];
+          const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            cnt += k0 + u < a.K && pack(sanitize(v[u]), (uint32_t)(k0 + u)) >= T;
+        }
+        cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+        if (lane == 0) S.chunk_sel[r][ch] = cnt;
+      }
+    }
+  }
+  for (int i = tid; i < n_items; i += kFBlock) S.work[i] = 0xFFFFFFFFu;  // empty until set
+  if (tid == 0) S.n_work = n_items;
+  __syncthreads();
+  // Chunk offsets in id order (warp r, row r).
+  if (warp < a.rows) {
+    const int per = (nch + 31) / 32, j0 = min(nch, lane * per), j1 = min(nch, j0 + per);
+    int sum = 0;
+    for (int j = j0; j < j1; ++j) sum += S.chunk_sel[warp][j];
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    int off = incl - sum;
+    for (int j = j0; j < j1; ++j) {
+      S.chunk_off[warp][j] = off;
+      off += S.chunk_sel[warp][j];
+    }
+  }
+  __syncthreads();
+  FH_STAMP(14);
+  // This CTA's items: [lo, hi) of rows * (p + n_special), row-major; row r's
+  // selected clusters in id order, then its special tokens. Only the chunks
+  // whose positions meet the range are walked.
+  if (!producer) {
+    for (int r = 0; r < a.rows; ++r) {
+      const int base = r * per_row;
+      const unsigned long long T = S.tkey[r];
+      const float4 *row4 = reinterpret_cast<const float4 *>(sc_s + r * Kp);
+      for (int ch = warp; ch < nch; ch += kFWarps) {
+        const int off = S.chunk_off[r][ch], cnt = S.chunk_sel[r][ch];
+        if (cnt == 0 || base + off + cnt <= lo || base + off >= hi || off >= a.p) continue;
+        const int k0 = (ch << 7) + 4 * lane;
+        bool f[4] = {false, false, false, false};
+        if (k0 < a.K) {
+          const float4 v4 = row4[k0 >> 2];
+          const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            f[u] = k0 + u < a.K && pack(sanitize(v[u]), (uint32_t)(k0 + u)) >= T;
+        }
+        const int c = (int)f[0] + (int)f[1] + (int)f[2] + (int)f[3];
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        int pos = off + incl - c;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (f[u]) {
+            const int idx = base + pos;
+            if (pos < a.p && idx >= lo && idx - lo < n_items)
+              S.work[idx - lo] = ((uint32_t)r << 28) | (uint32_t)(k0 + u);
+            ++pos;
+          }
+        }
+      }
+      for (int j = tid; j < a.n_special; j += kFThreads) {
+        const int idx = base + a.p + j;
+        if (idx >= lo && idx - lo < n_items)
+          S.work[idx - lo] = kItemSpecial | ((uint32_t)r << 28) | (uint32_t)j;
+      }
+    }
+  }
   __syncthreads();
   FH_STAMP(10);
 
@@ -584,7 +833,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
   const int rb3 = a.D * (int)sizeof(HT);
   const RingGeom g3 = ring_geom(rb3);
   const char *wp = reinterpret_cast<const char *>(a.w_perm);
-  // Producer state (thread 0 only): next work item and its next d-chunk.
+  // Producer state (producer lane 0 only): next work item and its next d-chunk.
   int p_item = 0, p_dc = 0;
   auto produce = [&](int s) {
     S2Chunk d;
@@ -594,8 +843,7 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
     d.dc = 0;
     d.last = 1;
     d.vid_in_smem = 0;
-    const int nw = min(S.n_work, kWorkCap);
-    if (p_item < nw) {
+    if (p_item < S.n_work) {
       const uint32_t item = S.work[p_item];
       d.row = (int)((item >> 28) & 3u);
       const int payload = (int)(item & 0x00FFFFFFu);
@@ -636,67 +884,12 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       if (vid_bulk) bulk_g2s(&S.vid[s][0], vsrc, (uint32_t)(d.n * 4), &S.mbar[s]);
     } else {
       S.desc[s] = d;
-      mbar_expect_tx(&S.mbar[s], 0u);  // invalid row or end of work: no data
+      mbar_expect_tx(&S.mbar[s], 0u);  // invalid item or end of work: no data
     }
   };
-  // Start streaming the certain clusters, then settle this CTA's bucket keys;
-  // slots are only marked end-of-work once the work list is final. Chunk i of
-  // stage 2 uses slot i % n_slots.
-  int n_prod = 0;  // thread 0: next chunk to produce
-  if (tid == 0)
-    while (n_prod < g3.n_slots && p_item < min(S.n_work, kWorkCap)) produce(n_prod++ % g3.n_slots);
-  // Rank this CTA's bucket keys exactly, one warp per key, against the full
-  // bucket: the published tie list (complete once its count reaches the
-  // histogram's), or, for a bucket larger than the list, the scores row itself.
-  bool any_bucket = false;
-  for (int hr = 0; hr < a.rows; ++hr) any_bucket |= S.bucket_keys[hr] > 0;
-  if (any_bucket) {
-    if (tid == 0) {
-      for (int hr = 0; hr < a.rows; ++hr) {
-        if (S.bucket_keys[hr] == 0 || S.thr[hr].cnt > kTieCap) continue;
-        const uint32_t want = (uint32_t)S.thr[hr].cnt;
-        uint32_t polls = 0;
-        while (ld_acquire_gpu(&a.sync[kSyncTieCount + hr]) < want) {
-          if (++polls >= a.barrier_polls) {
-            atomicOr(&S.s_err, kErrTieTimeout);
-            break;
-          }
-        }
-      }
-      __threadfence();
-    }
-    __syncthreads();
-    for (int i = warp; i < a.rows * nc; i += kFWarps) {
-      const int hr = i / nc, k = i - (i / nc) * nc;
-      const float v = sanitize(S.local[hr][k]);
-      const uint32_t P = S.thr[hr].prefix;
-      if ((mono(v) >> 16) != P) continue;  // warp-uniform
-      const unsigned long long mine = pack(v, (uint32_t)(c0 + k));
-      const int cnt = S.thr[hr].cnt;
-      int rank = 0;
-      if (cnt <= kTieCap) {
-        for (int t = lane; t < cnt; t += 32) rank += __ldcg(&ties[(size_t)hr * kTieCap + t]) > mine;
-      } else {
-        for (int t = lane; t < a.K; t += 32) {
-          const float u = sanitize(__ldcg(&a.scores[(size_t)hr * a.K + t]));
-          rank += (mono(u) >> 16) == P && pack(u, (uint32_t)t) > mine;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) rank += __shfl_xor_sync(0xFFFFFFFFu, rank, o);
-      if (lane == 0 && rank < S.thr[hr].need) {
-        const int w = atomicAdd(&S.n_work, 1);
-        if (w < kWorkCap) S.work[w] = ((uint32_t)hr << 28) | (uint32_t)(c0 + k);
-      }
-    }
-  }
-  FH_STAMP(4);
-  __syncthreads();
-  if (tid == 0)
-    while (n_prod < g3.n_slots) produce(n_prod++ % g3.n_slots);
   FH_TICK(7);
-  {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (!producer) {
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
     int tile = 0;
     for (int c = 0;; ++c) {
       const int s = c % g3.n_slots;
@@ -715,42 +908,65 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
         for (int grp = warp; grp < ng; grp += kFWarps) {
           const int q = grp ^ odd;
           const unsigned char *ra = slot + (size_t)gq * g3.pitch + q * 64 + tq * 16;
-          tile_group<HT, HT>(acc, ra, ra + 8 * g3.pitch, hrow3 + q * 32, hrow3 + q * 32);
+          tile_group<HT, HT>(acc0, acc1, ra, ra + 8 * g3.pitch, hrow3 + q * 32, hrow3 + q * 32);
         }
       }
-      // vocab id of tile row tid >> 4, read before the slot is refilled
-      uint32_t vid = 0u;
-      if (d.last && d.src >= 0 && tid < kTileRows * kFWarps && (tid & 15) == 0 &&
-          (tid >> 4) < d.n)
-        vid = (uint32_t)(d.vid_in_smem ? S.vid[s][tid >> 4] : __ldg(&a.vocab_map[d.src + (tid >> 4)]));
+      FH_TICK(5);
       if (d.last) {
         // every B column pair holds hidden row d.row: lanes t == 0 carry rows g, g + 8
         const int par = tile & 1;
+        if (tile >= 2) nbar_sync(kBarPart0 + par, kFBlock);
         if (tq == 0) {
-          S.part[par][warp][gq][0] = acc[odd];
-          S.part[par][warp][gq + 8][0] = acc[2 + odd];
+          S.part[par][gq][0][warp] = acc0[odd] + acc1[odd];
+          S.part[par][gq + 8][0][warp] = acc0[2 + odd] + acc1[2 + odd];
         }
-        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc0[u] = acc1[u] = 0.f;
+        ++tile;
       }
-      FH_TICK(5);
-      __syncthreads();  // slot s is free; partials of a finished tile are visible
-      if (tid == 0) produce(n_prod++ % g3.n_slots);
-      if (d.last && d.src >= 0 && tid < kTileRows * kFWarps) {
-        const int row = tid >> 4, w = tid & 15, par = tile & 1;
-        float v = S.part[par][w][row][0];
-        v += __shfl_xor_sync(0xFFFFFFFFu, v, 8);
-        v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
-        v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
-        v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
-        if (w == 0 && row < d.n) {
-          float key = v;
-          if (a.do_sample)
-            key = v / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)d.row, vid);
-          atomicMax(&S.best[d.row], pack(key, vid));
-        }
-      }
-      if (d.last) ++tile;
       FH_TICK(6);
+      nbar_arrive(kBarSlot0 + s, kFBlock);
+    }
+    for (int t = max(tile - 2, 0); t < tile; ++t) nbar_sync(kBarPart0 + (t & 1), kFBlock);
+  } else {
+    int n_prod = 0;  // lane 0: next chunk to produce (chunk i uses slot i % n_slots)
+    if (lane == 0)
+      while (n_prod < g3.n_slots) produce(n_prod++ % g3.n_slots);
+    __syncwarp();
+    int tile = 0;
+    for (int c = 0;; ++c) {
+      const int s = c % g3.n_slots;
+      const S2Chunk d = S.desc[s];
+      if (d.src == -2) break;
+      nbar_sync(kBarSlot0 + s, kFBlock);
+      if (d.last) {
+        const int par = tile & 1;
+        if (d.src >= 0) {
+          unsigned long long best = 0ull;
+          if (lane < kTileRows) {
+            const int row = lane;
+            const float4 *pp = reinterpret_cast<const float4 *>(&S.part[par][row][0][0]);
+            const float4 x0 = pp[0], x1 = pp[1], x2 = pp[2], x3 = pp[3];
+            const float v = ((x0.x + x0.y) + (x0.z + x0.w)) + ((x1.x + x1.y) + (x1.z + x1.w)) +
+                            (((x2.x + x2.y) + (x2.z + x2.w)) + ((x3.x + x3.y) + (x3.z + x3.w)));
+            if (row < d.n) {
+              const uint32_t vid =
+                  (uint32_t)(d.vid_in_smem ? S.vid[s][row] : __ldg(&a.vocab_map[d.src + row]));
+              float key = v;
+              if (a.do_sample)
+                key = v / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)d.row, vid);
+              best = pack(key, vid);
+            }
+          }
+          best = warp_max_u64(best);
+          if (lane == 0 && best > S.best[d.row]) S.best[d.row] = best;
+        }
+        __syncwarp();
+        nbar_arrive(kBarPart0 + par, kFBlock);
+        ++tile;
+      }
+      if (lane == 0) produce(n_prod++ % g3.n_slots);
+      __syncwarp();
     }
   }
   FH_TICK_FLUSH();
@@ -773,7 +989,6 @@ __global__ void __launch_bounds__(kFThreads, 1) k_fused_step(FusedArgs a) {
       const unsigned long long wv = atomicExch(&a.packed[tid], 0ull);
       a.out_ids[tid] = wv ? (int64_t)packed_id(wv) : (int64_t)0xFFFFFFFFll;
     }
-    if (tid < kFMaxRows) a.sync[kSyncTieCount + tid] = 0u;
     if (tid == 0) {
       a.sync[kSyncArrive] = 0u;
       a.sync[kSyncDone] = 0u;

@@ -43,9 +43,9 @@ int cuda_fail(cudaError_t e, const char *what) {
     if (_e != cudaSuccess) return cuda_fail(_e, what); \
   } while (0)
 
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <typename Kern, typename... Args>
 cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
@@ -120,7 +120,7 @@ cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(fh::kFThreads);
+  cfg.blockDim = dim3(fh::kFBlock);
   cfg.dynamicSmemBytes = fh::fused_smem_bytes(R, a.D, (int)sizeof(WT));
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -357,6 +357,12 @@ bool fused_ok(const fh_head_desc &d, int rows, bool sample, int grid) {
   if (d.n_clusters > 128 * grid || d.n_clusters > fh::kSelMaxItems) return false;
   if (d.n_probes > fh::kFMaxProbes || d.cluster_size > fh::kS3MaxRows) return false;
   if (d.n_special > fh::kFMaxSpecial || d.n_clusters >= (1 << 24)) return false;
+  if ((d.n_clusters + 127) / 128 > fh::kMaxChunks) return false;
+  // every CTA holds the score rows in its 128 KB ring; items per CTA fit its work list
+  if ((size_t)rows * round_up((size_t)d.n_clusters, 4) * sizeof(float) > (size_t)fh::kRingBytes)
+    return false;
+  if ((long long)rows * (d.n_probes + d.n_special) > (long long)(fh::kWorkCap - 1) * grid)
+    return false;
   return true;
 }
 
@@ -382,6 +388,7 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
   a.temperature = temperature;
   a.rng = rng_key(seed, offset);
   a.scores = w.scores;
+  a.score_stride = w.score_stride;
   a.sync = reinterpret_cast<uint32_t *>(w.counter);
   a.epoch_bufs = w.epoch_bufs;
   a.packed = w.packed;
@@ -484,7 +491,7 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   const int grid = sm_count();
-  if (fused_ok(head->d, rows, false, grid))
+  if (fused_ok(head->d, rows, false, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, grid, s);
   st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
   if (st != FH_OK) return st;
@@ -514,7 +521,7 @@ FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   const int grid = sm_count();
-  if (fused_ok(head->d, rows, true, grid))
+  if (fused_ok(head->d, rows, true, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, true, temperature, seed, offset, out_ids, w, grid, s);
   st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
                   nullptr, 0, s);

@@ -116,7 +116,7 @@ def test_valid_descriptor_and_workspace_size(lib):
         def rnd(x):
             return (x + 255) // 256 * 256
         for rows in (1, 8, 256):
-            hist = 2 * (4 * (256 + 65536) * 4 + 4 * 1024 * 8)
+            hist = 2 * 4 * (256 + 65536) * 4  # two epochs of 4 rows' histograms
             want = 256 + hist + rnd(rows * 8) + rnd(rows * 256 * 4) + rnd(rows * 8064 * 4) + 256
             assert lib.fh_workspace_bytes(h, rows) == want
         assert lib.fh_workspace_bytes(None, 1) == 0
