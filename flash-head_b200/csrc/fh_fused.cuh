@@ -49,6 +49,7 @@ constexpr int kFBlock = kFThreads + 32;    // + one producer / reducer warp
 constexpr int kBarSlot0 = 1;  // 1..4: slot s consumed (and a finished tile's partials written)
 constexpr int kBarPart0 = 5;  // 5..6: partial buffer (tile & 1) reduced, free again
 constexpr int kMaxChunks = 160;  // 128-cluster chunks of a score row
+constexpr int kMaxS1Chunks = 8;  // stage-1 chunks of one CTA (each with its own partials)
 constexpr int kRingBytes = 128 * 1024;
 constexpr int kMaxSlots = 4;
 constexpr int kTileRows = 16;
@@ -103,6 +104,7 @@ struct FusedArgs {
   uint32_t barrier_polls;      // grid-barrier poll limit
   uint32_t copy_polls;         // mbarrier poll limit
   int extra_arrivals;          // >0 only in the timeout test: wait for more CTAs than exist
+  unsigned long long *trace;   // profiling builds only: phase stamps (else null)
 };
 
 struct RowThreshold {
@@ -131,6 +133,7 @@ struct FusedSmem {
   __align__(16) int vid[kMaxSlots][kTileRows];
   S2Chunk desc[kMaxSlots];
   RowThreshold thr[kFMaxRows];
+  float t_est[kFMaxRows];                      // estimated selection threshold per row
   unsigned long long best[kFMaxRows];
   unsigned long long tkey[kFMaxRows];          // selection: key >= tkey[r]
   unsigned long long bkt[kFMaxRows][kBktCap];  // keys of row r's threshold bucket
@@ -143,16 +146,22 @@ struct FusedSmem {
   int n_work;
   uint32_t s_err;
   uint32_t s_last;
+#ifdef FH_TRACE
+  long long trace_clk[24];
+#endif
 };
 
 constexpr size_t kFSmemBase = (kRingBytes + sizeof(FusedSmem) + 127) / 128 * 128;
 constexpr size_t kFSmemMax = 226 * 1024;
 
-// Dynamic shared memory of k_fused_step: ring, FusedSmem, the hidden rows as
-// stage-2 B operands [R][D] (16-bit) and, for fp8 stage-1 rows, as f16
-// stage-1 B operands [R][D].
+// Dynamic shared memory of k_fused_step: ring, FusedSmem, stage-1 partials
+// [kMaxS1Chunks][16 rows][R][16 warps], the hidden rows as stage-2 B operands
+// [R][D] (16-bit) and, for fp8 stage-1 rows, as f16 stage-1 B operands [R][D].
+__host__ __device__ __forceinline__ size_t s1_part_bytes(int R) {
+  return (size_t)kMaxS1Chunks * kTileRows * R * kFWarps * sizeof(float);
+}
 __host__ __device__ __forceinline__ size_t fused_smem_bytes(int R, int D, int wt_bytes) {
-  return kFSmemBase + (size_t)R * D * 2 * (wt_bytes == 1 ? 2 : 1);
+  return kFSmemBase + s1_part_bytes(R) + (size_t)R * D * 2 * (wt_bytes == 1 ? 2 : 1);
 }
 
 // Ring geometry of one stage for rows of rb bytes: slots of 32 KB when a
@@ -238,12 +247,11 @@ __device__ __forceinline__ int fp8_hidden_slot(int e) {
 // (shared memory), hidden slice at h0 (and h1 for fp8: the second granule).
 // Even k-steps accumulate into c0, odd ones into c1 (two independent chains).
 template <typename WT, typename MT>
-__device__ __forceinline__ void tile_group(float *c0, float *c1, const unsigned char *ra,
-                                           const unsigned char *rb, const MT *h0,
-                                           const MT *h1) {
+__device__ __forceinline__ void tile_group_h(float *c0, float *c1, const unsigned char *ra,
+                                             const unsigned char *rb, const uint4 x0,
+                                             const uint4 x1) {
   const uint4 a0 = lds128(ra), b0 = lds128(rb);
   if constexpr (sizeof(WT) == 1) {
-    const uint4 x0 = lds128(h0), x1 = lds128(h1);
     const uint32_t wa[4] = {a0.x, a0.y, a0.z, a0.w}, wb[4] = {b0.x, b0.y, b0.z, b0.w};
     const uint32_t hh[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
@@ -254,7 +262,6 @@ __device__ __forceinline__ void tile_group(float *c0, float *c1, const unsigned 
       mma16816<MT>((j & 1) ? c1 : c0, a, b);
     }
   } else {
-    const uint4 x0 = lds128(h0);
     {
       const uint32_t a[4] = {a0.x, b0.x, a0.y, b0.y};
       const uint32_t b[2] = {x0.x, x0.y};
@@ -266,6 +273,14 @@ __device__ __forceinline__ void tile_group(float *c0, float *c1, const unsigned 
       mma16816<MT>(c1, a, b);
     }
   }
+}
+template <typename WT, typename MT>
+__device__ __forceinline__ void tile_group(float *c0, float *c1, const unsigned char *ra,
+                                           const unsigned char *rb, const MT *h0,
+                                           const MT *h1) {
+  const uint4 x0 = lds128(h0);
+  const uint4 x1 = sizeof(WT) == 1 ? lds128(h1) : x0;
+  tile_group_h<WT, MT>(c0, c1, ra, rb, x0, x1);
 }
 
 // Named barriers (warp-aligned: every lane of a warp calls them together).
@@ -290,42 +305,65 @@ __device__ __forceinline__ __nv_bfloat16 f2t<__nv_bfloat16>(float x) {
 }
 
 #ifdef FH_TRACE
-// Profiling builds only: per-CTA %globaltimer stamps at phase boundaries.
-__device__ unsigned long long *g_fh_trace;
-__device__ __forceinline__ void trace_stamp(int phase) {
-  if (threadIdx.x == 0 && g_fh_trace) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g_fh_trace[blockIdx.x * 24 + phase] = t;
-  }
-}
-#define FH_STAMP(p) trace_stamp(p)
-#define FH_STAMP_P(p) do { if (threadIdx.x == kFThreads && g_fh_trace) { unsigned long long _t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(_t)); g_fh_trace[blockIdx.x * 24 + (p)] = _t; } } while (0)
-// clock64 accumulators (thread 0): tick() returns cycles since the last tick
+// Profiling builds only. Phase stamps are clock64 values kept in shared
+// memory (thread 0, or producer lane 0 for FH_STAMP_P) and written out at the
+// end of the kernel as %globaltimer-aligned nanoseconds at 1965 MHz into
+// a.trace[b * 24 + p]; thread 0's clock64 accumulators go to
+// a.trace[G * 24 + b * 8 + k]. Nothing is stored to global memory before.
+#define FH_STAMP_AT(p, who)                                              \
+  do {                                                                   \
+    if (threadIdx.x == (who) && a.trace) S.trace_clk[p] = clock64();     \
+  } while (0)
+#define FH_STAMP(p) FH_STAMP_AT(p, 0)
+#define FH_STAMP_P(p) FH_STAMP_AT(p, kFThreads)
 #define FH_TICK_DECL long long fh_t0 = clock64(); long long fh_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #define FH_TICK(k) do { const long long _t = clock64(); fh_acc[k] += _t - fh_t0; fh_t0 = _t; } while (0)
-#define FH_TICK_FLUSH() do { if (threadIdx.x == 0 && g_fh_trace) for (int _k = 0; _k < 8; ++_k) g_fh_trace[gridDim.x * 24 + blockIdx.x * 8 + _k] = fh_acc[_k]; } while (0)
+#define FH_TICK_FLUSH() do { if (threadIdx.x == 0 && a.trace) for (int _k = 0; _k < 8; ++_k) a.trace[gridDim.x * 24 + blockIdx.x * 8 + _k] = fh_acc[_k]; } while (0)
+#define FH_TRACE_INIT()                                                  \
+  long long fh_clk0 = 0;                                                 \
+  unsigned long long fh_gt0 = 0;                                         \
+  if (threadIdx.x == 0) {                                                \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(fh_gt0));           \
+    fh_clk0 = clock64();                                                 \
+  }                                                                      \
+  for (int _i = threadIdx.x; _i < 24; _i += blockDim.x) S.trace_clk[_i] = 0;
+#define FH_TRACE_WRITE()                                                 \
+  do {                                                                   \
+    __syncthreads();                                                     \
+    if (threadIdx.x == 0 && a.trace)                                     \
+      for (int _p = 0; _p < 24; ++_p)                                    \
+        a.trace[blockIdx.x * 24 + _p] =                                  \
+            S.trace_clk[_p] ? fh_gt0 + (S.trace_clk[_p] - fh_clk0) * 1000 / 1965 : 0; \
+  } while (0)
 #else
 #define FH_STAMP(p) ((void)0)
 #define FH_STAMP_P(p) ((void)0)
 #define FH_TICK_DECL
 #define FH_TICK(k) ((void)0)
 #define FH_TICK_FLUSH() ((void)0)
+#define FH_TRACE_INIT()
+#define FH_TRACE_WRITE() ((void)0)
 #endif
 
 
 // Warp-level search of a 256-bin histogram (highest bin first) for the bin
 // holding the need-th largest key: returns the bin, the count above it and
 // the bin's count (all lanes).
+__device__ __forceinline__ void warp_find_bin_regs(const uint4 lo, const uint4 hi, int need,
+                                                   int &bin, int &above, int &cnt);
+// lane l owns bins 255-8l .. 248-8l (descending): bins + 248 - 8l (lo), + 252 - 8l (hi)
 template <bool kGlobal>
 __device__ __forceinline__ void warp_find_bin(const uint32_t *bins, int need, int &bin,
                                               int &above, int &cnt) {
   const int lane = threadIdx.x & 31;
-  // lane l owns bins 255-8l .. 248-8l (descending)
   const uint4 *plo = reinterpret_cast<const uint4 *>(bins + 248 - 8 * lane);
   const uint4 *phi = reinterpret_cast<const uint4 *>(bins + 252 - 8 * lane);
-  const uint4 lo = kGlobal ? __ldcg(plo) : *plo;
-  const uint4 hi = kGlobal ? __ldcg(phi) : *phi;
+  warp_find_bin_regs(kGlobal ? __ldcg(plo) : *plo, kGlobal ? __ldcg(phi) : *phi, need, bin, above,
+                     cnt);
+}
+__device__ __forceinline__ void warp_find_bin_regs(const uint4 lo, const uint4 hi, int need,
+                                                   int &bin, int &above, int &cnt) {
+  const int lane = threadIdx.x & 31;
   const uint32_t c[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
   int mine = 0;
 #pragma unroll
@@ -362,6 +400,50 @@ __device__ __forceinline__ void warp_find_bin(const uint32_t *bins, int need, in
   cnt = cn;
 }
 
+// Threshold bucket of one row (the 16-bit key prefix holding the p-th largest
+// key) from its two-level histogram: the coarse level and the fine levels of
+// the three coarse bins around `guess` are read in one round trip; a guess
+// that misses costs a second read.
+__device__ __forceinline__ RowThreshold warp_find_bucket(const uint32_t *h, int p, int guess) {
+  const int lane = threadIdx.x & 31;
+  const int o_lo = 248 - 8 * lane, o_hi = 252 - 8 * lane;
+  auto ld = [](const uint32_t *q) { return __ldcg(reinterpret_cast<const uint4 *>(q)); };
+  const int g0 = min(max(guess - 1, 0), kHistCoarse - 3);
+  const uint32_t *f = h + kHistCoarse + g0 * 256;
+  const uint4 clo = ld(h + o_lo), chi = ld(h + o_hi);
+  const uint4 f0l = ld(f + o_lo), f0h = ld(f + o_hi);
+  const uint4 f1l = ld(f + 256 + o_lo), f1h = ld(f + 256 + o_hi);
+  const uint4 f2l = ld(f + 512 + o_lo), f2h = ld(f + 512 + o_hi);
+  int cb, above1, cnt1;
+  warp_find_bin_regs(clo, chi, p, cb, above1, cnt1);
+  uint4 fl, fh;
+  const int j = cb - g0;  // warp-uniform
+  if (j == 0) {
+    fl = f0l;
+    fh = f0h;
+  } else if (j == 1) {
+    fl = f1l;
+    fh = f1h;
+  } else if (j == 2) {
+    fl = f2l;
+    fh = f2h;
+  } else {
+    fl = ld(h + kHistCoarse + cb * 256 + o_lo);
+    fh = ld(h + kHistCoarse + cb * 256 + o_hi);
+  }
+  int fb, above2, cnt2;
+  warp_find_bin_regs(fl, fh, p - above1, fb, above2, cnt2);
+  RowThreshold t;
+  t.prefix = (uint32_t)(cb * 256 + fb);
+  t.need = p - above1 - above2;
+  t.cnt = cnt2;
+  return t;
+}
+
+__device__ __forceinline__ const char *wp_bytes(const FusedArgs &a) {
+  return reinterpret_cast<const char *>(a.w_perm);
+}
+
 template <typename HT, typename WT, int R>
 __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   using M1 = typename S1Mma<WT>::T;  // stage-1 mma operand type
@@ -369,9 +451,10 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char *ring = smem;
   FusedSmem &S = *reinterpret_cast<FusedSmem *>(smem + kRingBytes);
-  HT *hB3 = reinterpret_cast<HT *>(smem + kFSmemBase);  // [R][D] stage-2 B operand
+  float *part1 = reinterpret_cast<float *>(smem + kFSmemBase);  // stage-1 partials
+  HT *hB3 = reinterpret_cast<HT *>(smem + kFSmemBase + s1_part_bytes(R));  // [R][D]
   // stage-1 B operand: a swizzled f16 copy for fp8 rows, else the same array
-  M1 *hB1 = kFp8 ? reinterpret_cast<M1 *>(smem + kFSmemBase + (size_t)R * a.D * 2)
+  M1 *hB1 = kFp8 ? reinterpret_cast<M1 *>(reinterpret_cast<unsigned char *>(hB3) + (size_t)R * a.D * 2)
                  : reinterpret_cast<M1 *>(hB3);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -379,6 +462,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   const int G = gridDim.x, b = blockIdx.x;
   const int gq = lane >> 2, tq = lane & 3, odd = gq & 1;  // mma fragment coordinates
   uint32_t phase = 0u;  // compute warps: parity of each slot's next mbarrier completion
+  FH_TRACE_INIT()
   if (tid == 0) {
     for (int s = 0; s < kMaxSlots; ++s) mbar_init(&S.mbar[s], 1);
     fence_mbar_init();
@@ -399,8 +483,18 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   uint32_t *hist_cur = reinterpret_cast<uint32_t *>(buf_cur);
 
   // ------------------------------------------------------------------ stage 1
-  const int c0 = (int)((long long)b * a.K / G), c1 = (int)((long long)(b + 1) * a.K / G);
+  // slice bounds in 32 bits: the host keeps K <= 128 * G, so b * K < 2^32
+  const int c0 = (int)((uint32_t)b * (uint32_t)a.K / (uint32_t)G);
+  const int c1 = (int)((uint32_t)(b + 1) * (uint32_t)a.K / (uint32_t)G);
   const int nc = c1 - c0;
+  // This CTA's stage-2 items: [lo, hi) of rows * (p + n_special), row-major;
+  // row r's selected clusters in id order, then its special tokens.
+  const int per_row = a.p + a.n_special;
+  const int total = a.rows * per_row;
+  // 32-bit bounds: total <= 4 * (4096 + 256) and G <= 1024
+  const int lo = (int)((uint32_t)b * (uint32_t)total / (uint32_t)G);
+  const int hi = (int)((uint32_t)(b + 1) * (uint32_t)total / (uint32_t)G);
+  const int n_items = min(hi - lo, kWorkCap);  // the host keeps hi - lo <= kWorkCap
   const int rb1 = a.D * (int)sizeof(WT);  // bytes per centroid row
   const RingGeom g1 = ring_geom(rb1);
   const int ntile1 = (nc + kTileRows - 1) / kTileRows;
@@ -447,6 +541,8 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
             make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
+    for (int i = tid; i < n_items; i += kFThreads) S.work[i] = 0xFFFFFFFFu;  // empty until set
+    if (tid == 0) S.n_work = n_items;
     // Zero this CTA's share of the histograms the next call will use.
     constexpr int n4 = (int)(kEpochBufBytes / 16);
     uint4 *z = reinterpret_cast<uint4 *>(buf_nxt);
@@ -460,9 +556,8 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
 
   FH_TICK_DECL
   if (!producer) {
-    // Compute warps: stream the tiles; partials of a tile go to
-    // part[tile & 1] once the producer has reduced tile - 2 from it.
-    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    // Compute warps: each chunk (a tile, or a d-range of one) into its own
+    // partial buffer; slots are refilled once per round of n_slots chunks.
     const int hrow = (gq >> 1) < R ? (gq >> 1) : 0;  // hidden row feeding column gq
     const M1 *hrow1 = hB1 + (size_t)hrow * a.D;
     for (int c = 0; c < n1; ++c) {
@@ -473,6 +568,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
         atomicOr(&S.s_err, kErrCopyTimeout);
       phase ^= 1u << s;
       FH_TICK(0);
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
       const unsigned char *slot = ring + (size_t)s * g1.slot_bytes;
       const int ng = cb / 64;
       const int qbase = dc * (g1.cb / 64);  // first 64-byte group of this chunk in the row
@@ -490,55 +586,51 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
         }
       }
       FH_TICK(1);
-      if (dc == g1.ndc - 1) {
-        // lane (g, t): row g (and g + 8) against hidden row t in c[odd] (c[2 + odd])
-        const int par = tile & 1;
-        if (tile >= 2) nbar_sync(kBarPart0 + par, kFBlock);
-        if (tq < R) {
-          S.part[par][gq][tq][warp] = acc0[odd] + acc1[odd];
-          S.part[par][gq + 8][tq][warp] = acc0[2 + odd] + acc1[2 + odd];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) acc0[u] = acc1[u] = 0.f;
+      // lane (g, t): row g (and g + 8) against hidden row t in c[odd] (c[2 + odd])
+      if (tq < R) {
+        float *pc = part1 + (size_t)c * (kTileRows * R * kFWarps);
+        pc[(gq * R + tq) * kFWarps + warp] = acc0[odd] + acc1[odd];
+        pc[((gq + 8) * R + tq) * kFWarps + warp] = acc0[2 + odd] + acc1[2 + odd];
       }
       FH_TICK(2);
-      nbar_arrive(kBarSlot0 + s, kFBlock);
+      if (s == g1.n_slots - 1 && c + 1 < n1) nbar_arrive(kBarSlot0, kFBlock);  // round done
     }
-    for (int t = max(ntile1 - 2, 0); t < ntile1; ++t) nbar_sync(kBarPart0 + (t & 1), kFBlock);
   } else {
-    // Producer warp: refill each slot once it is consumed; reduce each
-    // finished tile over the 16 warps, then score it into the histograms.
-    for (int c = 0; c < n1; ++c) {
-      const int s = c % g1.n_slots, tile = c / g1.ndc, dc = c - tile * g1.ndc;
-      nbar_sync(kBarSlot0 + s, kFBlock);
-      if (lane == 0 && c + g1.n_slots < n1) issue1(c + g1.n_slots);
-      if (dc == g1.ndc - 1) {
-        const int par = tile & 1, tr = min(kTileRows, nc - tile * kTileRows);
-        for (int qd = lane; qd < kTileRows * R; qd += 32) {
-          const int row = qd & (kTileRows - 1), col = qd / kTileRows;
-          const float4 *pp = reinterpret_cast<const float4 *>(&S.part[par][row][col][0]);
-          const float4 x0 = pp[0], x1 = pp[1], x2 = pp[2], x3 = pp[3];
-          const float v = ((x0.x + x0.y) + (x0.z + x0.w)) + ((x1.x + x1.y) + (x1.z + x1.w)) +
-                          (((x2.x + x2.y) + (x2.z + x2.w)) + ((x3.x + x3.y) + (x3.z + x3.w)));
-          if (row < tr && col < a.rows) {
-            const int k = c0 + tile * kTileRows + row;
-            float sc = v * S.scale[k - c0];
-            if (a.do_sample)
-              sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)col, (uint32_t)k);
-            S.local[col][k - c0] = sc;
-            a.scores[(size_t)col * a.score_stride + k] = sc;
-            const uint32_t key = mono(sanitize(sc));
-            atomicAdd(&hist_cur[(size_t)col * kHistWords + kHistCoarse + (key >> 16)], 1u);
-            atomicAdd(&S.coarse[col * kHistCoarse + (key >> 24)], 1u);
-          }
-        }
-        __syncwarp();
-        nbar_arrive(kBarPart0 + par, kFBlock);
-      }
+    // Producer warp: refill the slots after each round of n_slots chunks.
+    for (int c0r = g1.n_slots; c0r < n1; c0r += g1.n_slots) {
+      nbar_sync(kBarSlot0, kFBlock);
+      if (lane == 0)
+        for (int c = c0r; c < min(c0r + g1.n_slots, n1); ++c) issue1(c);
+      __syncwarp();
     }
   }
   __syncthreads();
   FH_STAMP(7);
+  // Stage-1 scores: one (cluster, hidden row) per thread, summed over the
+  // chunks of its tile and the 16 warps.
+  for (int qd = tid; qd < nc * R; qd += kFBlock) {
+    const int col = qd / nc, kk = qd - col * nc;
+    if (col >= a.rows) continue;
+    const int tile = kk / kTileRows, row = kk - tile * kTileRows;
+    float v = 0.f;
+    for (int dc = 0; dc < g1.ndc; ++dc) {
+      const float4 *pp = reinterpret_cast<const float4 *>(
+          part1 + (size_t)(tile * g1.ndc + dc) * (kTileRows * R * kFWarps) + (row * R + col) * kFWarps);
+      const float4 x0 = pp[0], x1 = pp[1], x2 = pp[2], x3 = pp[3];
+      v += ((x0.x + x0.y) + (x0.z + x0.w)) + ((x1.x + x1.y) + (x1.z + x1.w)) +
+           (((x2.x + x2.y) + (x2.z + x2.w)) + ((x3.x + x3.y) + (x3.z + x3.w)));
+    }
+    const int k = c0 + kk;
+    float sc = v * S.scale[kk];
+    if (a.do_sample)
+      sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)col, (uint32_t)k);
+    S.local[col][kk] = sc;
+    a.scores[(size_t)col * a.score_stride + k] = sc;
+    const uint32_t key = mono(sanitize(sc));
+    atomicAdd(&hist_cur[(size_t)col * kHistWords + kHistCoarse + (key >> 16)], 1u);
+    atomicAdd(&S.coarse[col * kHistCoarse + (key >> 24)], 1u);
+  }
+  __syncthreads();
   for (int i = tid; i < a.rows * kHistCoarse; i += kFBlock) {
     const uint32_t cc = S.coarse[i];
     if (cc) atomicAdd(&hist_cur[(size_t)(i / kHistCoarse) * kHistWords + (i % kHistCoarse)], cc);
@@ -552,33 +644,37 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
     FH_STAMP(8);
     atomicAdd(&a.sync[kSyncArrive], 1u);
   }
-  // Speculative L2 prefetch of stage-2 rows while the grid meets. HBM would
-  // sit idle through the barrier and the selection, so the producer warp
-  // pulls the w_perm rows of this CTA's clusters that are likely to be
-  // selected: score above its own mean + z * std, where z is the normal
-  // quantile of the selection rate minus a margin. A wrong guess only costs
-  // bandwidth that was idle.
-  if (producer && !a.do_sample && nc > 1) {
+  // While the grid meets, the producer warp estimates each row's selection
+  // threshold from this CTA's scores (mean + z * std, z the normal quantile
+  // of the selection rate minus a margin), used below to guess the histogram
+  // bin, and in greedy mode prefetches into L2 the w_perm rows of the
+  // clusters above the estimate: HBM would otherwise sit idle through the
+  // barrier and the selection, and a wrong guess only costs idle bandwidth.
+  if (producer) {
     const size_t cluster_bytes = (size_t)a.cap * a.D * sizeof(HT);
     for (int r = 0; r < a.rows; ++r) {
       float sum = 0.f, sq = 0.f;
+      int n = 0;
       for (int i = lane; i < nc; i += 32) {
         const float v = S.local[r][i];
         if (isfinite(v)) {
           sum += v;
           sq += v * v;
+          ++n;
         }
       }
       sum = warp_sum(sum);
       sq = warp_sum(sq);
-      const float mean = sum / nc;
-      const float sd = sqrtf(fmaxf(sq / nc - mean * mean, 0.f));
+      n = __reduce_add_sync(0xFFFFFFFFu, n);
+      const float mean = n > 0 ? sum / n : 0.f;
+      const float sd = n > 0 ? sqrtf(fmaxf(sq / n - mean * mean, 0.f)) : 0.f;
       const float frac = fminf(0.5f, (float)a.p / (float)a.K);
       const float t_est = mean + (-normcdfinvf(frac) - 0.25f) * sd;
-      for (int i = lane; i < nc; i += 32)
-        if (S.local[r][i] > t_est && cluster_bytes % 16 == 0)
-          bulk_prefetch_l2(reinterpret_cast<const char *>(a.w_perm) + (size_t)(c0 + i) * cluster_bytes,
-                           (uint32_t)cluster_bytes);
+      if (lane == 0) S.t_est[r] = t_est;
+      if (!a.do_sample && nc > 1 && cluster_bytes % 16 == 0)
+        for (int i = lane; i < nc; i += 32)
+          if (S.local[r][i] > t_est)
+            bulk_prefetch_l2(wp_bytes(a) + (size_t)(c0 + i) * cluster_bytes, (uint32_t)cluster_bytes);
     }
   }
   if (tid == 0) {
@@ -603,10 +699,10 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   if (warp >= kFMaxRows && !producer) {
     const int nv = a.rows * (Kp / 4), t0 = tid - kFMaxRows * 32;
     constexpr int nt = kFThreads - kFMaxRows * 32;
-    for (int i = t0; i < nv; i += 4 * nt) {
-      float4 v[4];
+    for (int i = t0; i < nv; i += 8 * nt) {
+      float4 v[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const int j = i + u * nt;
         if (j < nv) {
           const int r = j / (Kp / 4), cc = j - r * (Kp / 4);
@@ -614,59 +710,81 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 8; ++u)
         if (i + u * nt < nv) reinterpret_cast<float4 *>(sc_s)[i + u * nt] = v[u];
     }
   } else if (warp < a.rows) {
-    const uint32_t *h = hist_cur + (size_t)warp * kHistWords;
-    int cb, above1, cnt1, fb, above2, cnt2;
-    warp_find_bin<true>(h, a.p, cb, above1, cnt1);
-    warp_find_bin<true>(h + kHistCoarse + cb * 256, a.p - above1, fb, above2, cnt2);
-    if (lane == 0) {
-      S.thr[warp].prefix = (uint32_t)(cb * 256 + fb);
-      S.thr[warp].need = a.p - above1 - above2;
-      S.thr[warp].cnt = cnt2;
-    }
+    const float te = S.t_est[warp];
+    const int guess = isfinite(te) ? (int)(mono(te) >> 24) : kHistCoarse / 2;
+    const RowThreshold t = warp_find_bucket(hist_cur + (size_t)warp * kHistWords, a.p, guess);
+    if (lane == 0) S.thr[warp] = t;
   }
   __syncthreads();
   FH_STAMP(9);
-  // Pass A, 128-cluster chunks over the compute warps: keys above the
-  // threshold bucket per chunk, and the bucket's keys (when any is needed).
+  // Pass A: per 128-cluster chunk, the keys above the threshold bucket, and
+  // the bucket's keys when any of them is needed. Each warp takes four
+  // chunks per pass (loads first). Key order equals float order except at
+  // zero and non-finite values, so rows whose bucket bounds are finite and
+  // nonzero compare floats; the rest compare the monotone integer keys.
   const int nch = (a.K + 127) >> 7;
   if (!producer) {
     for (int r = 0; r < a.rows; ++r) {
       const uint32_t P = S.thr[r].prefix;
       const uint32_t thrA = P >= 0xFFFFu ? 0xFFFFFFFFu : (P + 1u) << 16;
       const uint32_t bktLo = P << 16;
+      const float X = unmono(thrA), Xlo = unmono(bktLo);
+      const bool fast = P < 0xFFFFu && isfinite(X) && X != 0.f && isfinite(Xlo) && Xlo != 0.f;
       const bool want = S.thr[r].need > 0;
       const float4 *row4 = reinterpret_cast<const float4 *>(sc_s + r * Kp);
-      for (int ch = warp; ch < nch; ch += kFWarps) {
-        const int k0 = (ch << 7) + 4 * lane;
-        int above = 0;
+      for (int ch0 = warp; ch0 < nch; ch0 += 4 * kFWarps) {
+        float v[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k0 = ((ch0 + j * kFWarps) << 7) + 4 * lane;
+          float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (k0 < a.K) v4 = row4[k0 >> 2];
+          v[j][0] = v4.x;
+          v[j][1] = v4.y;
+          v[j][2] = v4.z;
+          v[j][3] = v4.w;
+        }
+        int cnt[4];
         uint32_t inb = 0u;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (k0 < a.K) {
-          const float4 v4 = row4[k0 >> 2];
-          v[0] = v4.x;
-          v[1] = v4.y;
-          v[2] = v4.z;
-          v[3] = v4.w;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k0 = ((ch0 + j * kFWarps) << 7) + 4 * lane;
+          cnt[j] = 0;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const uint32_t m = mono(sanitize(v[u]));
             const bool ok = k0 + u < a.K;
-            above += ok && m >= thrA;
-            inb |= (uint32_t)(ok && m - bktLo < 65536u) << u;
+            bool above, in;
+            if (fast) {
+              const float x = v[j][u];
+              above = x >= X;
+              in = x >= Xlo && x < X;
+            } else {
+              const uint32_t m = mono(sanitize(v[j][u]));
+              above = m >= thrA;
+              in = m - bktLo < 65536u;
+            }
+            cnt[j] += ok && above;
+            inb |= (uint32_t)(ok && in) << (4 * j + u);
           }
         }
-        above = __reduce_add_sync(0xFFFFFFFFu, above);
-        if (lane == 0) S.chunk_sel[r][ch] = above;
-        if (want && __any_sync(0xFFFFFFFFu, inb != 0u)) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if ((inb >> u) & 1u) {
+        for (int j = 0; j < 4; ++j) cnt[j] = __reduce_add_sync(0xFFFFFFFFu, cnt[j]);
+        if (lane == 0) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (ch0 + j * kFWarps < nch) S.chunk_sel[r][ch0 + j * kFWarps] = cnt[j];
+        }
+        if (want && __any_sync(0xFFFFFFFFu, inb != 0u)) {
+          for (int bit = 0; bit < 16; ++bit)
+            if ((inb >> bit) & 1u) {
+              const int j = bit >> 2, u = bit & 3;
+              const int k = ((ch0 + j * kFWarps) << 7) + 4 * lane + u;
               const int m = atomicAdd(&S.bkt_n[r], 1);
-              if (m < kBktCap) S.bkt[r][m] = pack(sanitize(v[u]), (uint32_t)(k0 + u));
+              if (m < kBktCap) S.bkt[r][m] = pack(sanitize(v[j][u]), (uint32_t)k);
             }
         }
       }
@@ -674,30 +792,9 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   }
   __syncthreads();
   FH_STAMP(12);
-  // Threshold key of row r: keys above the bucket, plus the `need` largest
-  // keys of the bucket. Small buckets: the key of rank need - 1 (warp r).
-  if (warp < a.rows) {
-    const RowThreshold t = S.thr[warp];
-    const int n = S.bkt_n[warp];
-    unsigned long long T = t.prefix >= 0xFFFFu ? ~0ull : (unsigned long long)(t.prefix + 1u) << 48;
-    if (t.need > 0 && n <= kBktCap) {
-      T = (unsigned long long)t.prefix << 48;  // fewer keys than needed: take the whole bucket
-      for (int j = lane; j < n; j += 32) {
-        const unsigned long long mine = S.bkt[warp][j];
-        int rank = 0;
-        for (int m = 0; m < n; ++m) rank += S.bkt[warp][m] > mine;
-        if (rank == t.need - 1) S.tkey[warp] = mine;
-      }
-      __syncwarp();
-      if (lane == 0 && t.need <= n) T = S.tkey[warp];
-    }
-    __syncwarp();
-    if (lane == 0) S.tkey[warp] = T;
-  }
-  __syncthreads();
-  FH_STAMP(4);
-  // Large buckets: radix select of the need-th largest key, 8 bits per pass
-  // over the 48 key bits below the bucket prefix.
+  // Large buckets (rare): radix select of the need-th largest key, 8 bits per
+  // pass over the 48 key bits below the bucket prefix, then a recount of the
+  // selected keys per chunk.
   for (int r = 0; r < a.rows; ++r) {
     if (S.thr[r].need <= 0 || S.bkt_n[r] <= kBktCap) continue;  // block-uniform
     unsigned long long pre = (unsigned long long)S.thr[r].prefix << 48;
@@ -724,25 +821,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
       need -= S.rsel_above;
       __syncthreads();  // rsel_* and rhist are reused by the next pass
     }
-    if (tid == 0) S.tkey[r] = pre;
-    __syncthreads();
-  }
-  FH_STAMP(13);
-  // Selected keys (key >= tkey[r]) per chunk: the keys above the bucket plus
-  // the listed bucket winners, or a recount for a large bucket.
-  const int per_row = a.p + a.n_special;
-  const int total = a.rows * per_row;
-  const int lo = (int)((long long)b * total / G), hi = (int)((long long)(b + 1) * total / G);
-  const int n_items = min(hi - lo, kWorkCap);  // the host keeps hi - lo <= kWorkCap
-  for (int r = 0; r < a.rows; ++r) {
-    const unsigned long long T = S.tkey[r];
-    if (S.thr[r].need <= 0) continue;
-    if (S.bkt_n[r] <= kBktCap) {
-      for (int m = tid; m < S.bkt_n[r]; m += kFBlock) {
-        const unsigned long long key = S.bkt[r][m];
-        if (key >= T) atomicAdd(&S.chunk_sel[r][(int)(0xFFFFFFFFu - (uint32_t)key) >> 7], 1);
-      }
-    } else if (!producer) {
+    if (!producer) {
       const float4 *row4 = reinterpret_cast<const float4 *>(sc_s + r * Kp);
       for (int ch = warp; ch < nch; ch += kFWarps) {
         const int k0 = (ch << 7) + 4 * lane;
@@ -752,26 +831,56 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
           const float v[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
           for (int u = 0; u < 4; ++u)
-            cnt += k0 + u < a.K && pack(sanitize(v[u]), (uint32_t)(k0 + u)) >= T;
+            cnt += k0 + u < a.K && pack(sanitize(v[u]), (uint32_t)(k0 + u)) >= pre;
         }
         cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
         if (lane == 0) S.chunk_sel[r][ch] = cnt;
       }
     }
+    if (tid == 0) S.tkey[r] = pre;
+    __syncthreads();
   }
-  for (int i = tid; i < n_items; i += kFBlock) S.work[i] = 0xFFFFFFFFu;  // empty until set
-  if (tid == 0) S.n_work = n_items;
-  __syncthreads();
-  // Chunk offsets in id order (warp r, row r).
+  FH_STAMP(13);
+  // Warp r, row r: the threshold key (keys above the bucket plus the `need`
+  // largest keys of a small bucket: the key of rank need - 1), the bucket
+  // winners into their chunks' counts, then the chunks' first positions.
   if (warp < a.rows) {
+    const RowThreshold t = S.thr[warp];
+    const int n = S.bkt_n[warp];
+    if (t.need <= 0 || n <= kBktCap) {
+      unsigned long long T =
+          t.prefix >= 0xFFFFu ? ~0ull : (unsigned long long)(t.prefix + 1u) << 48;
+      if (t.need > 0) {
+        T = (unsigned long long)t.prefix << 48;  // fewer keys than needed: the whole bucket
+        unsigned long long found = 0ull;
+        bool hit = false;
+        for (int j = lane; j < n; j += 32) {
+          const unsigned long long mine = S.bkt[warp][j];
+          int rank = 0;
+          for (int m = 0; m < n; ++m) rank += S.bkt[warp][m] > mine;
+          if (rank == t.need - 1) {
+            found = mine;
+            hit = true;
+          }
+        }
+        const unsigned hm = __ballot_sync(0xFFFFFFFFu, hit);
+        if (hm) T = __shfl_sync(0xFFFFFFFFu, found, __ffs(hm) - 1);
+        for (int j = lane; j < n; j += 32) {
+          const unsigned long long key = S.bkt[warp][j];
+          if (key >= T) atomicAdd(&S.chunk_sel[warp][(int)(0xFFFFFFFFu - (uint32_t)key) >> 7], 1);
+        }
+      }
+      if (lane == 0) S.tkey[warp] = T;
+    }
+    __syncwarp();
     const int per = (nch + 31) / 32, j0 = min(nch, lane * per), j1 = min(nch, j0 + per);
     int sum = 0;
     for (int j = j0; j < j1; ++j) sum += S.chunk_sel[warp][j];
     int incl = sum;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl += t;
+      const int tt = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += tt;
     }
     int off = incl - sum;
     for (int j = j0; j < j1; ++j) {
@@ -781,9 +890,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   }
   __syncthreads();
   FH_STAMP(14);
-  // This CTA's items: [lo, hi) of rows * (p + n_special), row-major; row r's
-  // selected clusters in id order, then its special tokens. Only the chunks
-  // whose positions meet the range are walked.
+  // This CTA's items: only the chunks whose positions meet [lo, hi) are walked.
   if (!producer) {
     for (int r = 0; r < a.rows; ++r) {
       const int base = r * per_row;
@@ -995,6 +1102,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
       a.sync[kSyncEpoch] = epoch + 1u;
     }
   }
+  FH_TRACE_WRITE();
 }
 
 }  // namespace fh

@@ -46,6 +46,9 @@ int cuda_fail(cudaError_t e, const char *what) {
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+#ifdef FH_TRACE
+unsigned long long *g_trace_buf = nullptr;
+#endif
 
 template <typename Kern, typename... Args>
 cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
@@ -347,7 +350,8 @@ int run_stage1(const fh_head *h, const void *hidden, int rows, bool sample, floa
 // three-kernel path.
 bool fused_ok(const fh_head_desc &d, int rows, bool sample, int grid) {
   if (d.flags & FH_FLAG_NO_FUSED) return false;
-  if (rows < 1 || rows > fh::kFMaxRows || grid < rows || d.cluster_base != 0) return false;
+  if (rows < 1 || rows > fh::kFMaxRows || grid < rows || grid > 1024 || d.cluster_base != 0)
+    return false;
   const int wdt = sample ? d.sample_dtype : d.score_dtype;
   // rows of whole 128-byte group pairs; hidden rows (16-bit) in shared memory
   const int wt_bytes = wdt == FH_FP8_E4M3 ? 1 : 2;
@@ -358,6 +362,11 @@ bool fused_ok(const fh_head_desc &d, int rows, bool sample, int grid) {
   if (d.n_probes > fh::kFMaxProbes || d.cluster_size > fh::kS3MaxRows) return false;
   if (d.n_special > fh::kFMaxSpecial || d.n_clusters >= (1 << 24)) return false;
   if ((d.n_clusters + 127) / 128 > fh::kMaxChunks) return false;
+  {  // stage-1 chunks of the largest CTA slice, each with its own partial buffer
+    const fh::RingGeom g1 = fh::ring_geom(d.hidden * wt_bytes);
+    const int nc_max = (d.n_clusters + grid - 1) / grid;
+    if ((nc_max + fh::kTileRows - 1) / fh::kTileRows * g1.ndc > fh::kMaxS1Chunks) return false;
+  }
   // every CTA holds the score rows in its 128 KB ring; items per CTA fit its work list
   if ((size_t)rows * round_up((size_t)d.n_clusters, 4) * sizeof(float) > (size_t)fh::kRingBytes)
     return false;
@@ -397,6 +406,9 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
   a.barrier_polls = test_timeout ? (1u << 12) : (1u << 22);
   a.copy_polls = 1u << 22;
   a.extra_arrivals = test_timeout ? 1 : 0;
+#ifdef FH_TRACE
+  a.trace = g_trace_buf;
+#endif
   const int wdt = sample ? d.sample_dtype : d.score_dtype;
   FH_CHECK_LAUNCH(launch_fused(d.weight_dtype, wdt, a, grid, s), "one-kernel step launch");
   return FH_OK;
@@ -445,10 +457,11 @@ extern "C" {
 FH_API int fh_version(void) { return 1; }
 
 #ifdef FH_TRACE
-// Profiling builds only (not declared in the public header).
+// Profiling builds only (not declared in the public header): device buffer
+// for the one-kernel step's phase stamps, passed to every later launch.
 FH_API int fh_debug_set_trace(void *buf) {
-  const cudaError_t e = cudaMemcpyToSymbol(fh::g_fh_trace, &buf, sizeof(buf));
-  return e == cudaSuccess ? FH_OK : cuda_fail(e, "trace buffer");
+  g_trace_buf = reinterpret_cast<unsigned long long *>(buf);
+  return FH_OK;
 }
 #endif
 
