@@ -6,6 +6,7 @@
 // graph. Kernels after the first of a call are launched with programmatic
 // dependent launch so that their CTAs are resident before their predecessor
 // finishes.
+#include <cublasLt.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -15,9 +16,10 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/flashhead.h"
-#include "fh_fused.cuh"
+#include "fh_batched.cuh"
 
 namespace {
 
@@ -152,8 +154,20 @@ cudaError_t launch_fused(int hdt, int wdt, const fh::FusedArgs &a, int grid, cud
 
 }  // namespace
 
+// cuBLASLt objects of one batched stage-1 GEMM shape (rows x matrix).
+struct LtPlan {
+  int rows = 0, stride = 0;
+  bool sample = false;
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
+  cublasLtMatmulAlgo_t algo;
+};
+
 struct fh_head {
   fh_head_desc d;
+  mutable cublasLtHandle_t lt = nullptr;  // created by the first batched call
+  mutable std::mutex plan_mutex;  // the plan cache fills on first use of a row count
+  mutable std::vector<LtPlan> plans;
 };
 
 // ---------------------------------------------------------------------------
@@ -161,13 +175,19 @@ struct fh_head {
 // ---------------------------------------------------------------------------
 namespace {
 
+constexpr size_t kLtWorkspaceBytes = 8u << 20;  // cuBLASLt scratch of the batched GEMM
+
 struct Workspace {
   float *scores;                // [rows, score_stride]
   int score_stride;
   int32_t *probes;              // [rows, p]
   unsigned long long *packed;   // [rows]
   unsigned *counter;            // [1]
-  unsigned char *epoch_bufs;    // one-kernel histograms, queue, tie lists
+  unsigned char *epoch_bufs;    // one-kernel histograms
+  // batched steps (rows >= kBatchMinRows) only, else null
+  int *inv_cnt, *inv_off, *inv_item_off, *inv_cursor, *inv_meta, *inv_list;
+  fh::InvItem *inv_items;
+  void *lt_ws;
   size_t bytes;                 // bytes needed for `rows`
 };
 
@@ -187,7 +207,15 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
       256 + fh::kHistBytes + round_up((size_t)rows * sizeof(unsigned long long), 256);
   const size_t probes = round_up((size_t)rows * d.n_probes * sizeof(int32_t), 256);
   const size_t scores = round_up((size_t)rows * w.score_stride * sizeof(float), 256);
-  w.bytes = state + probes + scores + 256;
+  // batched steps: inverted index and GEMM scratch below the scores
+  const bool batched = rows >= fh::kBatchMinRows;
+  const size_t kint = round_up((size_t)d.n_clusters * sizeof(int), 256);
+  const size_t n_pairs = (size_t)rows * d.n_probes;
+  const size_t max_items = n_pairs / fh::kInvRows + (size_t)d.n_clusters + 1;
+  const size_t inv = batched ? 4 * kint + 256 + round_up(n_pairs * sizeof(int), 256) +
+                                   round_up(max_items * sizeof(fh::InvItem), 256) + kLtWorkspaceBytes
+                             : 0;
+  w.bytes = state + probes + scores + inv + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
   w.epoch_bufs = reinterpret_cast<unsigned char *>(p + 256);
   w.packed = reinterpret_cast<unsigned long long *>(p + 256 + fh::kHistBytes);
@@ -196,6 +224,23 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   const size_t scores_off = probes_off >= scores ? probes_off - scores : 0;
   w.probes = reinterpret_cast<int32_t *>(p + probes_off);
   w.scores = reinterpret_cast<float *>(p + scores_off);
+  w.inv_cnt = w.inv_off = w.inv_item_off = w.inv_cursor = w.inv_meta = w.inv_list = nullptr;
+  w.inv_items = nullptr;
+  w.lt_ws = nullptr;
+  if (batched) {
+    size_t q = scores_off >= inv ? scores_off - inv : 0;
+    w.lt_ws = p + q;
+    q += kLtWorkspaceBytes;
+    w.inv_items = reinterpret_cast<fh::InvItem *>(p + q);
+    q += round_up(max_items * sizeof(fh::InvItem), 256);
+    w.inv_list = reinterpret_cast<int *>(p + q);
+    q += round_up(n_pairs * sizeof(int), 256);
+    w.inv_cnt = reinterpret_cast<int *>(p + q);
+    w.inv_off = reinterpret_cast<int *>(p + q + kint);
+    w.inv_item_off = reinterpret_cast<int *>(p + q + 2 * kint);
+    w.inv_cursor = reinterpret_cast<int *>(p + q + 3 * kint);
+    w.inv_meta = reinterpret_cast<int *>(p + q + 4 * kint);
+  }
   return w;
 }
 
@@ -414,6 +459,257 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
   return FH_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Batched steps (rows >= kBatchMinRows): cuBLASLt stage-1 GEMM, the selection
+// kernel, the inverted index and the inverted stage 2.
+// ---------------------------------------------------------------------------
+bool batched_ok(const fh_head *h, int rows, bool sample) {
+  const fh_head_desc &d = h->d;
+  if (rows < fh::kBatchMinRows || (d.flags & FH_FLAG_NO_FUSED)) return false;
+  if (!(sample ? d.centroid_w16 : d.cluster_w16) || d.cluster_base != 0) return false;
+  if (d.cluster_size > fh::kTileRows || (d.hidden * 2) % 128 != 0) return false;
+  return sm_count() > 0;
+}
+
+const char *lt_status_name(cublasStatus_t st) {
+  switch (st) {
+    case CUBLAS_STATUS_NOT_INITIALIZED: return "not initialized";
+    case CUBLAS_STATUS_ALLOC_FAILED: return "allocation failed";
+    case CUBLAS_STATUS_INVALID_VALUE: return "invalid value";
+    case CUBLAS_STATUS_ARCH_MISMATCH: return "arch mismatch";
+    case CUBLAS_STATUS_EXECUTION_FAILED: return "execution failed";
+    case CUBLAS_STATUS_NOT_SUPPORTED: return "not supported";
+    default: return "error";
+  }
+}
+
+#define FH_CHECK_LT(expr, what)                                                           \
+  do {                                                                                    \
+    cublasStatus_t _st = (expr);                                                          \
+    if (_st != CUBLAS_STATUS_SUCCESS)                                                     \
+      return fail(FH_ERR_CUDA, "%s: cuBLASLt %s (%d)", what, lt_status_name(_st), (int)_st); \
+  } while (0)
+
+void destroy_plan(LtPlan &pl) {
+  if (pl.a) cublasLtMatrixLayoutDestroy(pl.a);
+  if (pl.b) cublasLtMatrixLayoutDestroy(pl.b);
+  if (pl.c) cublasLtMatrixLayoutDestroy(pl.c);
+  if (pl.op) cublasLtMatmulDescDestroy(pl.op);
+  pl.a = pl.b = pl.c = nullptr;
+  pl.op = nullptr;
+}
+
+// S^T (K x rows, column-major, ld = score_stride) = Wc (K x D) . H^T (D x rows):
+// the row-major [K, D] matrix is a column-major D x K operand taken transposed.
+int get_plan(const fh_head *h, int rows, bool sample, int stride, const LtPlan **out) {
+  std::lock_guard<std::mutex> lock(h->plan_mutex);
+  for (const LtPlan &pl : h->plans)
+    if (pl.rows == rows && pl.sample == sample && pl.stride == stride) {
+      *out = &pl;
+      return FH_OK;
+    }
+  const fh_head_desc &d = h->d;
+  if (!h->lt) {
+    const cublasStatus_t ls = cublasLtCreate(&h->lt);
+    if (ls != CUBLAS_STATUS_SUCCESS) {
+      h->lt = nullptr;
+      return fail(FH_ERR_CUDA, "cuBLASLt handle: %s", lt_status_name(ls));
+    }
+  }
+  LtPlan pl;
+  pl.rows = rows;
+  pl.stride = stride;
+  pl.sample = sample;
+  const cudaDataType_t dt = d.weight_dtype == FH_BF16 ? CUDA_R_16BF : CUDA_R_16F;
+  int st = FH_OK;
+  do {
+    if (cublasLtMatmulDescCreate(&pl.op, CUBLAS_COMPUTE_32F, CUDA_R_32F) != CUBLAS_STATUS_SUCCESS) {
+      st = fail(FH_ERR_CUDA, "cuBLASLt matmul descriptor");
+      break;
+    }
+    const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+    cublasLtMatmulDescSetAttribute(pl.op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta));
+    cublasLtMatmulDescSetAttribute(pl.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb));
+    if (cublasLtMatrixLayoutCreate(&pl.a, dt, d.hidden, d.n_clusters, d.hidden) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatrixLayoutCreate(&pl.b, dt, d.hidden, rows, d.hidden) != CUBLAS_STATUS_SUCCESS ||
+        cublasLtMatrixLayoutCreate(&pl.c, CUDA_R_32F, d.n_clusters, rows, stride) !=
+            CUBLAS_STATUS_SUCCESS) {
+      st = fail(FH_ERR_CUDA, "cuBLASLt matrix layouts");
+      break;
+    }
+    cublasLtMatmulPreference_t pref = nullptr;
+    if (cublasLtMatmulPreferenceCreate(&pref) != CUBLAS_STATUS_SUCCESS) {
+      st = fail(FH_ERR_CUDA, "cuBLASLt preference");
+      break;
+    }
+    const size_t ws = kLtWorkspaceBytes;
+    cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws,
+                                         sizeof(ws));
+    cublasLtMatmulHeuristicResult_t res;
+    int n = 0;
+    const cublasStatus_t hs = cublasLtMatmulAlgoGetHeuristic(h->lt, pl.op, pl.a, pl.b, pl.c, pl.c,
+                                                             pref, 1, &res, &n);
+    cublasLtMatmulPreferenceDestroy(pref);
+    if (hs != CUBLAS_STATUS_SUCCESS || n < 1) {
+      st = fail(FH_ERR_UNSUPPORTED, "no cuBLASLt algorithm for the %d-row stage-1 GEMM", rows);
+      break;
+    }
+    pl.algo = res.algo;
+  } while (false);
+  if (st != FH_OK) {
+    destroy_plan(pl);
+    return st;
+  }
+  h->plans.push_back(pl);
+  *out = &h->plans.back();
+  return FH_OK;
+}
+
+cudaError_t prepare_inv_build() {
+  static bool done[128];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(fh::k_inv_build, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(fh::kSelMaxItems * sizeof(int)));
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
+
+int grid_for(long long n, int block) {
+  long long g = (n + block - 1) / block;
+  const int cap = 4 * (sm_count() > 0 ? sm_count() : 148);
+  return (int)(g < 1 ? 1 : g > cap ? cap : g);
+}
+
+template <typename HT>
+cudaError_t launch_stage2_inv(const fh::InvArgs &a, int grid, cudaStream_t s) {
+  static bool attr_done[128];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (!attr_done[dev]) {
+      e = cudaFuncSetAttribute(fh::k_stage2_inv<HT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fh::kInvSmemBytes);
+      if (e != cudaSuccess) return e;
+      attr_done[dev] = true;
+    }
+  }
+  return launch(fh::k_stage2_inv<HT>, dim3(grid), dim3(fh::kInvBlock), fh::kInvSmemBytes, s, false,
+                a);
+}
+
+// Stage 1 of a batched step: GEMM scores (+ fp8 row scale, + sampling keys),
+// then the top-p clusters of every row into `probes` (if non-null).
+int run_batched_stage1(const fh_head *h, const void *hidden, int rows, bool sample,
+                       float temperature, uint64_t seed, uint64_t offset, const Workspace &w,
+                       float *scores, int stride, int32_t *probes, cudaStream_t s) {
+  const fh_head_desc &d = h->d;
+  const LtPlan *pl = nullptr;
+  int st = get_plan(h, rows, sample, stride, &pl);
+  if (st != FH_OK) return st;
+  const float alpha = 1.f, beta = 0.f;
+  FH_CHECK_LT(cublasLtMatmul(h->lt, pl->op, &alpha, sample ? d.centroid_w16 : d.cluster_w16,
+                             pl->a, hidden, pl->b, &beta, scores, pl->c, scores, pl->c, &pl->algo,
+                             w.lt_ws, kLtWorkspaceBytes, s),
+              "stage-1 GEMM");
+  const float *scale = sample ? d.centroid_scale : d.cluster_scale;
+  const int K = d.n_clusters;
+  if (scale || sample)
+    FH_CHECK_LAUNCH(launch(fh::k_score_epilogue, dim3((K + 1023) / 1024, rows), dim3(256), 0, s,
+                           false, scores, stride, rows, K, scale, sample ? 1 : 0, temperature,
+                           rng_key(seed, offset)),
+                    "stage-1 epilogue launch");
+  if (!probes) return FH_OK;
+  FH_CHECK_LAUNCH(prepare_select(), "select kernel attribute");
+  fh::SelectArgs se = select_dense_args(d, scores, stride, rows);
+  se.probes = probes;
+  se.wait_prior = 0;
+  FH_CHECK_LAUNCH(launch(fh::k_select, dim3(rows), dim3(fh::kSelThreads),
+                         (size_t)K * sizeof(unsigned long long), s, false, se),
+                  "probe selection launch");
+  return FH_OK;
+}
+
+int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+                uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
+                cudaStream_t s) {
+  const fh_head_desc &d = h->d;
+  int st = run_batched_stage1(h, hidden, rows, sample, temperature, seed, offset, w, w.scores,
+                              w.score_stride, w.probes, s);
+  if (st != FH_OK) return st;
+  const fh::RngKey rng = rng_key(seed, offset);
+  const int K = d.n_clusters, p = d.n_probes;
+  FH_CHECK_LAUNCH(cudaMemsetAsync(w.inv_cnt, 0, (size_t)K * sizeof(int), s), "index reset");
+  const long long pairs = (long long)rows * p;
+  FH_CHECK_LAUNCH(launch(fh::k_inv_count, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
+                         (const int32_t *)w.probes, rows, p, K, w.inv_cnt),
+                  "index count launch");
+  FH_CHECK_LAUNCH(prepare_inv_build(), "index build attribute");
+  FH_CHECK_LAUNCH(launch(fh::k_inv_build, dim3(1), dim3(1024), (size_t)K * sizeof(int), s, false,
+                         (const int *)w.inv_cnt,
+                         K, w.inv_off, w.inv_item_off, w.inv_cursor, w.inv_meta),
+                  "index build launch");
+  FH_CHECK_LAUNCH(launch(fh::k_inv_scatter, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
+                         (const int32_t *)w.probes, rows, p, K, (const int *)w.inv_off,
+                         w.inv_cursor, w.inv_list),
+                  "index scatter launch");
+  FH_CHECK_LAUNCH(launch(fh::k_inv_items, dim3(grid_for(K, 256)), dim3(256), 0, s, false,
+                         (const int *)w.inv_cnt, (const int *)w.inv_off,
+                         (const int *)w.inv_item_off, (const int *)w.inv_list, K, w.inv_items),
+                  "index items launch");
+  fh::InvArgs ia;
+  memset(&ia, 0, sizeof(ia));
+  ia.hidden = hidden;
+  ia.rows = rows;
+  ia.D = d.hidden;
+  ia.w_perm = d.w_perm;
+  ia.vocab_map = d.vocab_map;
+  ia.K = K;
+  ia.cap = d.cluster_size;
+  ia.items = w.inv_items;
+  ia.meta = w.inv_meta;
+  ia.do_sample = sample ? 1 : 0;
+  ia.temperature = temperature;
+  ia.rng = rng;
+  ia.packed = w.packed;
+  ia.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
+  ia.copy_polls = 1u << 22;
+  const int grid = sm_count();
+  if (d.weight_dtype == FH_BF16)
+    FH_CHECK_LAUNCH(launch_stage2_inv<__nv_bfloat16>(ia, grid, s), "inverted stage-2 launch");
+  else
+    FH_CHECK_LAUNCH(launch_stage2_inv<__half>(ia, grid, s), "inverted stage-2 launch");
+  if (d.n_special > 0) {
+    const long long warps = (long long)rows * d.n_special;
+    const int n_slots = K * d.cluster_size;
+    if (d.weight_dtype == FH_BF16)
+      FH_CHECK_LAUNCH(launch(fh::k_special_scores<__nv_bfloat16>, dim3(grid_for(warps * 32, 256)),
+                             dim3(256), 0, s, false, hidden, rows, d.hidden, d.w_perm, d.vocab_map,
+                             d.special_slots, d.n_special, n_slots, sample ? 1 : 0, temperature,
+                             rng, w.packed),
+                      "special-token launch");
+    else
+      FH_CHECK_LAUNCH(launch(fh::k_special_scores<__half>, dim3(grid_for(warps * 32, 256)),
+                             dim3(256), 0, s, false, hidden, rows, d.hidden, d.w_perm, d.vocab_map,
+                             d.special_slots, d.n_special, n_slots, sample ? 1 : 0, temperature,
+                             rng, w.packed),
+                      "special-token launch");
+  }
+  FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
+                         w.packed, rows, out_ids),
+                  "finalize launch");
+  return FH_OK;
+}
+
 int validate_desc(const fh_head_desc *d) {
   if (!d) return fail(FH_ERR_INVALID_ARGUMENT, "null descriptor");
   if (d->hidden <= 0 || d->hidden % 16 != 0)
@@ -444,6 +740,8 @@ int validate_desc(const fh_head_desc *d) {
   if (d->n_special < 0 || (d->n_special > 0 && !d->special_slots))
     return fail(FH_ERR_INVALID_ARGUMENT, "n_special=%d with null special_slots", d->n_special);
   if (d->cluster_base < 0) return fail(FH_ERR_INVALID_ARGUMENT, "cluster_base < 0");
+  if (!aligned16(d->cluster_w16) || !aligned16(d->centroid_w16))
+    return fail(FH_ERR_INVALID_ARGUMENT, "16-bit stage-1 copies must be 16-byte aligned");
   return FH_OK;
 }
 
@@ -480,13 +778,24 @@ FH_API int fh_head_create(const fh_head_desc *desc, fh_head **out) {
 }
 
 FH_API int fh_head_destroy(fh_head *head) {
+  if (head) {
+    for (LtPlan &pl : head->plans) destroy_plan(pl);
+    if (head->lt) cublasLtDestroy(head->lt);
+  }
   delete head;
   return FH_OK;
 }
 
 FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample) {
   if (!head || rows <= 0) return 0;
-  return fused_ok(head->d, rows, do_sample != 0, sm_count()) ? 1 : 3;
+  const fh_head_desc &d = head->d;
+  if (batched_ok(head, rows, do_sample != 0)) {
+    // GEMM, [epilogue], select, index reset, count, build, scatter, items,
+    // stage 2, [specials], finalize
+    const bool epi = do_sample || (do_sample ? d.centroid_scale : d.cluster_scale);
+    return 9 + (epi ? 1 : 0) + (d.n_special > 0 ? 1 : 0);
+  }
+  return fused_ok(d, rows, do_sample != 0, sm_count()) ? 1 : 3;
 }
 
 FH_API size_t fh_workspace_error_offset(void) { return fh::kSyncError * sizeof(uint32_t); }
@@ -504,6 +813,8 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   const int grid = sm_count();
+  if (batched_ok(head, rows, false))
+    return run_batched(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, s);
   if (fused_ok(head->d, rows, false, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, grid, s);
   st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
@@ -534,6 +845,8 @@ FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   const int grid = sm_count();
+  if (batched_ok(head, rows, true))
+    return run_batched(head, hidden, rows, true, temperature, seed, offset, out_ids, w, s);
   if (fused_ok(head->d, rows, true, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, true, temperature, seed, offset, out_ids, w, grid, s);
   st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
@@ -568,6 +881,11 @@ FH_API int fh_top_clusters(const fh_head *head, const void *hidden, int rows, in
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
+  // the stage 1 of the step the library runs for this many rows
+  if (batched_ok(head, rows, do_sample != 0))
+    return run_batched_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w,
+                              out_scores ? out_scores : w.scores,
+                              out_scores ? head->d.n_clusters : w.score_stride, out_probes, s);
   return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, out_scores,
                     out_probes, nullptr, 0, s);
 }

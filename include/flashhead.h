@@ -98,6 +98,14 @@ typedef struct fh_head_desc {
   const void *centroid_w;
   const float *centroid_scale;
   const int32_t *special_slots;
+  /* Optional copies of cluster_w / centroid_w in weight_dtype with the same
+   * values (fp8 values are exact in 16 bits; the fp8 row scales still apply).
+   * When present, calls with >= 16 rows run stage 1 as a tensor-core GEMM
+   * (cuBLASLt) and stage 2 over an inverted cluster -> rows index. New in this
+   * library; the reference runs its dense head above 10 rows
+   * (flash_head.py:292-301). */
+  const void *cluster_w16;
+  const void *centroid_w16;
 } fh_head_desc;
 
 /* fh_head_desc.flags */

@@ -1,0 +1,131 @@
+"""Batched decode steps (16 or more rows): tensor-core stage-1 GEMM, the
+selection kernel, the inverted cluster -> rows index and the inverted stage 2.
+
+Parity is checked the same way as for the other paths: probe sets equal the
+oracle's top-p up to near-ties of the p-th score, and each row's token is the
+oracle's argmax over the kernel's own probe set (ties to the smallest id) up
+to the logit tolerance. Sampling is compared draw for draw with the oracle's
+Gumbel-top-p / Gumbel-max restatement keyed by (seed, offset, row, id).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from headutil import OracleView, build_head, check_greedy_rows, to_np_f32
+from oracle import flashhead_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def llama1b_heads(config_a_head):
+    head, meta = config_a_head
+    p = meta["shape"]["n_probes"]
+    return {s: build_head(head.weight, head.centroids, head.assignments, p, stage1=s)
+            for s in ("model", "fp8")}
+
+
+def _tiny_head(K, cap, D, seed=0):
+    from flash_head.synthetic import HeadShape, make_head
+    return make_head(HeadShape(hidden=D, vocab=K * cap, n_clusters=K, cluster_size=cap), seed=seed)
+
+
+def _batched_kernel_count(nh, rows, sample=False):
+    n = nh.step_kernel_count(rows, sample)
+    assert n > 3, f"{rows} rows did not take the batched path ({n} launches)"
+    return n
+
+
+@pytest.mark.parametrize("rows", [16, 64, 256])
+@pytest.mark.parametrize("stage1", ["fp8", "model"])
+def test_batched_matches_oracle(llama1b_heads, rows, stage1):
+    from flash_head.synthetic import make_hidden
+    fh = llama1b_heads[stage1]
+    nh = fh.native()
+    _batched_kernel_count(nh, rows)
+    H = make_hidden(rows, fh._D, seed=900 + rows, device="cuda")
+    toks = nh.next_token(H).cpu().numpy()
+    probes = nh.top_clusters(H).cpu().numpy()
+    check_greedy_rows(fh, H, toks, probes)
+    assert nh.workspace_error() == 0
+    # a second call on the same workspace (index and accumulator reset)
+    toks2 = nh.next_token(H).cpu().numpy()
+    assert np.array_equal(toks, toks2)
+
+
+@pytest.mark.parametrize("K,cap,D,p,rows", [(100, 16, 512, 100, 17), (37, 4, 1024, 5, 20),
+                                            (513, 8, 256, 40, 33), (300, 16, 4096, 64, 24),
+                                            (4097, 16, 128, 200, 64)])
+def test_batched_shapes(K, cap, D, p, rows):
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(K, cap, D)
+    for stage1 in ("model", "fp8"):
+        fh = build_head(head.weight, head.centroids, head.assignments, p, stage1=stage1)
+        nh = fh.native()
+        _batched_kernel_count(nh, rows)
+        H = make_hidden(rows, D, seed=rows, device="cuda")
+        toks = nh.next_token(H).cpu().numpy()
+        check_greedy_rows(fh, H, toks, nh.top_clusters(H).cpu().numpy())
+        assert nh.workspace_error() == 0
+
+
+def test_batched_special_tokens():
+    """Special tokens compete with every row's candidates; one far outside
+    the probed clusters still wins for a row aimed at it."""
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(256, 16, 512, seed=3)
+    specials = [0, 17, 4095]
+    fh = build_head(head.weight, head.centroids, head.assignments, 12, specials=specials,
+                    stage1="model")
+    nh = fh.native()
+    ov = OracleView(fh)
+    H = make_hidden(20, 512, seed=41, device="cuda")
+    H[7] = torch.from_numpy(ov.W[4095] * 50).to("cuda", torch.bfloat16)
+    Hn = to_np_f32(H)
+    probes = nh.top_clusters(H).cpu().numpy()
+    toks = nh.next_token(H).cpu().numpy()
+    for r in range(H.shape[0]):
+        want = ov.greedy_given_probes(Hn[r], probes[r])
+        assert O.token_within_tolerance(toks[r], want, lambda v: ov.logit(Hn[r], v), 1e-5), r
+    assert toks[7] == 4095
+
+
+@pytest.mark.parametrize("stage1", ["model", "fp8"])
+def test_batched_sampling_matches_oracle_draw_for_draw(stage1):
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(256, 16, 512, seed=8)
+    fh = build_head(head.weight, head.centroids, head.assignments, 12, stage1=stage1)
+    nh = fh.native()
+    _batched_kernel_count(nh, 16, sample=True)
+    ov = OracleView(fh)
+    H = make_hidden(16, 512, seed=5, device="cuda", std=4.0)
+    Hn = to_np_f32(H)
+    cd = ov.sw * (ov.sscale[:, None] if ov.sscale is not None else 1.0)
+    n, agree = 0, 0
+    for off in range(12):
+        toks = nh.next_token(H, do_sample=True, temperature=0.7, seed=77, offset=off).cpu().numpy()
+        for r in range(16):
+            want = O.sample_token(Hn[r], ov.w_perm, ov.vm, cd, ov.p, 0.7, 77, off, r)[0]
+            agree += int(toks[r] == want)
+            n += 1
+    assert agree >= 0.98 * n, (agree, n)
+
+
+def test_batched_step_replays_in_a_cuda_graph(llama1b_heads):
+    from flash_head.synthetic import make_hidden
+    fh = llama1b_heads["fp8"]
+    nh = fh.native()
+    H = make_hidden(64, fh._D, seed=3, device="cuda")
+    want = nh.next_token(H).clone()  # first call: plans and workspace exist before capture
+    out = torch.empty(64, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        nh.next_token(H, out=out)
+    for _ in range(3):
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
