@@ -26,6 +26,8 @@
 
 namespace fh {
 
+// From 16 rows; 5..15 rows take the three-kernel path, which streams each
+// row's clusters with more memory-level parallelism at that size.
 constexpr int kBatchMinRows = 16;
 constexpr int kInvRows = 8;          // hidden rows per item (two mma column sets)
 constexpr int kInvThreads = kFThreads;
@@ -64,6 +66,149 @@ __global__ void k_score_epilogue(float *scores, int stride, int rows, int K, con
     if (do_sample) v = v / temperature + gumbel(rng, kStageClusters, (uint32_t)r, (uint32_t)k);
     p[u] = v;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Top-p clusters of one row per CTA (1024 threads): the same rule as k_select
+// (the p largest (score, -id) keys, ids ascending) found with two 8-bit
+// histogram levels over the monotone key (bf16 resolution), an exact rank of
+// the threshold bucket's few keys (a radix select over the remaining 48 key
+// bits when the bucket is large), and one ordered compaction.
+// Dynamic shared memory: K floats (the row) + 32 warp histograms of 256 bins.
+// ---------------------------------------------------------------------------
+constexpr int kHSelThreads = 1024;
+constexpr int kHSelWarps = kHSelThreads / 32;
+constexpr int kHSelBkt = 256;  // bucket keys ranked directly
+
+struct HSelSmem {
+  __align__(16) uint32_t hist[256];
+  unsigned long long bkt[kHSelBkt];
+  int n_bkt;
+  int bin, above, cnt;
+  unsigned long long T;
+  int warp_counts[kHSelWarps];
+};
+
+__host__ __device__ __forceinline__ size_t hsel_row_bytes(int K) {
+  return ((size_t)K * sizeof(float) + 15) / 16 * 16;
+}
+__host__ __device__ __forceinline__ size_t hsel_smem_bytes(int K) {
+  return hsel_row_bytes(K) + (size_t)kHSelWarps * 256 * sizeof(uint32_t) + sizeof(HSelSmem);
+}
+
+__global__ void __launch_bounds__(kHSelThreads) k_select_hist(const float *scores, int stride, int K,
+                                                               int p, int32_t *probes) {
+  extern __shared__ __align__(16) unsigned char hsm[];
+  float *sc = reinterpret_cast<float *>(hsm);
+  uint32_t *wh = reinterpret_cast<uint32_t *>(hsm + hsel_row_bytes(K));  // [32][256]
+  HSelSmem &S = *reinterpret_cast<HSelSmem *>(hsm + hsel_row_bytes(K) +
+                                              (size_t)kHSelWarps * 256 * sizeof(uint32_t));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
+  for (int i = tid; i < kHSelWarps * 256; i += kHSelThreads) wh[i] = 0u;
+  if (tid < 256) S.hist[tid] = 0u;
+  if (tid == 0) S.n_bkt = 0;
+  const float *row = scores + (size_t)r * stride;
+  for (int k = tid; k < K; k += kHSelThreads) sc[k] = sanitize(__ldcg(&row[k]));
+  __syncthreads();
+  // level 1: coarse bins (key >> 24), one private histogram per warp
+  for (int k = tid; k < K; k += kHSelThreads) atomicAdd(&wh[warp * 256 + (mono(sc[k]) >> 24)], 1u);
+  __syncthreads();
+  if (tid < 256) {
+    uint32_t t = 0;
+    for (int w = 0; w < kHSelWarps; ++w) t += wh[w * 256 + tid];
+    S.hist[tid] = t;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int b, above, cnt;
+    warp_find_bin<false>(S.hist, p, b, above, cnt);
+    if (lane == 0) {
+      S.bin = b;
+      S.above = above;
+    }
+  }
+  __syncthreads();
+  const uint32_t cb = (uint32_t)S.bin;
+  const int above1 = S.above;
+  if (tid < 256) S.hist[tid] = 0u;
+  __syncthreads();
+  // level 2: fine bins ((key >> 16) & 255) of the coarse bin
+  for (int k = tid; k < K; k += kHSelThreads) {
+    const uint32_t m = mono(sc[k]);
+    if ((m >> 24) == cb) atomicAdd(&S.hist[(m >> 16) & 255u], 1u);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int b, above, cnt;
+    warp_find_bin<false>(S.hist, p - above1, b, above, cnt);
+    if (lane == 0) {
+      S.bin = b;
+      S.above = above;
+      S.cnt = cnt;
+    }
+  }
+  __syncthreads();
+  const uint32_t P = (cb << 8) | (uint32_t)S.bin;  // 16-bit bucket prefix
+  const int need = p - above1 - S.above;
+  // bucket keys
+  if (need > 0)
+    for (int k = tid; k < K; k += kHSelThreads) {
+      const float v = sc[k];
+      if ((mono(v) >> 16) == P) {
+        const int m = atomicAdd(&S.n_bkt, 1);
+        if (m < kHSelBkt) S.bkt[m] = pack(v, (uint32_t)k);
+      }
+    }
+  __syncthreads();
+  const int nb = S.n_bkt;
+  if (need <= 0) {
+    if (tid == 0) S.T = P >= 0xFFFFu ? ~0ull : (unsigned long long)(P + 1u) << 48;
+  } else if (nb <= kHSelBkt) {
+    if (tid == 0) S.T = (unsigned long long)P << 48;  // fewer keys than needed: the whole bucket
+    __syncthreads();
+    for (int j = tid; j < nb; j += kHSelThreads) {
+      const unsigned long long mine = S.bkt[j];
+      int rank = 0;
+      for (int m = 0; m < nb; ++m) rank += S.bkt[m] > mine;
+      if (rank == need - 1) S.T = mine;
+    }
+  } else {
+    // large bucket: radix select of the need-th largest key over the low 48 bits
+    unsigned long long pre = (unsigned long long)P << 48;
+    int nd = need;
+    for (int shift = 40; shift >= 0; shift -= 8) {
+      if (tid < 256) S.hist[tid] = 0u;
+      __syncthreads();
+      const unsigned long long hi_sel = pre >> (shift + 8);
+      for (int k = tid; k < K; k += kHSelThreads) {
+        const unsigned long long key = pack(sc[k], (uint32_t)k);
+        if ((key >> (shift + 8)) == hi_sel) atomicAdd(&S.hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        int b, above, cnt;
+        warp_find_bin<false>(S.hist, nd, b, above, cnt);
+        if (lane == 0) {
+          S.bin = b;
+          S.above = above;
+        }
+      }
+      __syncthreads();
+      pre |= (unsigned long long)S.bin << shift;
+      nd -= S.above;
+      __syncthreads();
+    }
+    if (tid == 0) S.T = pre;
+  }
+  __syncthreads();
+  const unsigned long long T = S.T;
+  int32_t *out = probes + (size_t)r * p;
+  block_ordered_compact(
+      K, [&](int k) { return pack(sc[k], (uint32_t)k) >= T; },
+      [&](int pos, int k) {
+        if (pos < p) out[pos] = k;
+      },
+      S.warp_counts);
 }
 
 // ---------------------------------------------------------------------------

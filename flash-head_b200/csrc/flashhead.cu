@@ -565,6 +565,22 @@ int get_plan(const fh_head *h, int rows, bool sample, int stride, const LtPlan *
   return FH_OK;
 }
 
+cudaError_t prepare_select_hist() {
+  static bool done[128];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(fh::k_select_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)fh::hsel_smem_bytes(fh::kSelMaxItems));
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t prepare_inv_build() {
   static bool done[128];
   int dev = 0;
@@ -629,12 +645,10 @@ int run_batched_stage1(const fh_head *h, const void *hidden, int rows, bool samp
                            rng_key(seed, offset)),
                     "stage-1 epilogue launch");
   if (!probes) return FH_OK;
-  FH_CHECK_LAUNCH(prepare_select(), "select kernel attribute");
-  fh::SelectArgs se = select_dense_args(d, scores, stride, rows);
-  se.probes = probes;
-  se.wait_prior = 0;
-  FH_CHECK_LAUNCH(launch(fh::k_select, dim3(rows), dim3(fh::kSelThreads),
-                         (size_t)K * sizeof(unsigned long long), s, false, se),
+  FH_CHECK_LAUNCH(prepare_select_hist(), "select kernel attribute");
+  FH_CHECK_LAUNCH(launch(fh::k_select_hist, dim3(rows), dim3(fh::kHSelThreads),
+                         fh::hsel_smem_bytes(K), s, false, (const float *)scores, stride, K,
+                         d.n_probes, probes),
                   "probe selection launch");
   return FH_OK;
 }
