@@ -55,10 +55,20 @@ def derive_buffers(w_perm: torch.Tensor, vocab_maps: torch.Tensor, cluster_w: to
             bufs["cluster_w"], bufs["centroid_w"] = cw, raw
             bufs["cluster_scale"] = bufs["centroid_scale"] = None
             bufs["cluster_w16"], bufs["centroid_w16"] = cw, raw
-        inv = torch.empty_like(flat)
-        inv[flat] = torch.arange(flat.numel(), device=dev)
+        # Slots of the special tokens: the vocab ids need not be a permutation
+        # of [0, K*cap) (a tensor-parallel shard holds a subset of the vocab).
         sp = special_ids.to(device=dev, dtype=torch.int64)
-        bufs["special_slots"] = inv[sp].to(torch.int32).contiguous() if sp.numel() else None
+        if sp.numel():
+            span = max(int(flat.max()), int(sp.max())) + 1
+            inv = torch.full((span,), -1, dtype=torch.int64, device=dev)
+            inv[flat] = torch.arange(flat.numel(), device=dev)
+            slots = inv[sp]
+            if bool((slots < 0).any()):
+                raise ValueError("special token ids missing from the vocab maps: "
+                                 f"{sp[slots < 0].tolist()}")
+            bufs["special_slots"] = slots.to(torch.int32).contiguous()
+        else:
+            bufs["special_slots"] = None
     return bufs
 
 

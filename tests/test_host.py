@@ -132,6 +132,28 @@ def test_derive_and_shard_buffers(golden_small):
         assert int(bufs["vocab_map"][lo * 16 + s]) in (7, 2047)
 
 
+def test_derive_buffers_of_a_shard_slice(golden_small):
+    """A tensor-parallel shard derives its buffers from its clusters alone,
+    whose vocab ids are a subset of the vocabulary, not a permutation of
+    [0, K_shard * cap)."""
+    from flash_head.native import derive_buffers
+    g = golden_small
+    W = torch.from_numpy(g["weight_bits"].view(np.int16)).view(torch.bfloat16)
+    vm = torch.from_numpy(g["ref_vocab_maps"])
+    w_perm = W[vm.reshape(-1)].view(128, 16, 64)
+    cw = torch.from_numpy(O_norm(g["centroids"]))
+    craw = torch.from_numpy(g["centroids"])
+    sl = slice(64, 128)
+    part = derive_buffers(w_perm[sl], vm[sl], cw[sl], craw[:, sl], torch.zeros(0, dtype=torch.int64),
+                          "fp8")
+    assert part["special_slots"] is None and part["w_perm"].shape == (64 * 16, 64)
+    inside = int(vm[100, 3])
+    part = derive_buffers(w_perm[sl], vm[sl], cw[sl], craw[:, sl], torch.tensor([inside]), "fp8")
+    assert part["special_slots"].tolist() == [(100 - 64) * 16 + 3]
+    with pytest.raises(ValueError, match="missing"):
+        derive_buffers(w_perm[sl], vm[sl], cw[sl], craw[:, sl], torch.tensor([int(vm[3, 0])]), "fp8")
+
+
 def O_norm(centroids):
     from oracle import flashhead_oracle as O
     return O.normalized_cluster_weight(centroids)
