@@ -440,6 +440,57 @@ __device__ __forceinline__ RowThreshold warp_find_bucket(const uint32_t *h, int 
   return t;
 }
 
+// Large threshold bucket of row r (more keys than the direct rank list holds):
+// radix select of the need-th largest key, 8 bits per pass over the 48 key
+// bits below the bucket prefix, then a recount of the selected keys per
+// 128-cluster chunk. All threads of the block call it; kept out of line so the
+// common path does not jump over its code.
+template <typename SmemT>
+__device__ __noinline__ void fused_radix_row(SmemT &S, const float *row_s, int K, int r, int nch) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned long long pre = (unsigned long long)S.thr[r].prefix << 48;
+  int need = S.thr[r].need;
+  for (int shift = 40; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) S.rhist[i] = 0u;
+    __syncthreads();
+    const unsigned long long hi_sel = pre >> (shift + 8);
+    for (int k = tid; k < K; k += blockDim.x) {
+      const unsigned long long key = pack(sanitize(row_s[k]), (uint32_t)k);
+      if ((key >> (shift + 8)) == hi_sel) atomicAdd(&S.rhist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int bin, above, cnt;
+      warp_find_bin<false>(S.rhist, need, bin, above, cnt);
+      if (lane == 0) {
+        S.rsel_bin = bin;
+        S.rsel_above = above;
+      }
+    }
+    __syncthreads();
+    pre |= (unsigned long long)S.rsel_bin << shift;
+    need -= S.rsel_above;
+    __syncthreads();  // rsel_* and rhist are reused by the next pass
+  }
+  if (warp < kFWarps) {
+    const float4 *row4 = reinterpret_cast<const float4 *>(row_s);
+    for (int ch = warp; ch < nch; ch += kFWarps) {
+      const int k0 = (ch << 7) + 4 * lane;
+      int cnt = 0;
+      if (k0 < K) {
+        const float4 v4 = row4[k0 >> 2];
+        const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) cnt += k0 + u < K && pack(sanitize(v[u]), (uint32_t)(k0 + u)) >= pre;
+      }
+      cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+      if (lane == 0) S.chunk_sel[r][ch] = cnt;
+    }
+  }
+  if (tid == 0) S.tkey[r] = pre;
+  __syncthreads();
+}
+
 __device__ __forceinline__ const char *wp_bytes(const FusedArgs &a) {
   return reinterpret_cast<const char *>(a.w_perm);
 }
@@ -463,24 +514,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   const int gq = lane >> 2, tq = lane & 3, odd = gq & 1;  // mma fragment coordinates
   uint32_t phase = 0u;  // compute warps: parity of each slot's next mbarrier completion
   FH_TRACE_INIT()
-  if (tid == 0) {
-    for (int s = 0; s < kMaxSlots; ++s) mbar_init(&S.mbar[s], 1);
-    fence_mbar_init();
-    S.s_err = 0u;
-    S.n_work = 0;
-  }
-  if (tid < kFMaxRows) {
-    S.best[tid] = 0ull;
-    S.bkt_n[tid] = 0;
-  }
-  for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFBlock) S.coarse[i] = 0u;
-  __syncthreads();
   FH_STAMP(0);
-
-  const uint32_t epoch = __ldcg(&a.sync[kSyncEpoch]);
-  unsigned char *buf_cur = a.epoch_bufs + (size_t)(epoch & 1u) * kEpochBufBytes;
-  unsigned char *buf_nxt = a.epoch_bufs + (size_t)((epoch + 1u) & 1u) * kEpochBufBytes;
-  uint32_t *hist_cur = reinterpret_cast<uint32_t *>(buf_cur);
 
   // ------------------------------------------------------------------ stage 1
   // slice bounds in 32 bits: the host keeps K <= 128 * G, so b * K < 2^32
@@ -515,11 +549,29 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
         bulk_g2s(dst + (size_t)r * g1.pitch, src + (size_t)r * rb1, (uint32_t)cb, &S.mbar[s]);
     }
   };
-  if (producer) {
-    if (lane == 0)
-      for (int c = 0; c < min(g1.n_slots, n1); ++c) issue1(c);
-    FH_STAMP_P(15);
-  } else {
+  // The first copies go out before anything else: producer lane 0 initialises
+  // the mbarriers itself; the other threads wait on them only after the block
+  // barrier below.
+  if (producer && lane == 0) {
+    for (int s = 0; s < kMaxSlots; ++s) mbar_init(&S.mbar[s], 1);
+    fence_mbar_init();
+    for (int c = 0; c < min(g1.n_slots, n1); ++c) issue1(c);
+  }
+  FH_STAMP_P(15);
+  if (tid == 0) {
+    S.s_err = 0u;
+    S.n_work = 0;
+  }
+  if (tid < kFMaxRows) {
+    S.best[tid] = 0ull;
+    S.bkt_n[tid] = 0;
+  }
+  for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFBlock) S.coarse[i] = 0u;
+  const uint32_t epoch = __ldcg(&a.sync[kSyncEpoch]);
+  unsigned char *buf_cur = a.epoch_bufs + (size_t)(epoch & 1u) * kEpochBufBytes;
+  unsigned char *buf_nxt = a.epoch_bufs + (size_t)((epoch + 1u) & 1u) * kEpochBufBytes;
+  uint32_t *hist_cur = reinterpret_cast<uint32_t *>(buf_cur);
+  if (!producer) {
     if (tid < nc) S.scale[tid] = a.cscale ? a.cscale[c0 + tid] : 1.f;
     // hidden rows as mma B operands (16-bit) in shared memory, 16 bytes per
     // thread and load (one round trip for R * D <= 4096)
@@ -542,16 +594,10 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
       }
     }
     for (int i = tid; i < n_items; i += kFThreads) S.work[i] = 0xFFFFFFFFu;  // empty until set
-    if (tid == 0) S.n_work = n_items;
-    // Zero this CTA's share of the histograms the next call will use.
-    constexpr int n4 = (int)(kEpochBufBytes / 16);
-    uint4 *z = reinterpret_cast<uint4 *>(buf_nxt);
-    const int z1 = (int)((long long)(b + 1) * n4 / G);
-    for (int i = (int)((long long)b * n4 / G) + tid; i < z1; i += kFThreads)
-      z[i] = make_uint4(0, 0, 0, 0);
     FH_STAMP(16);
   }
   __syncthreads();
+  if (tid == 0) S.n_work = n_items;
   FH_STAMP(17);
 
   FH_TICK_DECL
@@ -603,6 +649,12 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
         for (int c = c0r; c < min(c0r + g1.n_slots, n1); ++c) issue1(c);
       __syncwarp();
     }
+    // Zero this CTA's share of the histograms the next call will use (32-bit
+    // bounds: b * n4 < 2^32 for G <= 1024).
+    constexpr uint32_t n4 = (uint32_t)(kEpochBufBytes / 16);
+    uint4 *z = reinterpret_cast<uint4 *>(buf_nxt);
+    const uint32_t z0 = (uint32_t)b * n4 / (uint32_t)G, z1 = (uint32_t)(b + 1) * n4 / (uint32_t)G;
+    for (uint32_t i = z0 + lane; i < z1; i += 32) z[i] = make_uint4(0, 0, 0, 0);
   }
   __syncthreads();
   FH_STAMP(7);
@@ -792,53 +844,10 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   }
   __syncthreads();
   FH_STAMP(12);
-  // Large buckets (rare): radix select of the need-th largest key, 8 bits per
-  // pass over the 48 key bits below the bucket prefix, then a recount of the
-  // selected keys per chunk.
+  // Large buckets (rare, out of line): exact threshold key and chunk counts.
   for (int r = 0; r < a.rows; ++r) {
     if (S.thr[r].need <= 0 || S.bkt_n[r] <= kBktCap) continue;  // block-uniform
-    unsigned long long pre = (unsigned long long)S.thr[r].prefix << 48;
-    int need = S.thr[r].need;
-    for (int shift = 40; shift >= 0; shift -= 8) {
-      for (int i = tid; i < 256; i += kFBlock) S.rhist[i] = 0u;
-      __syncthreads();
-      const unsigned long long hi_sel = pre >> (shift + 8);
-      for (int k = tid; k < a.K; k += kFBlock) {
-        const unsigned long long key = pack(sanitize(sc_s[r * Kp + k]), (uint32_t)k);
-        if ((key >> (shift + 8)) == hi_sel) atomicAdd(&S.rhist[(key >> shift) & 255u], 1u);
-      }
-      __syncthreads();
-      if (warp == 0) {
-        int bin, above, cnt;
-        warp_find_bin<false>(S.rhist, need, bin, above, cnt);
-        if (lane == 0) {
-          S.rsel_bin = bin;
-          S.rsel_above = above;
-        }
-      }
-      __syncthreads();
-      pre |= (unsigned long long)S.rsel_bin << shift;
-      need -= S.rsel_above;
-      __syncthreads();  // rsel_* and rhist are reused by the next pass
-    }
-    if (!producer) {
-      const float4 *row4 = reinterpret_cast<const float4 *>(sc_s + r * Kp);
-      for (int ch = warp; ch < nch; ch += kFWarps) {
-        const int k0 = (ch << 7) + 4 * lane;
-        int cnt = 0;
-        if (k0 < a.K) {
-          const float4 v4 = row4[k0 >> 2];
-          const float v[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            cnt += k0 + u < a.K && pack(sanitize(v[u]), (uint32_t)(k0 + u)) >= pre;
-        }
-        cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
-        if (lane == 0) S.chunk_sel[r][ch] = cnt;
-      }
-    }
-    if (tid == 0) S.tkey[r] = pre;
-    __syncthreads();
+    fused_radix_row(S, sc_s + r * Kp, a.K, r, nch);
   }
   FH_STAMP(13);
   // Warp r, row r: the threshold key (keys above the bucket plus the `need`
