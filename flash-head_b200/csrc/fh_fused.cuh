@@ -567,6 +567,11 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
     S.bkt_n[tid] = 0;
   }
   for (int i = tid; i < kFMaxRows * kHistCoarse; i += kFBlock) S.coarse[i] = 0u;
+  // Inputs and workspace may come from the previous kernel in the stream
+  // (programmatic dependent launch): wait for it here, after the first
+  // weight copies are in flight, and let the next step be scheduled.
+  grid_dep_wait();
+  grid_dep_launch();
   const uint32_t epoch = __ldcg(&a.sync[kSyncEpoch]);
   unsigned char *buf_cur = a.epoch_bufs + (size_t)(epoch & 1u) * kEpochBufBytes;
   unsigned char *buf_nxt = a.epoch_bufs + (size_t)((epoch + 1u) & 1u) * kEpochBufBytes;

@@ -128,10 +128,29 @@ cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream
   cfg.blockDim = dim3(fh::kFBlock);
   cfg.dynamicSmemBytes = fh::fused_smem_bytes(R, a.D, (int)sizeof(WT));
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  // Cooperative (all CTAs resident: the grid barrier needs it) and, where
+  // the runtime accepts the pair, programmatic dependent launch: the step may
+  // start streaming its stage-1 rows while the previous kernel in the stream
+  // drains; it reads the hidden states and the workspace only after
+  // griddepcontrol.wait.
+  static int pdl_ok[128];  // 0 unknown, 1 accepted, -1 rejected
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
+  if (pdl_ok[dev] >= 0) {
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e == cudaSuccess) {
+      pdl_ok[dev] = 1;
+      return e;
+    }
+    if (pdl_ok[dev] == 1) return e;
+    (void)cudaGetLastError();  // the pair is not supported here: launch without PDL
+    pdl_ok[dev] = -1;
+  }
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
