@@ -310,25 +310,19 @@ def measure_dense(head, rows, steps, dist, hidden_pool):
 
 
 def measure_e2e(reps, rows, steps, warmup, dist, D):
-    """Through the C-ABI call with host buffers: per step, pinned host -> device
-    copy of the hidden states, fh_get_next_token, device -> pinned host copy of
-    the ids, stream sync."""
+    """Through the C-ABI call with host buffers (fh_get_next_token_host): per
+    step the library copies the pinned host hidden states to the device, runs
+    the step, copies the ids to pinned host memory and synchronises."""
     import torch
 
     from flash_head.synthetic import make_hidden
     n_host = 8
     host_h = [make_hidden(rows, D, seed=9000 + i).pin_memory() for i in range(n_host)]
     host_out = torch.empty(rows, dtype=torch.int64).pin_memory()
-    dev_h = torch.empty((rows, D), dtype=torch.bfloat16, device="cuda")
-    dev_out = torch.empty(rows, dtype=torch.int64, device="cuda")
-    stream = torch.cuda.current_stream()
     R = len(reps)
 
     def one(i):
-        dev_h.copy_(host_h[i % n_host], non_blocking=True)
-        reps[i % R].next_token(dev_h, out=dev_out)
-        host_out.copy_(dev_out, non_blocking=True)
-        stream.synchronize()
+        reps[i % R].next_token_host(host_h[i % n_host], out_host=host_out)
 
     for i in range(warmup):
         one(i)
@@ -489,7 +483,7 @@ def run_flashhead(args, dist):
         "sweep": sweep,
         "e2e": {"value": rows * dist.world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "us_per_step": e2e_s * 1e6,
-                "path": "C-ABI fh_get_next_token with pinned host buffers, sync per step"},
+                "path": "C-ABI fh_get_next_token_host: pinned host buffers, copies and stream sync inside the call"},
         "gpu_launches": launches * args.steps,
         "step_kernels": launches,
         "clocks": clocks,

@@ -867,6 +867,49 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
   return FH_OK;
 }
 
+namespace {
+size_t host_staging_bytes(const fh_head *head, int rows) {
+  return round_up((size_t)rows * head->d.hidden * 2, 256) + round_up((size_t)rows * 8, 256);
+}
+}  // namespace
+
+FH_API size_t fh_workspace_bytes_host(const fh_head *head, int rows) {
+  if (!head || rows < 0) return 0;
+  return round_up(layout(head->d, rows, nullptr, 0).bytes, 256) + host_staging_bytes(head, rows);
+}
+
+FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, int rows,
+                                  int64_t *out_ids_host, void *workspace, size_t workspace_bytes,
+                                  fh_stream_t stream) {
+  if (!head) return fail(FH_ERR_INVALID_ARGUMENT, "null head");
+  if (rows < 0) return fail(FH_ERR_INVALID_ARGUMENT, "rows=%d < 0", rows);
+  if (rows == 0) return FH_OK;
+  if (!hidden_host || !out_ids_host) return fail(FH_ERR_INVALID_ARGUMENT, "null host buffer");
+  if (!workspace) return fail(FH_ERR_WORKSPACE, "null workspace");
+  const size_t need = fh_workspace_bytes_host(head, rows);
+  if (workspace_bytes < need)
+    return fail(FH_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed for %d host rows",
+                workspace_bytes, need, rows);
+  // staging at the end of the workspace; the step's own layout below it
+  const size_t stage = host_staging_bytes(head, rows);
+  const size_t inner = (workspace_bytes / 256) * 256 - stage;
+  char *base = reinterpret_cast<char *>(workspace);
+  void *dev_h = base + inner;
+  int64_t *dev_out = reinterpret_cast<int64_t *>(base + inner +
+                                                 round_up((size_t)rows * head->d.hidden * 2, 256));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  FH_CHECK_LAUNCH(cudaMemcpyAsync(dev_h, hidden_host, (size_t)rows * head->d.hidden * 2,
+                                  cudaMemcpyHostToDevice, s),
+                  "hidden-state copy to the device");
+  const int st = fh_get_next_token(head, dev_h, rows, dev_out, workspace, inner, stream);
+  if (st != FH_OK) return st;
+  FH_CHECK_LAUNCH(cudaMemcpyAsync(out_ids_host, dev_out, (size_t)rows * sizeof(int64_t),
+                                  cudaMemcpyDeviceToHost, s),
+                  "id copy to the host");
+  FH_CHECK_LAUNCH(cudaStreamSynchronize(s), "stream synchronisation");
+  return FH_OK;
+}
+
 FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int rows,
                                     float temperature, uint64_t seed, uint64_t offset,
                                     int64_t *out_ids, void *workspace, size_t workspace_bytes,

@@ -83,6 +83,8 @@ SIGNATURES = {
     "fh_step_kernel_count": (_I, [_P, _I, _I]),
     "fh_get_next_token": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "fh_get_next_token_noalloc": (_I, [_P, _P, _I, _P, _P]),
+    "fh_get_next_token_host": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
+    "fh_workspace_bytes_host": (_SZ, [_P, _I]),
     "fh_get_next_token_sample": (_I, [_P, _P, _I, _F, _U64, _U64, _P, _P, _SZ, _P]),
     "fh_top_clusters": (_I, [_P, _P, _I, _I, _F, _U64, _U64, _P, _P, _P, _SZ, _P]),
     "fh_cluster_scores": (_I, [_P, _P, _I, _I, _F, _U64, _U64, _P, _P]),

@@ -150,9 +150,12 @@ class NativeHead:
     def workspace_bytes(self, rows: int) -> int:
         return int(self.lib.fh_workspace_bytes(self.handle, rows))
 
-    def workspace(self, rows: int) -> torch.Tensor:
+    def workspace(self, rows: int, host: bool = False) -> torch.Tensor:
+        """This device's workspace, grown (zero-filled) to serve `rows` rows;
+        `host`: sized for fh_get_next_token_host (device staging included)."""
         idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
-        need = self.workspace_bytes(rows)
+        need = (int(self.lib.fh_workspace_bytes_host(self.handle, rows)) if host
+                else self.workspace_bytes(rows))
         ws = self._ws.get(idx)
         if ws is None or ws.numel() < need:
             # zero-filled: fh_stage2_next_token expects a clean accumulator
@@ -202,6 +205,23 @@ class NativeHead:
             _lib.call("fh_get_next_token", self.handle, h.data_ptr(), n, out.data_ptr(),
                       ws.data_ptr(), ws.numel(), s)
         return out
+
+    def next_token_host(self, hidden_host: torch.Tensor, out_host: Optional[torch.Tensor] = None):
+        """Greedy ids with host buffers through fh_get_next_token_host:
+        [N, D] CPU hidden states (pinned for asynchronous copies) -> [N] int64
+        CPU ids; returns after the ids are on the host."""
+        h = hidden_host.contiguous()
+        if h.device.type != "cpu" or h.dtype != self.dtype:
+            raise ValueError(f"expected a CPU {self.dtype} tensor, got {h.device} {h.dtype}")
+        n = h.shape[0]
+        if out_host is None:
+            out_host = torch.empty(n, dtype=torch.int64, pin_memory=True)
+        if n == 0:
+            return out_host
+        ws = self.workspace(n, host=True)
+        _lib.call("fh_get_next_token_host", self.handle, h.data_ptr(), n, out_host.data_ptr(),
+                  ws.data_ptr(), ws.numel(), _lib.stream_ptr())
+        return out_host
 
     def top_clusters(self, hidden, do_sample=False, temperature=1.0, seed=0, offset=0,
                      return_scores=False):

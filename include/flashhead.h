@@ -140,7 +140,10 @@ FH_API size_t fh_workspace_error_offset(void);
 /*
  * Kernel launches one fh_get_next_token / fh_get_next_token_sample call makes
  * for `rows` hidden states on the current device: 1 when the one-kernel step
- * applies (rows <= 4 and supported shapes), else 3.
+ * applies (rows <= 4 and supported shapes), 3 for the three stage kernels
+ * (5..15 rows, or unsupported shapes), and 10 to 11 for batched steps (16+
+ * rows with cluster_w16 / centroid_w16: GEMM, selection, inverted index,
+ * inverted stage 2).
  */
 FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample);
 
@@ -154,6 +157,21 @@ FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample);
 FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
                              int64_t *out_ids, void *workspace,
                              size_t workspace_bytes, fh_stream_t stream);
+
+/*
+ * Greedy next token with HOST buffers: hidden_host [rows, hidden] (page-locked
+ * host memory keeps the copies asynchronous), out_ids_host [rows] int64. The
+ * call copies the hidden states to the device, runs fh_get_next_token on the
+ * workspace, copies the ids back and synchronises `stream` before returning.
+ * For C and C++ callers that keep the decode state on the host; the
+ * reference's get_next_token (flash_head.py:277-334) takes device tensors.
+ * The workspace must hold fh_workspace_bytes_host(head, rows) bytes (the
+ * device staging of inputs and ids sits at its end).
+ */
+FH_API size_t fh_workspace_bytes_host(const fh_head *head, int rows);
+FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, int rows,
+                                  int64_t *out_ids_host, void *workspace,
+                                  size_t workspace_bytes, fh_stream_t stream);
 
 /*
  * Greedy next token WITHOUT a workspace argument; nothing is allocated. No

@@ -372,6 +372,19 @@ def test_tp_shards_reproduce_unsharded(llama1b_heads, world, do_sample):
     assert torch.equal(ids, whole)
 
 
+def test_host_buffer_entry_point(llama1b_heads):
+    """fh_get_next_token_host (pinned host in, host ids out, synchronised on
+    return) gives the ids of fh_get_next_token on the same rows."""
+    from flash_head.synthetic import make_hidden
+    nh = llama1b_heads["fp8"].native()
+    for rows in (1, 3, 7, 20):
+        H = make_hidden(rows, nh.D, seed=800 + rows)
+        got = nh.next_token_host(H.pin_memory())
+        want = nh.next_token(H.to("cuda")).cpu()
+        assert got.device.type == "cpu" and torch.equal(got, want), rows
+    assert nh.next_token_host(H[:0]).numel() == 0
+
+
 def test_workspace_reuse_across_row_counts(llama1b_heads):
     """One workspace serves calls with any row count: stage 2 alone (which
     relies on the accumulator left zeroed by earlier calls) matches the full
