@@ -316,13 +316,25 @@ def measure_e2e(reps, rows, steps, warmup, dist, D):
     import torch
 
     from flash_head.synthetic import make_hidden
+    from flash_head import _lib
     n_host = 8
     host_h = [make_hidden(rows, D, seed=9000 + i).pin_memory() for i in range(n_host)]
     host_out = torch.empty(rows, dtype=torch.int64).pin_memory()
     R = len(reps)
+    # The C function bound once, its arguments resolved up front: per step the
+    # host makes exactly the library call a C caller would make.
+    fn = reps[0].lib.fh_get_next_token_host
+    stream = _lib.stream_ptr()
+    wss = [r.workspace(rows, host=True) for r in reps]
+    args = [(reps[j].handle, wss[j].data_ptr(), wss[j].numel()) for j in range(R)]
+    hp = [h.data_ptr() for h in host_h]
+    op = host_out.data_ptr()
 
     def one(i):
-        reps[i % R].next_token_host(host_h[i % n_host], out_host=host_out)
+        handle, wp, wn = args[i % R]
+        st = fn(handle, hp[i % n_host], rows, op, wp, wn, stream)
+        if st != 0:
+            raise RuntimeError(_lib.last_error())
 
     for i in range(warmup):
         one(i)

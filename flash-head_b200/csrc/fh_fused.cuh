@@ -497,6 +497,33 @@ __device__ __noinline__ void fused_radix_row(SmemT &S, const float *row_s, int K
   __syncthreads();
 }
 
+// Pass A of one row with monotone integer keys (bucket bounds at zero or
+// non-finite values, where float order and key order differ): per 128-cluster
+// chunk the keys above the bucket, and the bucket's keys. Compute warps only.
+template <typename SmemT>
+__device__ __noinline__ void fused_pass_a_keys(SmemT &S, const float *row_s, int K, int r, int nch,
+                                               uint32_t P, bool want) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t thrA = P >= 0xFFFFu ? 0xFFFFFFFFu : (P + 1u) << 16;
+  const uint32_t bktLo = P << 16;
+  for (int ch = warp; ch < nch; ch += kFWarps) {
+    int cnt = 0;
+    for (int u = 0; u < 4; ++u) {
+      const int k = (ch << 7) + 4 * lane + u;
+      if (k >= K) break;
+      const float x = sanitize(row_s[k]);
+      const uint32_t m = mono(x);
+      cnt += m >= thrA;
+      if (want && m - bktLo < 65536u) {
+        const int slot = atomicAdd(&S.bkt_n[r], 1);
+        if (slot < kBktCap) S.bkt[r][slot] = pack(x, (uint32_t)k);
+      }
+    }
+    cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+    if (lane == 0) S.chunk_sel[r][ch] = cnt;
+  }
+}
+
 __device__ __forceinline__ const char *wp_bytes(const FusedArgs &a) {
   return reinterpret_cast<const char *>(a.w_perm);
 }
@@ -761,21 +788,20 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   float *sc_s = reinterpret_cast<float *>(ring);  // [rows][Kp]
   const int Kp = (a.K + 3) & ~3;
   if (warp >= kFMaxRows && !producer) {
-    const int nv = a.rows * (Kp / 4), t0 = tid - kFMaxRows * 32;
+    const int t0 = tid - kFMaxRows * 32, n4 = Kp / 4;
     constexpr int nt = kFThreads - kFMaxRows * 32;
-    for (int i = t0; i < nv; i += 8 * nt) {
-      float4 v[8];
+    for (int r = 0; r < a.rows; ++r) {
+      const float4 *src = reinterpret_cast<const float4 *>(a.scores + (size_t)r * a.score_stride);
+      float4 *dst = reinterpret_cast<float4 *>(sc_s + (size_t)r * Kp);
+      for (int c = t0; c < n4; c += 4 * nt) {
+        float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = i + u * nt;
-        if (j < nv) {
-          const int r = j / (Kp / 4), cc = j - r * (Kp / 4);
-          v[u] = __ldcg(reinterpret_cast<const float4 *>(a.scores + (size_t)r * a.score_stride) + cc);
-        }
+        for (int u = 0; u < 4; ++u)
+          if (c + u * nt < n4) v[u] = __ldcg(src + c + u * nt);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c + u * nt < n4) dst[c + u * nt] = v[u];
       }
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (i + u * nt < nv) reinterpret_cast<float4 *>(sc_s)[i + u * nt] = v[u];
     }
   } else if (warp < a.rows) {
     const float te = S.t_est[warp];
@@ -812,7 +838,12 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
       const float X = unmono(thrA), Xlo = unmono(bktLo);
       const bool fast = P < 0xFFFFu && isfinite(X) && X != 0.f && isfinite(Xlo) && Xlo != 0.f;
       const bool want = S.thr[r].need > 0;
-      const float4 *row4 = reinterpret_cast<const float4 *>(sc_s + r * Kp);
+      const float *row_s = sc_s + r * Kp;
+      const float4 *row4 = reinterpret_cast<const float4 *>(row_s);
+      if (!fast) {  // zero or non-finite bucket bounds (rare): integer keys, out of line
+        fused_pass_a_keys(S, sc_s + r * Kp, a.K, r, nch, P, want);
+        continue;
+      }
       for (int ch0 = warp; ch0 < nch; ch0 += 4 * kFWarps) {
         float v[4][4];
 #pragma unroll
@@ -834,18 +865,9 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const bool ok = k0 + u < a.K;
-            bool above, in;
-            if (fast) {
-              const float x = v[j][u];
-              above = x >= X;
-              in = x >= Xlo && x < X;
-            } else {
-              const uint32_t m = mono(sanitize(v[j][u]));
-              above = m >= thrA;
-              in = m - bktLo < 65536u;
-            }
-            cnt[j] += ok && above;
-            inb |= (uint32_t)(ok && in) << (4 * j + u);
+            const float x = v[j][u];
+            cnt[j] += ok && x >= X;
+            inb |= (uint32_t)(ok && x >= Xlo && x < X) << (4 * j + u);
           }
         }
 #pragma unroll
@@ -856,13 +878,13 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
             if (ch0 + j * kFWarps < nch) S.chunk_sel[r][ch0 + j * kFWarps] = cnt[j];
         }
         if (want && __any_sync(0xFFFFFFFFu, inb != 0u)) {
-          for (int bit = 0; bit < 16; ++bit)
-            if ((inb >> bit) & 1u) {
-              const int j = bit >> 2, u = bit & 3;
-              const int k = ((ch0 + j * kFWarps) << 7) + 4 * lane + u;
-              const int m = atomicAdd(&S.bkt_n[r], 1);
-              if (m < kBktCap) S.bkt[r][m] = pack(sanitize(v[j][u]), (uint32_t)k);
-            }
+#pragma unroll 1
+          for (uint32_t m = inb; m != 0u; m &= m - 1u) {
+            const int bit = __ffs(m) - 1, j = bit >> 2, u = bit & 3;
+            const int k = ((ch0 + j * kFWarps) << 7) + 4 * lane + u;
+            const int slot = atomicAdd(&S.bkt_n[r], 1);
+            if (slot < kBktCap) S.bkt[r][slot] = pack(row_s[k], (uint32_t)k);
+          }
         }
       }
     }

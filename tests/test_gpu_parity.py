@@ -379,9 +379,11 @@ def test_host_buffer_entry_point(llama1b_heads):
     nh = llama1b_heads["fp8"].native()
     for rows in (1, 3, 7, 20):
         H = make_hidden(rows, nh.D, seed=800 + rows)
-        got = nh.next_token_host(H.pin_memory())
         want = nh.next_token(H.to("cuda")).cpu()
+        got = nh.next_token_host(H.pin_memory())
         assert got.device.type == "cpu" and torch.equal(got, want), rows
+        paged = nh.next_token_host(H.clone(), out_host=torch.empty(rows, dtype=torch.int64))
+        assert torch.equal(paged, want), rows  # pageable buffers work too (synchronous copies)
     assert nh.next_token_host(H[:0]).numel() == 0
 
 
