@@ -56,6 +56,9 @@ constexpr int kMaxS1Chunks = 8;  // stage-1 chunks of one CTA (each with its own
 // be selected: more would compete for HBM with CTAs still streaming stage 1
 // (measured: margin -1 is ~1.5 us faster per step than +0.25).
 constexpr float kPrefetchMargin = -1.0f;
+// Bulk copies per stage-2 cluster: four copies of 4 rows complete sooner than
+// one of 16 (measured ~0.4 us per step at batch 1).
+constexpr int kS2Pieces = 4;
 constexpr int kRingBytes = 128 * 1024;
 constexpr int kMaxSlots = 4;
 constexpr int kTileRows = 16;
@@ -1039,7 +1042,11 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
       unsigned char *dst = ring + (size_t)s * g3.slot_bytes;
       const char *src = wp + (size_t)d.src * rb3 + (size_t)d.dc * g3.cb;
       if (g3.ndc == 1) {
-        bulk_g2s(dst, src, (uint32_t)(d.n * rb3), &S.mbar[s]);
+        // the rows as kS2Pieces copies of whole rows (copies proceed in parallel)
+        const int per = (d.n + kS2Pieces - 1) / kS2Pieces;
+        for (int r0 = 0; r0 < d.n; r0 += per)
+          bulk_g2s(dst + (size_t)r0 * rb3, src + (size_t)r0 * rb3,
+                   (uint32_t)(min(per, d.n - r0) * rb3), &S.mbar[s]);
       } else {
         for (int r = 0; r < d.n; ++r)
           bulk_g2s(dst + (size_t)r * g3.pitch, src + (size_t)r * rb3, (uint32_t)cb, &S.mbar[s]);
