@@ -428,7 +428,10 @@ __global__ void __launch_bounds__(kInvBlock, 1) k_stage2_inv(InvArgs a) {
         unsigned char *dst = ring + (size_t)s * kInvSlotBytes;
         const char *wsrc = wp + (size_t)src * rb + (size_t)d.dc * cb_max;
         if (ndc == 1) {
-          bulk_g2s(dst, wsrc, (uint32_t)(a.cap * rb), &S.mbar[s]);
+          const int per = (a.cap + kS2Pieces - 1) / kS2Pieces;  // rows per bulk copy
+          for (int r0 = 0; r0 < a.cap; r0 += per)
+            bulk_g2s(dst + (size_t)r0 * rb, wsrc + (size_t)r0 * rb,
+                     (uint32_t)(min(per, a.cap - r0) * rb), &S.mbar[s]);
         } else {
           for (int r = 0; r < a.cap; ++r)
             bulk_g2s(dst + (size_t)r * pitch, wsrc + (size_t)r * rb, (uint32_t)cb, &S.mbar[s]);
