@@ -309,6 +309,21 @@ def measure_dense(head, rows, steps, dist, hidden_pool):
     return time_graph(g, dist) / steps
 
 
+def measure_library_dense(reps, rows, steps, dist, hidden_pool):
+    """The library's exact dense head (fh_dense_next_token: tensor-core GEMMs
+    against K-row blocks of w_perm + block argmax), rotating head replicas."""
+    import torch
+    Hs = [h[:rows].contiguous() for h in hidden_pool]
+    for r in reps:
+        r.workspace(rows)
+    outs = [torch.empty(rows, dtype=torch.int64, device="cuda") for _ in range(steps)]
+    R = len(reps)
+    g = capture([(lambda i=i: reps[i % R].dense_next_token(Hs[i % len(Hs)], out=outs[i]))
+                 for i in range(steps)])
+    g.replay()
+    return time_graph(g, dist) / steps
+
+
 def measure_e2e(reps, rows, steps, warmup, dist, D):
     """Through the C-ABI call with host buffers (fh_get_next_token_host): per
     step the library copies the pinned host hidden states to the device, runs
@@ -465,6 +480,9 @@ def run_flashhead(args, dist):
                           "frac_hbm": (a1 + a3) / r["step_s"] / 1e9 / peak,
                           "stage1_us": r["s1_s"] * 1e6, "stage2_us": r["s3_s"] * 1e6,
                           "dense_us_per_step": d * 1e6, "speedup_vs_dense": d / r["step_s"]})
+            if b >= 16:  # the library's exact dense head (the reference's branch above 10 rows)
+                ld = measure_library_dense(reps, b, args.steps, dist, hidden_pool)
+                sweep[-1].update({"library_dense_us": ld * 1e6, "library_dense_vs_dense": d / ld})
 
     e2e_s, h2d, d2h = measure_e2e(reps, rows, args.steps, args.warmup, dist, shape.hidden)
 

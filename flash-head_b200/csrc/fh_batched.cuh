@@ -609,6 +609,27 @@ __global__ void k_special_scores(const void *hidden, int rows, int D, const void
   }
 }
 
+// Dense head on the tensor cores: the vocabulary is cap blocks of K w_perm
+// rows; block j's logits [rows, K] (a GEMM into the score scratch) fold into
+// packed[row] as (logit or Gumbel key, vocab id). Grid (rows, splits).
+__global__ void k_dense_block_argmax(const float *logits, int stride, int rows, int K,
+                                    const int32_t *vocab_map, int slot0, int do_sample,
+                                    float temperature, RngKey rng, unsigned long long *packed) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const float *row = logits + (size_t)r * stride;
+  unsigned long long best = 0ull;
+  for (int k = blockIdx.y * blockDim.x + threadIdx.x; k < K; k += gridDim.y * blockDim.x) {
+    const uint32_t vid = (uint32_t)__ldg(&vocab_map[slot0 + k]);
+    float key = sanitize(__ldcg(&row[k]));
+    if (do_sample) key = key / temperature + gumbel(rng, kStageTokens, (uint32_t)r, vid);
+    const unsigned long long w = pack(key, vid);
+    best = w > best ? w : best;
+  }
+  best = warp_max_u64(best);
+  if ((threadIdx.x & 31) == 0 && best) atomicMax(&packed[r], best);
+}
+
 __global__ void k_inv_finalize(unsigned long long *packed, int rows, int64_t *out_ids) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) {
     const unsigned long long w = packed[i];

@@ -9,6 +9,7 @@
 #include <cublasLt.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cmath>
@@ -173,9 +174,10 @@ cudaError_t launch_fused(int hdt, int wdt, const fh::FusedArgs &a, int grid, cud
 
 }  // namespace
 
-// cuBLASLt objects of one batched stage-1 GEMM shape (rows x matrix).
+// cuBLASLt objects of one GEMM shape: `rows` hidden states against `mat`
+// rows of a [*, D] weight matrix (the centroids, or blocks of w_perm).
 struct LtPlan {
-  int rows = 0, stride = 0;
+  int rows = 0, stride = 0, mat = 0;
   bool sample = false;
   cublasLtMatmulDesc_t op = nullptr;
   cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
@@ -195,6 +197,21 @@ struct fh_head {
 namespace {
 
 constexpr size_t kLtWorkspaceBytes = 8u << 20;  // cuBLASLt scratch of the batched GEMM
+constexpr size_t kDenseScratchBytes = 64u << 20;  // logits of one dense GEMM (rows >= 16)
+
+// Dense head of a batched call: the cap K-row blocks of w_perm are multiplied
+// in GEMMs of `blocks` blocks each (as many as fit kDenseScratchBytes of f32
+// logits, balanced over the GEMMs); `stride` is the logits row pitch.
+struct DenseSplit {
+  int blocks, gemms, stride;
+};
+DenseSplit dense_split(const fh_head_desc &d, int rows) {
+  const size_t per_block = (size_t)rows * d.n_clusters * sizeof(float);
+  int g = (int)std::min<size_t>((size_t)d.cluster_size, std::max<size_t>(1, kDenseScratchBytes / per_block));
+  const int gemms = (d.cluster_size + g - 1) / g;
+  g = (d.cluster_size + gemms - 1) / gemms;
+  return DenseSplit{g, gemms, (int)round_up((size_t)g * d.n_clusters, 64)};
+}
 
 struct Workspace {
   float *scores;                // [rows, score_stride]
@@ -207,6 +224,7 @@ struct Workspace {
   int *inv_cnt, *inv_off, *inv_item_off, *inv_cursor, *inv_meta, *inv_list;
   fh::InvItem *inv_items;
   void *lt_ws;
+  float *dense;                 // [rows, dense stride] logits of the dense GEMMs
   size_t bytes;                 // bytes needed for `rows`
 };
 
@@ -231,8 +249,11 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   const size_t kint = round_up((size_t)d.n_clusters * sizeof(int), 256);
   const size_t n_pairs = (size_t)rows * d.n_probes;
   const size_t max_items = n_pairs / fh::kInvRows + (size_t)d.n_clusters + 1;
+  const size_t dense =
+      batched ? round_up((size_t)rows * dense_split(d, rows).stride * sizeof(float), 256) : 0;
   const size_t inv = batched ? 4 * kint + 256 + round_up(n_pairs * sizeof(int), 256) +
-                                   round_up(max_items * sizeof(fh::InvItem), 256) + kLtWorkspaceBytes
+                                   round_up(max_items * sizeof(fh::InvItem), 256) +
+                                   kLtWorkspaceBytes + dense
                              : 0;
   w.bytes = state + probes + scores + inv + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
@@ -246,8 +267,11 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   w.inv_cnt = w.inv_off = w.inv_item_off = w.inv_cursor = w.inv_meta = w.inv_list = nullptr;
   w.inv_items = nullptr;
   w.lt_ws = nullptr;
+  w.dense = nullptr;
   if (batched) {
     size_t q = scores_off >= inv ? scores_off - inv : 0;
+    w.dense = reinterpret_cast<float *>(p + q);
+    q += dense;
     w.lt_ws = p + q;
     q += kLtWorkspaceBytes;
     w.inv_items = reinterpret_cast<fh::InvItem *>(p + q);
@@ -520,10 +544,10 @@ void destroy_plan(LtPlan &pl) {
 
 // S^T (K x rows, column-major, ld = score_stride) = Wc (K x D) . H^T (D x rows):
 // the row-major [K, D] matrix is a column-major D x K operand taken transposed.
-int get_plan(const fh_head *h, int rows, bool sample, int stride, const LtPlan **out) {
+int get_plan(const fh_head *h, int rows, bool sample, int stride, int mat, const LtPlan **out) {
   std::lock_guard<std::mutex> lock(h->plan_mutex);
   for (const LtPlan &pl : h->plans)
-    if (pl.rows == rows && pl.sample == sample && pl.stride == stride) {
+    if (pl.rows == rows && pl.sample == sample && pl.stride == stride && pl.mat == mat) {
       *out = &pl;
       return FH_OK;
     }
@@ -538,6 +562,7 @@ int get_plan(const fh_head *h, int rows, bool sample, int stride, const LtPlan *
   LtPlan pl;
   pl.rows = rows;
   pl.stride = stride;
+  pl.mat = mat;
   pl.sample = sample;
   const cudaDataType_t dt = d.weight_dtype == FH_BF16 ? CUDA_R_16BF : CUDA_R_16F;
   int st = FH_OK;
@@ -549,9 +574,9 @@ int get_plan(const fh_head *h, int rows, bool sample, int stride, const LtPlan *
     const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
     cublasLtMatmulDescSetAttribute(pl.op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta));
     cublasLtMatmulDescSetAttribute(pl.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb));
-    if (cublasLtMatrixLayoutCreate(&pl.a, dt, d.hidden, d.n_clusters, d.hidden) != CUBLAS_STATUS_SUCCESS ||
+    if (cublasLtMatrixLayoutCreate(&pl.a, dt, d.hidden, mat, d.hidden) != CUBLAS_STATUS_SUCCESS ||
         cublasLtMatrixLayoutCreate(&pl.b, dt, d.hidden, rows, d.hidden) != CUBLAS_STATUS_SUCCESS ||
-        cublasLtMatrixLayoutCreate(&pl.c, CUDA_R_32F, d.n_clusters, rows, stride) !=
+        cublasLtMatrixLayoutCreate(&pl.c, CUDA_R_32F, mat, rows, stride) !=
             CUBLAS_STATUS_SUCCESS) {
       st = fail(FH_ERR_CUDA, "cuBLASLt matrix layouts");
       break;
@@ -570,7 +595,7 @@ int get_plan(const fh_head *h, int rows, bool sample, int stride, const LtPlan *
                                                              pref, 1, &res, &n);
     cublasLtMatmulPreferenceDestroy(pref);
     if (hs != CUBLAS_STATUS_SUCCESS || n < 1) {
-      st = fail(FH_ERR_UNSUPPORTED, "no cuBLASLt algorithm for the %d-row stage-1 GEMM", rows);
+      st = fail(FH_ERR_UNSUPPORTED, "no cuBLASLt algorithm for the %d x %d GEMM", rows, mat);
       break;
     }
     pl.algo = res.algo;
@@ -649,7 +674,7 @@ int run_batched_stage1(const fh_head *h, const void *hidden, int rows, bool samp
                        float *scores, int stride, int32_t *probes, cudaStream_t s) {
   const fh_head_desc &d = h->d;
   const LtPlan *pl = nullptr;
-  int st = get_plan(h, rows, sample, stride, &pl);
+  int st = get_plan(h, rows, sample, stride, h->d.n_clusters, &pl);
   if (st != FH_OK) return st;
   const float alpha = 1.f, beta = 0.f;
   FH_CHECK_LT(cublasLtMatmul(h->lt, pl->op, &alpha, sample ? d.centroid_w16 : d.cluster_w16,
@@ -736,6 +761,46 @@ int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, flo
                              d.special_slots, d.n_special, n_slots, sample ? 1 : 0, temperature,
                              rng, w.packed),
                       "special-token launch");
+  }
+  FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
+                         w.packed, rows, out_ids),
+                  "finalize launch");
+  return FH_OK;
+}
+
+// Dense head for batched calls: GEMMs of the hidden rows against groups of
+// K-row blocks of w_perm into f32 logits, each folded into packed[] by
+// k_dense_block_argmax (the smallest-id tie rule of the packed words), then the
+// ids. The logits are exact f32 dot products of the 16-bit operands.
+bool dense_gemm_ok(const fh_head *h, int rows) {
+  const fh_head_desc &d = h->d;
+  return rows >= fh::kBatchMinRows && !(d.flags & FH_FLAG_NO_FUSED) && d.cluster_base == 0 &&
+         sm_count() > 0;
+}
+
+int run_dense_gemm(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+                   uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
+                   cudaStream_t s) {
+  const fh_head_desc &d = h->d;
+  const DenseSplit sp = dense_split(d, rows);
+  const int K = d.n_clusters;
+  const size_t block_bytes = (size_t)K * d.hidden * 2;
+  const fh::RngKey rng = rng_key(seed, offset);
+  for (int j0 = 0; j0 < d.cluster_size; j0 += sp.blocks) {
+    const int n = (std::min(d.cluster_size, j0 + sp.blocks) - j0) * K;
+    const LtPlan *pl = nullptr;
+    const int st = get_plan(h, rows, false, sp.stride, n, &pl);
+    if (st != FH_OK) return st;
+    const float alpha = 1.f, beta = 0.f;
+    const void *wj = reinterpret_cast<const char *>(d.w_perm) + (size_t)j0 * block_bytes;
+    FH_CHECK_LT(cublasLtMatmul(h->lt, pl->op, &alpha, wj, pl->a, hidden, pl->b, &beta, w.dense,
+                               pl->c, w.dense, pl->c, &pl->algo, w.lt_ws, kLtWorkspaceBytes, s),
+                "dense GEMM");
+    const int splits = std::max(1, std::min(64, (4 * sm_count() + rows - 1) / rows));
+    FH_CHECK_LAUNCH(launch(fh::k_dense_block_argmax, dim3(rows, splits), dim3(256), 0, s, false,
+                           (const float *)w.dense, sp.stride, rows, n, d.vocab_map, j0 * K,
+                           sample ? 1 : 0, temperature, rng, w.packed),
+                    "dense argmax launch");
   }
   FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
                          w.packed, rows, out_ids),
@@ -1030,6 +1095,9 @@ FH_API int fh_dense_next_token(const fh_head *head, const void *hidden, int rows
     return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
+  if (dense_gemm_ok(head, rows))
+    return run_dense_gemm(head, hidden, rows, do_sample != 0, temperature, seed, offset, out_ids, w,
+                          s);
   FH_CHECK_LAUNCH(launch(fh::k_fill_u64, dim3((rows + 255) / 256), dim3(256), 0, s, false,
                          w.packed, rows, 0ull),
                   "fill launch");

@@ -266,10 +266,12 @@ class NativeHead:
                       out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
         return out
 
-    def dense_next_token(self, hidden, do_sample=False, temperature=1.0, seed=0, offset=0):
+    def dense_next_token(self, hidden, do_sample=False, temperature=1.0, seed=0, offset=0,
+                         out=None):
         h = self._h(hidden)
         n = h.shape[0]
-        out = torch.empty(n, dtype=torch.int64, device=self.device)
+        if out is None:
+            out = torch.empty(n, dtype=torch.int64, device=self.device)
         if n:
             ws = self.workspace(n)
             _lib.call("fh_dense_next_token", self.handle, h.data_ptr(), n, int(bool(do_sample)),
