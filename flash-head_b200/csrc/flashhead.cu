@@ -7,6 +7,7 @@
 // dependent launch so that their CTAs are resident before their predecessor
 // finishes.
 #include <cublasLt.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -21,6 +22,7 @@
 
 #include "../../include/flashhead.h"
 #include "fh_batched.cuh"
+#include "fh_dense_tc.cuh"
 
 namespace {
 
@@ -189,6 +191,8 @@ struct fh_head {
   mutable cublasLtHandle_t lt = nullptr;  // created by the first batched call
   mutable std::mutex plan_mutex;  // the plan cache fills on first use of a row count
   mutable std::vector<LtPlan> plans;
+  mutable CUtensorMap tm_w;  // w_perm rows for the dense tensor-core kernel
+  mutable int tm_w_tile = 0;  // its box height, 0: not encoded yet
 };
 
 // ---------------------------------------------------------------------------
@@ -768,6 +772,127 @@ int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, flo
   return FH_OK;
 }
 
+// cuTensorMapEncodeTiled from the driver, resolved once through the runtime
+// (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D map of a row-major [n_rows, D] 16-bit matrix: boxes of box_rows rows x
+// 64 elements (128 bytes), 128-byte swizzle, zero fill outside the matrix.
+bool encode_rows_map(CUtensorMap *tm, const void *base, int dtype, int D, long long n_rows,
+                     int box_rows) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc || !aligned16(base)) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)n_rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)fh::kDtKBlock, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return enc(tm,
+             dtype == FH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+             2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tiling of the dense tensor-core kernel: vocab tiles of n_tile slots (a
+// multiple of 16, at most 256) sized so the tiles split evenly over the SMs.
+struct DenseTcPlan {
+  int n_tile, n_tiles, mt, stages, grid;
+  size_t smem;
+};
+bool dense_tc_plan(const fh_head_desc &d, int rows, DenseTcPlan *p) {
+  const long long G = sm_count();
+  const long long V = (long long)d.n_clusters * d.cluster_size;
+  if (G <= 0 || rows < 1 || rows > fh::kDtMaxRows || V < 1 || V > (1ll << 30)) return false;
+  const long long t = (V + G * fh::kDtMaxTile - 1) / (G * fh::kDtMaxTile);
+  long long n = 16 * ((V + 16 * G * t - 1) / (16 * G * t));
+  n = std::min<long long>(std::max<long long>(n, 16), fh::kDtMaxTile);
+  p->n_tile = (int)n;
+  p->n_tiles = (int)((V + n - 1) / n);
+  p->mt = rows > fh::kDtMTile ? 2 : 1;
+  const size_t sb = fh::dense_tc_stage_bytes(p->mt, p->n_tile);
+  const size_t avail = (size_t)fh::kDtSmemMax - 1024 - sizeof(fh::DenseTcCtrl);
+  p->stages = (int)std::min<size_t>((size_t)fh::kDtMaxStages, avail / sb);
+  if (p->stages < 2) return false;
+  p->smem = fh::dense_tc_smem_bytes(p->mt, p->n_tile, p->stages);
+  p->grid = (int)std::min<long long>(G, p->n_tiles);
+  return true;
+}
+
+cudaError_t prepare_dense_tc() {
+  static bool done[128];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(fh::k_dense_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fh::kDtSmemMax);
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
+
+// Greedy dense head in one tensor-core kernel (logits stay on chip). Returns
+// FH_ERR_UNSUPPORTED without launching anything when the shape or the tensor
+// maps do not fit it; the caller then takes the GEMM + argmax route.
+int run_dense_tc(const fh_head *h, const void *hidden, int rows, int64_t *out_ids,
+                 const Workspace &w, cudaStream_t s) {
+  const fh_head_desc &d = h->d;
+  DenseTcPlan pl;
+  if ((d.flags & FH_FLAG_NO_FUSED) || d.cluster_base != 0 || !dense_tc_plan(d, rows, &pl))
+    return FH_ERR_UNSUPPORTED;
+  const long long V = (long long)d.n_clusters * d.cluster_size;
+  CUtensorMap tm_w, tm_h;
+  {
+    std::lock_guard<std::mutex> lock(h->plan_mutex);
+    if (h->tm_w_tile != pl.n_tile) {
+      if (!encode_rows_map(&h->tm_w, d.w_perm, d.weight_dtype, d.hidden, V, pl.n_tile))
+        return FH_ERR_UNSUPPORTED;
+      h->tm_w_tile = pl.n_tile;
+    }
+    tm_w = h->tm_w;
+  }
+  if (!encode_rows_map(&tm_h, hidden, d.weight_dtype, d.hidden, rows, fh::kDtMTile))
+    return FH_ERR_UNSUPPORTED;
+  FH_CHECK_LAUNCH(prepare_dense_tc(), "dense tensor-core kernel attribute");
+  fh::DenseTcArgs a;
+  a.rows = rows;
+  a.V = (int)V;
+  a.n_tile = pl.n_tile;
+  a.n_tiles = pl.n_tiles;
+  a.mt = pl.mt;
+  a.stages = pl.stages;
+  a.nk = (d.hidden + fh::kDtKBlock - 1) / fh::kDtKBlock;
+  a.idesc = fh::dense_tc_idesc(d.weight_dtype == FH_BF16, pl.n_tile);
+  a.vocab_map = d.vocab_map;
+  a.packed = w.packed;
+  a.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
+  a.polls = 1u << 22;
+  FH_CHECK_LAUNCH(launch(fh::k_dense_tc, dim3(pl.grid), dim3(fh::kDtThreads), pl.smem, s, false,
+                         tm_h, tm_w, a),
+                  "dense tensor-core launch");
+  FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
+                         w.packed, rows, out_ids),
+                  "finalize launch");
+  return FH_OK;
+}
+
 // Dense head for batched calls: GEMMs of the hidden rows against groups of
 // K-row blocks of w_perm into f32 logits, each folded into packed[] by
 // k_dense_block_argmax (the smallest-id tie rule of the packed words), then the
@@ -782,6 +907,10 @@ int run_dense_gemm(const fh_head *h, const void *hidden, int rows, bool sample, 
                    uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
                    cudaStream_t s) {
   const fh_head_desc &d = h->d;
+  if (!sample) {
+    const int st = run_dense_tc(h, hidden, rows, out_ids, w, s);
+    if (st != FH_ERR_UNSUPPORTED) return st;
+  }
   const DenseSplit sp = dense_split(d, rows);
   const int K = d.n_clusters;
   const size_t block_bytes = (size_t)K * d.hidden * 2;

@@ -151,3 +151,41 @@ def test_dense_gemm_path_is_the_exact_argmax(llama1b_heads, rows):
     a = nh.dense_next_token(H, do_sample=True, temperature=0.8, seed=3, offset=1)
     b = nh.dense_next_token(H, do_sample=True, temperature=0.8, seed=3, offset=1)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("rows", [128, 129, 256])
+def test_dense_tensor_core_kernel_row_tiles(llama1b_heads, rows):
+    """Greedy dense head in one tcgen05 kernel (csrc/fh_dense_tc.cuh): one
+    128-row hidden tile (double-buffered accumulators), a second tile holding
+    one row, and two full tiles. Every row's token is the fp32 argmax over the
+    whole vocabulary (plain PyTorch fp32 reference of the same w_perm and
+    vocab map) up to 1e-5-relative logit ties; a spread of rows is also
+    checked against the oracle's float64 dense argmax."""
+    from flash_head.synthetic import make_hidden
+    fh = llama1b_heads["fp8"]
+    nh = fh.native()
+    H = make_hidden(rows, fh._D, seed=1400 + rows, device="cuda")
+    toks = nh.dense_next_token(H)
+    torch.cuda.synchronize()
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        again = nh.dense_next_token(H)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert any("k_dense_tc" in n for n in names), names
+    assert torch.equal(toks, again)
+    wp, vm = nh.bufs["w_perm"], nh.bufs["vocab_map"].long()
+    logits = torch.empty(rows, wp.shape[0], dtype=torch.float32, device="cuda")
+    for j0 in range(0, wp.shape[0], 16384):  # fp32 reference, by vocab blocks
+        logits[:, j0:j0 + 16384] = H.float() @ wp[j0:j0 + 16384].float().t()
+    best = logits.max(dim=1).values
+    slot_of = torch.empty_like(vm)
+    slot_of[vm] = torch.arange(vm.numel(), device="cuda")
+    mine = logits.gather(1, slot_of[toks].view(-1, 1)).view(-1)
+    gap = (best - mine).abs() / best.abs().clamp_min(1e-30)
+    assert bool((gap <= 1e-5).all()), (int(gap.argmax()), float(gap.max()))
+    ov = OracleView(fh)
+    Hn = to_np_f32(H)
+    for r in sorted({0, 1, 127, min(128, rows - 1), rows - 1}):
+        want = O.dense_argmax(Hn[r], ov.W)
+        assert O.token_within_tolerance(int(toks[r]), want, lambda v: ov.logit(Hn[r], v), 1e-5), r
