@@ -310,8 +310,9 @@ def measure_dense(head, rows, steps, dist, hidden_pool):
 
 
 def measure_library_dense(reps, rows, steps, dist, hidden_pool):
-    """The library's exact dense head (fh_dense_next_token: tensor-core GEMMs
-    against K-row blocks of w_perm + block argmax), rotating head replicas."""
+    """The library's exact dense head (fh_dense_next_token; greedy from 16 rows:
+    one tcgen05 GEMM + argmax kernel and the id publish), rotating head
+    replicas."""
     import torch
     Hs = [h[:rows].contiguous() for h in hidden_pool]
     for r in reps:
@@ -480,9 +481,18 @@ def run_flashhead(args, dist):
                           "frac_hbm": (a1 + a3) / r["step_s"] / 1e9 / peak,
                           "stage1_us": r["s1_s"] * 1e6, "stage2_us": r["s3_s"] * 1e6,
                           "dense_us_per_step": d * 1e6, "speedup_vs_dense": d / r["step_s"]})
-            if b >= 16:  # the library's exact dense head (the reference's branch above 10 rows)
+            # FlashHead.get_next_token runs the dense head above 10 rows
+            # (flash_head.py:292-301): the library's tcgen05 dense kernel
+            if b > 10:
                 ld = measure_library_dense(reps, b, args.steps, dist, hidden_pool)
-                sweep[-1].update({"library_dense_us": ld * 1e6, "library_dense_vs_dense": d / ld})
+                sweep[-1].update({"library_dense_us": ld * 1e6, "library_dense_vs_dense": d / ld,
+                                  "get_next_token_path": "dense (more than 10 rows)",
+                                  "get_next_token_us": ld * 1e6,
+                                  "get_next_token_vs_dense": d / ld})
+            else:
+                sweep[-1].update({"get_next_token_path": "probes",
+                                  "get_next_token_us": r["step_s"] * 1e6,
+                                  "get_next_token_vs_dense": d / r["step_s"]})
 
     e2e_s, h2d, d2h = measure_e2e(reps, rows, args.steps, args.warmup, dist, shape.hidden)
 
@@ -578,7 +588,8 @@ def run_reference(args):
 
 def run_profile(args):
     """Small eager run for ncu: one head replica (about 0.6 GB), W warm-up steps,
-    then --profile-steps greedy steps launched one by one (no graphs)."""
+    then --profile-steps greedy steps launched one by one (no graphs); with
+    --profile-path dense the steps are the dense head (fh_dense_next_token)."""
     import torch
 
     from flash_head.synthetic import make_hidden
@@ -589,11 +600,12 @@ def run_profile(args):
     nh = reps[0]
     H = [make_hidden(rows, wl["shape"].hidden, seed=1000 + i, device="cuda") for i in range(8)]
     out = torch.empty(rows, dtype=torch.int64, device="cuda")
+    step = nh.dense_next_token if args.profile_path == "dense" else nh.next_token
     for i in range(args.warmup):
-        nh.next_token(H[i % 8], out=out)
+        step(H[i % 8], out=out)
     torch.cuda.synchronize()
     for i in range(args.profile_steps):
-        nh.next_token(H[i % 8], out=out)
+        step(H[i % 8], out=out)
     torch.cuda.synchronize()
     print(json.dumps({"profile_steps": args.profile_steps, "rows": rows,
                       "workload": workload_label(wl, rows), "last_ids": out.tolist()}))
@@ -611,6 +623,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="eager profiling run (for ncu) instead of the benchmark")
+    ap.add_argument("--profile-path", choices=["step", "dense"], default="step")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

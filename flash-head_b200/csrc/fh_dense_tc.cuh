@@ -5,7 +5,7 @@
 // branch above 10 rows as F.linear over w_perm + argmax
 // (src/flash_head/flash_head.py:292-301).
 //
-// One persistent CTA per SM, 6 warps:
+// One persistent CTA per SM, 10 warps:
 //   warp 0  lane 0 issues TMA tensor copies (128-byte swizzle) of the hidden
 //           tiles (128 rows x 64 elements) and the w_perm tile (n_tile rows x
 //           64 elements) of each k-block into a ring of shared-memory stages;
@@ -13,12 +13,14 @@
 //           (M = 128 hidden rows, N = n_tile vocab slots, K = 16) per k-block
 //           and tcgen05.commit's the stage back to the producer, and the
 //           finished accumulator to the epilogue;
-//   warps 2..5  read the accumulator with tcgen05.ld (warp w owns TMEM lanes
-//           32*(w%4) ..), i.e. each thread one hidden row, and keep that row's
-//           best packed (logit, vocab id) word over the CTA's vocab tiles;
-//           one atomicMax per row at the end.
-// With one 128-row hidden tile the accumulator is double-buffered (columns
-// 0 and 256), so the epilogue of tile i overlaps the MMAs of tile i + 1.
+//   warps 2..9  read the accumulator with tcgen05.ld (warp w owns TMEM lanes
+//           32*(w%4) .., warps 2..5 the first half of the tile's columns,
+//           warps 6..9 the second), i.e. each thread one hidden row, and keep
+//           that row's best packed (logit, vocab id) word over the CTA's vocab
+//           tiles in four independent chains; one atomicMax per row and half
+//           at the end.
+// When n_acc * mt accumulators fit the 512 TMEM columns they are
+// double-buffered, so the epilogue of tile i overlaps the MMAs of tile i + 1.
 // Every wait is bounded; on a timeout the kernel records kErrCopyTimeout,
 // drains its own copies and MMAs (bounded) and frees TMEM before it returns.
 #pragma once
@@ -29,15 +31,23 @@
 
 namespace fh {
 
-constexpr int kDtThreads = 192;
-constexpr int kDtKBlock = 64;                  // 16-bit elements per k-block: one 128-byte row
+constexpr int kDtThreads = 320;
+constexpr int kDtEpiThreads = 256;  // warps 2..9
+// Bytes of a row per k-block: 128 (128-byte swizzle, 64 elements), or 64
+// (64-byte swizzle, stages half the size, twice as many in flight; measured
+// slower on the Llama-3.2-1B head: 92 vs 86 us at 64 rows, 144 vs 134 us at 256).
+#ifndef FH_DT_KBYTES
+#define FH_DT_KBYTES 128
+#endif
+constexpr int kDtKBytes = FH_DT_KBYTES;
+static_assert(kDtKBytes == 64 || kDtKBytes == 128, "k-block of 64 or 128 bytes");
+constexpr int kDtKBlock = kDtKBytes / 2;       // 16-bit elements per k-block
 constexpr int kDtMTile = 128;                  // hidden rows per MMA (TMEM lanes)
-constexpr int kDtATileBytes = kDtMTile * 128;  // 16 KB
+constexpr int kDtATileBytes = kDtMTile * kDtKBytes;
 constexpr int kDtMaxRows = 2 * kDtMTile;
 constexpr int kDtMaxTile = 256;                // vocab slots per tile (MMA N)
-constexpr int kDtMaxStages = 8;
+constexpr int kDtMaxStages = 12;
 constexpr int kDtTmemCols = 512;
-constexpr int kDtAccStride = 256;              // TMEM columns between accumulators
 constexpr int kDtSmemMax = 227 * 1024;
 
 struct DenseTcArgs {
@@ -48,6 +58,8 @@ struct DenseTcArgs {
   int mt;        // 128-row hidden tiles: 1 or 2
   int stages;
   int nk;        // k-blocks: ceil(D / 64)
+  int n_acc;     // accumulator sets (2: the epilogue overlaps the next tile's MMAs)
+  int acc_stride;  // TMEM columns per accumulator (>= n_tile); n_acc*mt*acc_stride <= 512
   uint32_t idesc;
   const int32_t *vocab_map;
   unsigned long long *packed;  // [rows], max-folded
@@ -67,7 +79,7 @@ struct DenseTcCtrl {
 };
 
 __host__ __device__ inline size_t dense_tc_stage_bytes(int mt, int n_tile) {
-  return (size_t)mt * kDtATileBytes + (size_t)n_tile * 128;
+  return (size_t)mt * kDtATileBytes + (size_t)n_tile * kDtKBytes;
 }
 __host__ __device__ inline size_t dense_tc_smem_bytes(int mt, int n_tile, int stages) {
   return 1024 + (size_t)stages * dense_tc_stage_bytes(mt, n_tile) + sizeof(DenseTcCtrl);
@@ -80,14 +92,17 @@ __host__ __device__ inline uint32_t dense_tc_idesc(bool bf16, int n_tile) {
          ((uint32_t)(kDtMTile >> 4) << 24);
 }
 
-// Shared-memory matrix descriptor of a K-major tile written by a 128-byte
-// swizzled TMA copy: rows 128 bytes apart, 8-row groups 1024 bytes apart
-// (stride byte offset), leading byte offset unused (1), descriptor version 1,
-// layout type 2 (128-byte swizzle). The tile base is 1024-byte aligned; the
-// k-th 16-element step inside the 128-byte row adds 32 bytes to the start.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
-         (2ull << 61);
+// Shared-memory matrix descriptor of a K-major tile written by a TMA copy
+// with the k-block's swizzle (64 or 128 bytes): rows kDtKBytes apart, 8-row
+// groups 8 * kDtKBytes apart (stride byte offset), leading byte offset unused
+// (1), descriptor version 1, layout type 4 (64-byte swizzle) or 2 (128-byte).
+// The tile base is 1024-byte aligned; the k-th 16-element step inside the
+// row adds 32 bytes to the start address.
+__device__ __forceinline__ uint64_t umma_desc_k(uint32_t saddr) {
+  constexpr uint64_t layout = kDtKBytes == 128 ? 2ull : 4ull;
+  constexpr uint64_t sbo = (8ull * kDtKBytes) >> 4;
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (sbo << 32) | (1ull << 46) |
+         (layout << 61);
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y,
@@ -147,7 +162,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int G = gridDim.x, b = blockIdx.x;
   const int t0 = (int)((long long)b * a.n_tiles / G);
   const int t1 = (int)((long long)(b + 1) * a.n_tiles / G);
-  const int n_acc = a.mt == 1 ? 2 : 1;
+  const int n_acc = a.n_acc;
 
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -156,7 +171,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&S.acc_full[j], 1);
-      mbar_init(&S.acc_empty[j], 128);
+      mbar_init(&S.acc_empty[j], kDtEpiThreads);
     }
     mbar_init(&S.drain, 1);
     S.s_err = 0u;
@@ -221,7 +236,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           }
           tc_fence_after();
         }
-        const uint32_t acc = tmem + (uint32_t)(buf * kDtAccStride);
+        const uint32_t acc = tmem + (uint32_t)(buf * a.mt * a.acc_stride);
         for (int kb = 0; kb < a.nk; ++kb) {
           if (!mbar_wait(&S.full[s], ph, a.polls)) {
             atomicOr(&S.s_err, kErrCopyTimeout);
@@ -230,12 +245,12 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           }
           tc_fence_after();
           const uint32_t st = smem_u32(ring + (size_t)s * sb);
-          const uint64_t bd = umma_desc_sw128(st + (uint32_t)(a.mt * kDtATileBytes));
+          const uint64_t bd = umma_desc_k(st + (uint32_t)(a.mt * kDtATileBytes));
           for (int m = 0; m < a.mt; ++m) {
-            const uint64_t ad = umma_desc_sw128(st + (uint32_t)(m * kDtATileBytes));
+            const uint64_t ad = umma_desc_k(st + (uint32_t)(m * kDtATileBytes));
 #pragma unroll
             for (int k = 0; k < kDtKBlock / 16; ++k)
-              tc_mma_f16(acc + (uint32_t)(m * kDtAccStride), ad + 2u * k, bd + 2u * k, a.idesc,
+              tc_mma_f16(acc + (uint32_t)(m * a.acc_stride), ad + 2u * k, bd + 2u * k, a.idesc,
                          (kb | k) != 0 ? 1u : 0u);
           }
           tc_commit(&S.empty[s]);
@@ -251,15 +266,23 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       if (!mbar_wait(&S.drain, 0u, a.polls)) atomicOr(&S.s_err, kErrCopyTimeout);
     }
   } else {
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;          // TMEM lane quadrant this warp may access
+    const int hf = (warp - 2) >> 2;  // column half of the tile
     const int et = tid - 64;
-    unsigned long long best0 = 0ull, best1 = 0ull;
+    const int nc = a.n_tile >> 4;    // 16-column chunks per tile
+    const int c_lo = hf ? (nc + 1) >> 1 : 0, c_hi = hf ? nc : (nc + 1) >> 1;
+    unsigned long long bst[2][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) bst[m][u] = 0ull;
     bool ok = true;
     for (int t = t0, i = 0; t < t1; ++t, ++i) {
       const int v0 = t * a.n_tile;
       int *vid = S.vid[i & 1];
-      for (int j = et; j < a.n_tile; j += 128) vid[j] = v0 + j < a.V ? __ldg(&a.vocab_map[v0 + j]) : 0;
-      nbar_sync(1, 128);
+      for (int j = et; j < a.n_tile; j += kDtEpiThreads)
+        vid[j] = v0 + j < a.V ? __ldg(&a.vocab_map[v0 + j]) : 0;
+      nbar_sync(1, kDtEpiThreads);
       const int buf = i % n_acc, use = i / n_acc;
       if (ok && !mbar_wait(&S.acc_full[buf], (uint32_t)(use & 1), a.polls)) {
         atomicOr(&S.s_err, kErrCopyTimeout);
@@ -269,34 +292,48 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       if (!ok) continue;
       tc_fence_after();
       const int n_valid = min(a.n_tile, a.V - v0);
-      for (int m = 0; m < a.mt; ++m) {
-        unsigned long long best = m == 0 ? best0 : best1;
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        if (m >= a.mt) break;
         const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) +
-                              (uint32_t)(buf * kDtAccStride + m * kDtAccStride);
-        for (int c = 0; c < a.n_tile; c += 16) {
-          uint32_t v[16];
-          tc_ld16(base + (uint32_t)c, v);
+                              (uint32_t)((buf * a.mt + m) * a.acc_stride);
+        // up to four 16-column loads in flight per wait
+        for (int c = c_lo; c < c_hi; c += 4) {
+          const int nq = min(4, c_hi - c);
+          uint32_t v[4][16];
+          tc_ld16(base + (uint32_t)(16 * c), v[0]);
+          if (nq > 1) tc_ld16(base + (uint32_t)(16 * (c + 1)), v[1]);
+          if (nq > 2) tc_ld16(base + (uint32_t)(16 * (c + 2)), v[2]);
+          if (nq > 3) tc_ld16(base + (uint32_t)(16 * (c + 3)), v[3]);
           tc_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (c + j < n_valid) {
-              const unsigned long long w =
-                  pack(sanitize(__uint_as_float(v[j])), (uint32_t)vid[c + j]);
-              best = w > best ? w : best;
+          for (int u = 0; u < 4; ++u) {
+            if (u < nq) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int col = 16 * (c + u) + j;
+                if (col < n_valid) {
+                  const unsigned long long w =
+                      pack(sanitize(__uint_as_float(v[u][j])), (uint32_t)vid[col]);
+                  bst[m][j & 3] = w > bst[m][j & 3] ? w : bst[m][j & 3];
+                }
+              }
             }
           }
         }
-        if (m == 0)
-          best0 = best;
-        else
-          best1 = best;
       }
       tc_fence_before();
       mbar_arrive_cta(&S.acc_empty[buf]);
     }
     const int r0 = 32 * q + lane;
-    if (r0 < a.rows && best0) atomicMax(&a.packed[r0], best0);
-    if (a.mt > 1 && r0 + kDtMTile < a.rows && best1) atomicMax(&a.packed[r0 + kDtMTile], best1);
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      unsigned long long best = bst[m][0];
+#pragma unroll
+      for (int u = 1; u < 4; ++u) best = bst[m][u] > best ? bst[m][u] : best;
+      const int row = m * kDtMTile + r0;
+      if (m < a.mt && row < a.rows && best) atomicMax(&a.packed[row], best);
+    }
   }
   tc_fence_before();
   __syncthreads();

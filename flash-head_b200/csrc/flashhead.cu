@@ -791,7 +791,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // 2-D map of a row-major [n_rows, D] 16-bit matrix: boxes of box_rows rows x
-// 64 elements (128 bytes), 128-byte swizzle, zero fill outside the matrix.
+// one k-block (kDtKBytes bytes) with the swizzle of that width, zero fill
+// outside the matrix.
 bool encode_rows_map(CUtensorMap *tm, const void *base, int dtype, int D, long long n_rows,
                      int box_rows) {
   const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
@@ -803,26 +804,37 @@ bool encode_rows_map(CUtensorMap *tm, const void *base, int dtype, int D, long l
   return enc(tm,
              dtype == FH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
              2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             fh::kDtKBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Tiling of the dense tensor-core kernel: vocab tiles of n_tile slots (a
 // multiple of 16, at most 256) sized so the tiles split evenly over the SMs.
 struct DenseTcPlan {
-  int n_tile, n_tiles, mt, stages, grid;
+  int n_tile, n_tiles, mt, stages, grid, n_acc, acc_stride;
   size_t smem;
 };
+#ifndef FH_DT_MT2_DOUBLE_BUFFER
+#define FH_DT_MT2_DOUBLE_BUFFER 0
+#endif
 bool dense_tc_plan(const fh_head_desc &d, int rows, DenseTcPlan *p) {
   const long long G = sm_count();
   const long long V = (long long)d.n_clusters * d.cluster_size;
   if (G <= 0 || rows < 1 || rows > fh::kDtMaxRows || V < 1 || V > (1ll << 30)) return false;
-  const long long t = (V + G * fh::kDtMaxTile - 1) / (G * fh::kDtMaxTile);
+  p->mt = rows > fh::kDtMTile ? 2 : 1;
+  // 512 TMEM columns: one hidden tile -> two 256-column accumulators; two
+  // hidden tiles -> one set of two 256-column accumulators, or two sets of
+  // 128 columns (narrower vocab tiles)
+  const bool db = p->mt == 1 || FH_DT_MT2_DOUBLE_BUFFER;
+  p->n_acc = db ? 2 : 1;
+  p->acc_stride = fh::kDtTmemCols / (p->n_acc * p->mt);
+  const long long cap_n = std::min<long long>(fh::kDtMaxTile, p->acc_stride);
+  const long long t = (V + G * cap_n - 1) / (G * cap_n);
   long long n = 16 * ((V + 16 * G * t - 1) / (16 * G * t));
-  n = std::min<long long>(std::max<long long>(n, 16), fh::kDtMaxTile);
+  n = std::min<long long>(std::max<long long>(n, 16), cap_n);
   p->n_tile = (int)n;
   p->n_tiles = (int)((V + n - 1) / n);
-  p->mt = rows > fh::kDtMTile ? 2 : 1;
   const size_t sb = fh::dense_tc_stage_bytes(p->mt, p->n_tile);
   const size_t avail = (size_t)fh::kDtSmemMax - 1024 - sizeof(fh::DenseTcCtrl);
   p->stages = (int)std::min<size_t>((size_t)fh::kDtMaxStages, avail / sb);
@@ -878,6 +890,8 @@ int run_dense_tc(const fh_head *h, const void *hidden, int rows, int64_t *out_id
   a.n_tiles = pl.n_tiles;
   a.mt = pl.mt;
   a.stages = pl.stages;
+  a.n_acc = pl.n_acc;
+  a.acc_stride = pl.acc_stride;
   a.nk = (d.hidden + fh::kDtKBlock - 1) / fh::kDtKBlock;
   a.idesc = fh::dense_tc_idesc(d.weight_dtype == FH_BF16, pl.n_tile);
   a.vocab_map = d.vocab_map;
