@@ -630,6 +630,15 @@ __global__ void k_dense_block_argmax(const float *logits, int stride, int rows, 
   if ((threadIdx.x & 31) == 0 && best) atomicMax(&packed[r], best);
 }
 
+// Copies n16 16-byte words from page-locked host memory into device memory;
+// lets the dependent step launch at once (the step waits for this grid's
+// completion before it reads the copy).
+__global__ void k_stage_in(uint4 *dst, const uint4 *src, int n16) {
+  grid_dep_launch();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
 __global__ void k_inv_finalize(unsigned long long *packed, int rows, int64_t *out_ids) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) {
     const unsigned long long w = packed[i];

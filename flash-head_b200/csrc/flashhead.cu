@@ -1076,6 +1076,17 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
 }
 
 namespace {
+// Device address of a page-locked host buffer (with unified addressing, the
+// same address), or null for pageable memory.
+void *mapped_host(const void *p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
+
 size_t host_staging_bytes(const fh_head *head, int rows) {
   return round_up((size_t)rows * head->d.hidden * 2, 256) + round_up((size_t)rows * 8, 256);
 }
@@ -1106,14 +1117,30 @@ FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, 
   int64_t *dev_out = reinterpret_cast<int64_t *>(base + inner +
                                                  round_up((size_t)rows * head->d.hidden * 2, 256));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  FH_CHECK_LAUNCH(cudaMemcpyAsync(dev_h, hidden_host, (size_t)rows * head->d.hidden * 2,
-                                  cudaMemcpyHostToDevice, s),
-                  "hidden-state copy to the device");
-  const int st = fh_get_next_token(head, dev_h, rows, dev_out, workspace, inner, stream);
+  const size_t hbytes = (size_t)rows * head->d.hidden * 2;
+  // Page-locked host buffers are read and written by the kernels themselves
+  // over the bus (one small copy kernel in, the step's own id stores out),
+  // which costs less latency than two copy-engine transfers; pageable ones
+  // go through cudaMemcpyAsync.
+  const void *h_mapped = mapped_host(hidden_host);
+  if (h_mapped && aligned16(h_mapped) && hbytes % 16 == 0) {
+    const int n16 = (int)(hbytes / 16);
+    FH_CHECK_LAUNCH(launch(fh::k_stage_in, dim3(grid_for(n16, 256)), dim3(256), 0, s, false,
+                           reinterpret_cast<uint4 *>(dev_h),
+                           reinterpret_cast<const uint4 *>(h_mapped), n16),
+                    "hidden-state copy kernel");
+  } else {
+    FH_CHECK_LAUNCH(cudaMemcpyAsync(dev_h, hidden_host, hbytes, cudaMemcpyHostToDevice, s),
+                    "hidden-state copy to the device");
+  }
+  int64_t *o_mapped = reinterpret_cast<int64_t *>(mapped_host(out_ids_host));
+  const int st =
+      fh_get_next_token(head, dev_h, rows, o_mapped ? o_mapped : dev_out, workspace, inner, stream);
   if (st != FH_OK) return st;
-  FH_CHECK_LAUNCH(cudaMemcpyAsync(out_ids_host, dev_out, (size_t)rows * sizeof(int64_t),
-                                  cudaMemcpyDeviceToHost, s),
-                  "id copy to the host");
+  if (!o_mapped)
+    FH_CHECK_LAUNCH(cudaMemcpyAsync(out_ids_host, dev_out, (size_t)rows * sizeof(int64_t),
+                                    cudaMemcpyDeviceToHost, s),
+                    "id copy to the host");
   FH_CHECK_LAUNCH(cudaStreamSynchronize(s), "stream synchronisation");
   return FH_OK;
 }

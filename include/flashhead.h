@@ -159,10 +159,12 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
                              size_t workspace_bytes, fh_stream_t stream);
 
 /*
- * Greedy next token with HOST buffers: hidden_host [rows, hidden] (page-locked
- * host memory keeps the copies asynchronous), out_ids_host [rows] int64. The
- * call copies the hidden states to the device, runs fh_get_next_token on the
- * workspace, copies the ids back and synchronises `stream` before returning.
+ * Greedy next token with HOST buffers: hidden_host [rows, hidden],
+ * out_ids_host [rows] int64. The call brings the hidden states to the device,
+ * runs fh_get_next_token on the workspace, returns the ids and synchronises
+ * `stream` before returning. Page-locked buffers are read and written by the
+ * kernels directly (a small copy kernel in, the step's own id stores out);
+ * pageable ones go through cudaMemcpyAsync.
  * For C and C++ callers that keep the decode state on the host; the
  * reference's get_next_token (flash_head.py:277-334) takes device tensors.
  * The workspace must hold fh_workspace_bytes_host(head, rows) bytes (the
