@@ -1123,7 +1123,9 @@ FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, 
   // which costs less latency than two copy-engine transfers; pageable ones
   // go through cudaMemcpyAsync.
   const void *h_mapped = mapped_host(hidden_host);
-  if (h_mapped && aligned16(h_mapped) && hbytes % 16 == 0) {
+  if (!(h_mapped && aligned16(h_mapped) && hbytes % 16 == 0)) h_mapped = nullptr;
+  int64_t *o_mapped = reinterpret_cast<int64_t *>(mapped_host(out_ids_host));
+  if (h_mapped) {
     const int n16 = (int)(hbytes / 16);
     FH_CHECK_LAUNCH(launch(fh::k_stage_in, dim3(grid_for(n16, 256)), dim3(256), 0, s, false,
                            reinterpret_cast<uint4 *>(dev_h),
@@ -1133,7 +1135,6 @@ FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, 
     FH_CHECK_LAUNCH(cudaMemcpyAsync(dev_h, hidden_host, hbytes, cudaMemcpyHostToDevice, s),
                     "hidden-state copy to the device");
   }
-  int64_t *o_mapped = reinterpret_cast<int64_t *>(mapped_host(out_ids_host));
   const int st =
       fh_get_next_token(head, dev_h, rows, o_mapped ? o_mapped : dev_out, workspace, inner, stream);
   if (st != FH_OK) return st;

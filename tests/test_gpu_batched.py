@@ -153,6 +153,61 @@ def test_dense_gemm_path_is_the_exact_argmax(llama1b_heads, rows):
     assert torch.equal(a, b)
 
 
+def _check_dense_tc(nh, H):
+    """Runs the dense head twice (the second call under the CUDA profiler, to
+    see that the tcgen05 kernel ran), then checks every row's token against
+    the fp32 logits of the same w_perm and vocab map (plain PyTorch fp32
+    reference) up to 1e-5-relative ties. Returns the tokens."""
+    rows = H.shape[0]
+    toks = nh.dense_next_token(H)
+    torch.cuda.synchronize()
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        again = nh.dense_next_token(H)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert any("k_dense_tc" in n for n in names), names
+    assert torch.equal(toks, again)
+    assert nh.workspace_error() == 0
+    wp, vm = nh.bufs["w_perm"], nh.bufs["vocab_map"].long()
+    logits = torch.empty(rows, wp.shape[0], dtype=torch.float32, device="cuda")
+    for j0 in range(0, wp.shape[0], 16384):  # fp32 reference, by vocab blocks
+        logits[:, j0:j0 + 16384] = H.float() @ wp[j0:j0 + 16384].float().t()
+    best = logits.max(dim=1).values
+    slot_of = torch.empty_like(vm)
+    slot_of[vm] = torch.arange(vm.numel(), device="cuda")
+    mine = logits.gather(1, slot_of[toks].view(-1, 1)).view(-1)
+    gap = (best - mine).abs() / best.abs().clamp_min(1e-30)
+    assert bool((gap <= 1e-5).all()), (int(gap.argmax()), float(gap.max()))
+    return toks
+
+
+@pytest.mark.parametrize("K,cap,D,rows,dtype", [
+    (37, 16, 80, 17, torch.bfloat16),      # second k-block 16 of 64 elements; 37 tiles < SMs
+    (513, 8, 1040, 33, torch.float16),     # f16 operands; last vocab tile 8 of 32 slots
+    (300, 16, 4096, 200, torch.bfloat16),  # two hidden tiles, the second 72 of 128 rows
+])
+def test_dense_tensor_core_kernel_shapes(K, cap, D, rows, dtype):
+    """The tcgen05 dense kernel away from the Llama head: hidden sizes that
+    leave a partial last k-block (zero fill of the TMA boxes), vocabularies
+    smaller than the grid and not a multiple of the vocab tile, fp16 weights
+    and hidden states, and row counts that leave most of a 128-row tile
+    empty; checked against the fp32 reference and the oracle's float64
+    argmax on a few rows."""
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(K, cap, D, seed=K)
+    fh = build_head(head.weight, head.centroids, head.assignments, min(K, 16), stage1="model",
+                    dtype=dtype)
+    nh = fh.native()
+    H = make_hidden(rows, D, seed=rows + D, device="cuda").to(dtype)
+    toks = _check_dense_tc(nh, H)
+    ov = OracleView(fh)
+    Hn = to_np_f32(H)
+    for r in (0, rows // 2, rows - 1):
+        want = O.dense_argmax(Hn[r], ov.W)
+        assert O.token_within_tolerance(int(toks[r]), want, lambda v: ov.logit(Hn[r], v), 1e-5), r
+
+
 @pytest.mark.parametrize("rows", [128, 129, 256])
 def test_dense_tensor_core_kernel_row_tiles(llama1b_heads, rows):
     """Greedy dense head in one tcgen05 kernel (csrc/fh_dense_tc.cuh): one
@@ -165,25 +220,7 @@ def test_dense_tensor_core_kernel_row_tiles(llama1b_heads, rows):
     fh = llama1b_heads["fp8"]
     nh = fh.native()
     H = make_hidden(rows, fh._D, seed=1400 + rows, device="cuda")
-    toks = nh.dense_next_token(H)
-    torch.cuda.synchronize()
-    from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        again = nh.dense_next_token(H)
-        torch.cuda.synchronize()
-    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
-    assert any("k_dense_tc" in n for n in names), names
-    assert torch.equal(toks, again)
-    wp, vm = nh.bufs["w_perm"], nh.bufs["vocab_map"].long()
-    logits = torch.empty(rows, wp.shape[0], dtype=torch.float32, device="cuda")
-    for j0 in range(0, wp.shape[0], 16384):  # fp32 reference, by vocab blocks
-        logits[:, j0:j0 + 16384] = H.float() @ wp[j0:j0 + 16384].float().t()
-    best = logits.max(dim=1).values
-    slot_of = torch.empty_like(vm)
-    slot_of[vm] = torch.arange(vm.numel(), device="cuda")
-    mine = logits.gather(1, slot_of[toks].view(-1, 1)).view(-1)
-    gap = (best - mine).abs() / best.abs().clamp_min(1e-30)
-    assert bool((gap <= 1e-5).all()), (int(gap.argmax()), float(gap.max()))
+    toks = _check_dense_tc(nh, H)
     ov = OracleView(fh)
     Hn = to_np_f32(H)
     for r in sorted({0, 1, 127, min(128, rows - 1), rows - 1}):

@@ -387,6 +387,28 @@ def test_host_buffer_entry_point(llama1b_heads):
     assert nh.next_token_host(H[:0]).numel() == 0
 
 
+def test_host_buffer_entry_point_reused_buffers(llama1b_heads):
+    """Repeated calls on the same page-locked buffers (read and written by
+    the kernels directly) see the buffers' current contents every time, for
+    the one-kernel, three-kernel and batched paths; pageable buffers in
+    between change nothing."""
+    from flash_head.synthetic import make_hidden
+    nh = llama1b_heads["fp8"].native()
+    for rows in (1, 7, 20):
+        hbuf = torch.empty(rows, nh.D, dtype=torch.bfloat16).pin_memory()
+        obuf = torch.empty(rows, dtype=torch.int64).pin_memory()
+        for i in range(5):
+            H = make_hidden(rows, nh.D, seed=950 + 10 * rows + i)
+            hbuf.copy_(H)
+            got = nh.next_token_host(hbuf, out_host=obuf)
+            want = nh.next_token(H.to("cuda")).cpu()
+            assert got.data_ptr() == obuf.data_ptr() and torch.equal(got, want), (rows, i)
+            if i == 2:
+                paged = nh.next_token_host(H.clone(), out_host=torch.empty(rows, dtype=torch.int64))
+                assert torch.equal(paged, want), rows
+    assert nh.workspace_error() == 0
+
+
 def test_workspace_reuse_across_row_counts(llama1b_heads):
     """One workspace serves calls with any row count: stage 2 alone (which
     relies on the accumulator left zeroed by earlier calls) matches the full
