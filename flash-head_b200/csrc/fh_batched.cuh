@@ -29,6 +29,14 @@ namespace fh {
 // From 16 rows; 5..15 rows take the three-kernel path, which streams each
 // row's clusters with more memory-level parallelism at that size.
 constexpr int kBatchMinRows = 16;
+// From this many rows (below kBatchMinRows) the three-kernel path scores
+// stage 1 with the cuBLASLt GEMM + k_select_hist instead of the CUDA-core
+// k_scores + k_select.
+#ifndef FH_GEMM_S1_MIN_ROWS
+#define FH_GEMM_S1_MIN_ROWS 5
+#endif
+constexpr int kGemmS1MinRows = FH_GEMM_S1_MIN_ROWS;
+static_assert(kGemmS1MinRows <= kBatchMinRows, "GEMM stage 1 covers the batched steps");
 constexpr int kInvRows = 8;          // hidden rows per item (two mma column sets)
 constexpr int kInvThreads = kFThreads;
 constexpr int kInvBlock = kFBlock;   // + producer / reducer warp

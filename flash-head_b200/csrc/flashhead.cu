@@ -224,7 +224,8 @@ struct Workspace {
   unsigned long long *packed;   // [rows]
   unsigned *counter;            // [1]
   unsigned char *epoch_bufs;    // one-kernel histograms
-  // batched steps (rows >= kBatchMinRows) only, else null
+  // batched steps (rows >= kBatchMinRows) only, else null; lt_ws from
+  // kGemmS1MinRows rows
   int *inv_cnt, *inv_off, *inv_item_off, *inv_cursor, *inv_meta, *inv_list;
   fh::InvItem *inv_items;
   void *lt_ws;
@@ -248,17 +249,19 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
       256 + fh::kHistBytes + round_up((size_t)rows * sizeof(unsigned long long), 256);
   const size_t probes = round_up((size_t)rows * d.n_probes * sizeof(int32_t), 256);
   const size_t scores = round_up((size_t)rows * w.score_stride * sizeof(float), 256);
-  // batched steps: inverted index and GEMM scratch below the scores
+  // GEMM stage 1 (kGemmS1MinRows+ rows): cuBLASLt scratch; batched steps
+  // (kBatchMinRows+): also the inverted index and dense logits; below the scores
   const bool batched = rows >= fh::kBatchMinRows;
+  const bool gemm = rows >= fh::kGemmS1MinRows;
   const size_t kint = round_up((size_t)d.n_clusters * sizeof(int), 256);
   const size_t n_pairs = (size_t)rows * d.n_probes;
   const size_t max_items = n_pairs / fh::kInvRows + (size_t)d.n_clusters + 1;
   const size_t dense =
       batched ? round_up((size_t)rows * dense_split(d, rows).stride * sizeof(float), 256) : 0;
-  const size_t inv = batched ? 4 * kint + 256 + round_up(n_pairs * sizeof(int), 256) +
-                                   round_up(max_items * sizeof(fh::InvItem), 256) +
-                                   kLtWorkspaceBytes + dense
-                             : 0;
+  const size_t inv = (batched ? 4 * kint + 256 + round_up(n_pairs * sizeof(int), 256) +
+                                    round_up(max_items * sizeof(fh::InvItem), 256) + dense
+                              : 0) +
+                     (gemm ? kLtWorkspaceBytes : 0);
   w.bytes = state + probes + scores + inv + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
   w.epoch_bufs = reinterpret_cast<unsigned char *>(p + 256);
@@ -272,21 +275,23 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   w.inv_items = nullptr;
   w.lt_ws = nullptr;
   w.dense = nullptr;
-  if (batched) {
+  if (gemm) {  // (batched implies gemm)
     size_t q = scores_off >= inv ? scores_off - inv : 0;
-    w.dense = reinterpret_cast<float *>(p + q);
+    if (batched) w.dense = reinterpret_cast<float *>(p + q);
     q += dense;
     w.lt_ws = p + q;
     q += kLtWorkspaceBytes;
-    w.inv_items = reinterpret_cast<fh::InvItem *>(p + q);
-    q += round_up(max_items * sizeof(fh::InvItem), 256);
-    w.inv_list = reinterpret_cast<int *>(p + q);
-    q += round_up(n_pairs * sizeof(int), 256);
-    w.inv_cnt = reinterpret_cast<int *>(p + q);
-    w.inv_off = reinterpret_cast<int *>(p + q + kint);
-    w.inv_item_off = reinterpret_cast<int *>(p + q + 2 * kint);
-    w.inv_cursor = reinterpret_cast<int *>(p + q + 3 * kint);
-    w.inv_meta = reinterpret_cast<int *>(p + q + 4 * kint);
+    if (batched) {
+      w.inv_items = reinterpret_cast<fh::InvItem *>(p + q);
+      q += round_up(max_items * sizeof(fh::InvItem), 256);
+      w.inv_list = reinterpret_cast<int *>(p + q);
+      q += round_up(n_pairs * sizeof(int), 256);
+      w.inv_cnt = reinterpret_cast<int *>(p + q);
+      w.inv_off = reinterpret_cast<int *>(p + q + kint);
+      w.inv_item_off = reinterpret_cast<int *>(p + q + 2 * kint);
+      w.inv_cursor = reinterpret_cast<int *>(p + q + 3 * kint);
+      w.inv_meta = reinterpret_cast<int *>(p + q + 4 * kint);
+    }
   }
   return w;
 }
@@ -510,9 +515,9 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
 // Batched steps (rows >= kBatchMinRows): cuBLASLt stage-1 GEMM, the selection
 // kernel, the inverted index and the inverted stage 2.
 // ---------------------------------------------------------------------------
-bool batched_ok(const fh_head *h, int rows, bool sample) {
+bool batched_ok(const fh_head *h, int rows, bool sample, int min_rows = fh::kBatchMinRows) {
   const fh_head_desc &d = h->d;
-  if (rows < fh::kBatchMinRows || (d.flags & FH_FLAG_NO_FUSED)) return false;
+  if (rows < min_rows || (d.flags & FH_FLAG_NO_FUSED)) return false;
   if (!(sample ? d.centroid_w16 : d.cluster_w16) || d.cluster_base != 0) return false;
   if (d.cluster_size > fh::kTileRows || (d.hidden * 2) % 128 != 0) return false;
   return sm_count() > 0;
@@ -1030,13 +1035,16 @@ FH_API int fh_head_destroy(fh_head *head) {
 FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample) {
   if (!head || rows <= 0) return 0;
   const fh_head_desc &d = head->d;
+  const bool epi = do_sample || (do_sample ? d.centroid_scale : d.cluster_scale);
   if (batched_ok(head, rows, do_sample != 0)) {
     // GEMM, [epilogue], select, index reset, count, build, scatter, items,
     // stage 2, [specials], finalize
-    const bool epi = do_sample || (do_sample ? d.centroid_scale : d.cluster_scale);
     return 9 + (epi ? 1 : 0) + (d.n_special > 0 ? 1 : 0);
   }
-  return fused_ok(d, rows, do_sample != 0, sm_count()) ? 1 : 3;
+  if (fused_ok(d, rows, do_sample != 0, sm_count())) return 1;
+  // GEMM, [epilogue], select, stage 2; or scores, select, stage 2
+  if (batched_ok(head, rows, do_sample != 0, fh::kGemmS1MinRows)) return 3 + (epi ? 1 : 0);
+  return 3;
 }
 
 FH_API size_t fh_workspace_error_offset(void) { return fh::kSyncError * sizeof(uint32_t); }
@@ -1058,7 +1066,11 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
     return run_batched(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, s);
   if (fused_ok(head->d, rows, false, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, grid, s);
-  st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
+  if (batched_ok(head, rows, false, fh::kGemmS1MinRows))
+    st = run_batched_stage1(head, hidden, rows, false, 1.f, 0, 0, w, w.scores, w.score_stride,
+                            w.probes, s);
+  else
+    st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
   if (st != FH_OK) return st;
   fh::Stage2Args a = stage2_args(head->d, hidden, rows);
   a.probes = w.probes;
@@ -1161,8 +1173,12 @@ FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int
     return run_batched(head, hidden, rows, true, temperature, seed, offset, out_ids, w, s);
   if (fused_ok(head->d, rows, true, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, true, temperature, seed, offset, out_ids, w, grid, s);
-  st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
-                  nullptr, 0, s);
+  if (batched_ok(head, rows, true, fh::kGemmS1MinRows))
+    st = run_batched_stage1(head, hidden, rows, true, temperature, seed, offset, w, w.scores,
+                            w.score_stride, w.probes, s);
+  else
+    st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
+                    nullptr, 0, s);
   if (st != FH_OK) return st;
   fh::Stage2Args a = stage2_args(head->d, hidden, rows);
   a.probes = w.probes;
@@ -1194,7 +1210,7 @@ FH_API int fh_top_clusters(const fh_head *head, const void *hidden, int rows, in
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   // the stage 1 of the step the library runs for this many rows
-  if (batched_ok(head, rows, do_sample != 0))
+  if (batched_ok(head, rows, do_sample != 0, fh::kGemmS1MinRows))
     return run_batched_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w,
                               out_scores ? out_scores : w.scores,
                               out_scores ? head->d.n_clusters : w.score_stride, out_probes, s);

@@ -256,7 +256,12 @@ FH_API int fh_stage2_next_token(const fh_head *head, const void *hidden,
 /*
  * Full-vocabulary next token over w_perm (greedy, or sampled at temperature
  * when do_sample != 0). Replaces the dense branch of get_next_token for
- * hidden_states.shape[0] > 10 (flash_head.py:292-301).
+ * hidden_states.shape[0] > 10 (flash_head.py:292-301). Greedy calls of 16..256
+ * rows run one tcgen05 GEMM + argmax kernel (the logits stay on chip);
+ * sampled calls of 16+ rows run cuBLASLt GEMMs into workspace logits and a
+ * Gumbel-max pass; fewer rows run the block-sparse stage 2 over every cluster.
+ * Ties go to the smallest vocab id; logits are f32 sums of the 16-bit
+ * products, so ids equal the exact argmax up to f32 rounding of near-ties.
  */
 FH_API int fh_dense_next_token(const fh_head *head, const void *hidden,
                                int rows, int do_sample, float temperature,

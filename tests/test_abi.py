@@ -118,13 +118,15 @@ def test_valid_descriptor_and_workspace_size(lib):
         for rows in (1, 8, 256):
             hist = 2 * 4 * (256 + 65536) * 4  # two epochs of 4 rows' histograms
             want = 256 + hist + rnd(rows * 8) + rnd(rows * 256 * 4) + rnd(rows * 8064 * 4) + 256
-            if rows >= 16:  # batched steps: inverted index, item list, GEMM scratch, logits
+            if rows >= 5:  # GEMM stage 1: cuBLASLt scratch
+                want += 8 << 20
+            if rows >= 16:  # batched steps: inverted index, item list, dense logits
                 K, pairs, cap = 8016, rows * 256, 16
                 g = min(cap, max(1, (64 << 20) // (rows * K * 4)))  # w_perm blocks per dense GEMM
                 g = -(-cap // -(-cap // g))
                 dense = rnd(rows * ((g * K + 63) // 64 * 64) * 4)
                 want += (4 * rnd(K * 4) + 256 + rnd(pairs * 4) + rnd((pairs // 8 + K + 1) * 64)
-                         + (8 << 20) + dense)
+                         + dense)
             assert lib.fh_workspace_bytes(h, rows) == want
         assert lib.fh_workspace_bytes(None, 1) == 0
     finally:
