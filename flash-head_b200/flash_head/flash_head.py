@@ -235,6 +235,57 @@ class FlashHead(nn.Module):
             seed, offset = self._next_seed()
         return self.native().dense_next_token(hidden, do_sample, temperature, seed or 0, offset)
 
+    def candidate_logprobs(self, hidden: torch.Tensor, token_ids: torch.Tensor,
+                           num_logprobs: int):
+        """Log-probabilities of a step over its candidate set, in the layout of
+        vLLM's ``Sampler.gather_logprobs``: (ids [N, k+1] int32, logprobs
+        [N, k+1] float32, ranks [N] int64), column 0 the given token, then the
+        k most likely candidates; rank = candidates at least as likely as the
+        token.
+
+        The reference returns no logprobs on its FlashHead path
+        (patches/sampler.py:21). Here the candidate set of a row is the tokens
+        of its top-p clusters (greedy stage 1), the special tokens and the
+        given token; the softmax is taken over that set only, so the
+        probability mass of unprobed clusters is left out (logprobs are those
+        of the renormalised candidate distribution, close to the full ones
+        when the probes hold the mass). Logits are the kernels' f32 sums
+        rounded to the head dtype, as vLLM's own LM head returns them."""
+        from .fused import block_sparse_logits
+        nh = self.native()
+        h = nh._h(hidden)
+        N, k = h.shape[0], int(num_logprobs)
+        if k < 0:
+            raise ValueError("num_logprobs must be >= 0")
+        tok = token_ids.to(device=h.device, dtype=torch.int64).view(-1)
+        if tok.numel() != N:
+            raise ValueError(f"{tok.numel()} token ids for {N} rows")
+        cap = self._cap
+        probes = nh.top_clusters(h).to(torch.int64)                       # [N, p]
+        logits = block_sparse_logits(h, self.w_perm.view(-1), probes, self._K, cap).float()
+        ids = self.vocab_maps.index_select(0, probes.view(-1)).view(N, -1)
+        # special tokens and the given token, unless already among the candidates
+        flat = self.vocab_maps.view(-1)
+        slot_of = torch.empty_like(flat)
+        slot_of[flat] = torch.arange(flat.numel(), device=flat.device)
+        sp = self.special_token_ids_tensor.to(h.device)
+        extra = torch.cat([sp.unsqueeze(0).expand(N, -1), tok.view(N, 1)], 1)   # [N, S+1]
+        slots = slot_of.index_select(0, extra.view(-1)).view(N, -1)
+        rows = self.w_perm.view(-1, self._D).index_select(0, slots.view(-1)).view(N, -1, self._D)
+        ex_logits = torch.einsum("nsd,nd->ns", rows.float(), h.float()).to(h.dtype).float()
+        dup = ((slots // cap).unsqueeze(2) == probes.unsqueeze(1)).any(dim=2)
+        earlier = (extra.unsqueeze(2) == extra.unsqueeze(1)).tril(diagonal=-1).any(dim=2)
+        ex_logits = ex_logits.masked_fill(dup | earlier, float("-inf"))
+        all_ids = torch.cat([ids, extra], 1)
+        lp = torch.log_softmax(torch.cat([logits, ex_logits], 1), dim=-1)
+        hit = (all_ids == tok.view(N, 1)) & torch.isfinite(lp)
+        tok_lp = lp.masked_fill(~hit, float("-inf")).max(dim=1).values
+        top_lp, top_i = torch.topk(lp, k, dim=-1)
+        out_ids = torch.cat([tok.view(N, 1), all_ids.gather(1, top_i)], 1).to(torch.int32)
+        out_lp = torch.cat([tok_lp.view(N, 1), top_lp], 1)
+        ranks = (lp >= tok_lp.view(N, 1)).sum(dim=1)
+        return out_ids, out_lp, ranks
+
     # ------------------------------------------------------------------
     # Reference-named methods (flash_head.py:190-334)
     # ------------------------------------------------------------------

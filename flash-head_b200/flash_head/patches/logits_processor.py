@@ -34,13 +34,33 @@ def _get_flash_head():
     return _flash_head
 
 
+# hidden states of the last step that returned FlashHead ids; the sampler
+# hook reads them when the step's requests ask for logprobs
+_last_hidden = None
+
+
 def flash_head_token_ids(hidden_states: torch.Tensor):
     """Token ids [n, 1] int32 for a decode step, or None if FlashHead does not apply."""
+    global _last_hidden
     fh = _get_flash_head()
     n = hidden_states.shape[0]
     if fh is None or not (1 <= n <= max_decode_rows()):
+        _last_hidden = None
         return None
-    return fh.get_next_token_batched(hidden_states.reshape(n, -1)).view(n, 1).to(torch.int32)
+    h = hidden_states.reshape(n, -1)
+    _last_hidden = h
+    return fh.get_next_token_batched(h).view(n, 1).to(torch.int32)
+
+
+def step_candidate_logprobs(token_ids: torch.Tensor, num_logprobs: int):
+    """(ids, logprobs, ranks) of the last FlashHead step over its candidate
+    set (FlashHead.candidate_logprobs), or None when there is no such step."""
+    fh = _flash_head
+    if fh is _FLASH_HEAD_NOT_LOADED or fh is None or _last_hidden is None:
+        return None
+    if _last_hidden.shape[0] != token_ids.numel():
+        return None
+    return fh.candidate_logprobs(_last_hidden, token_ids, num_logprobs)
 
 
 def patch_logits_processor():

@@ -409,6 +409,66 @@ def test_host_buffer_entry_point_reused_buffers(llama1b_heads):
     assert nh.workspace_error() == 0
 
 
+def _oracle_candidate_logprobs(ov, h, probes, tok):
+    """float64 log-softmax over one row's candidates (probed clusters, special
+    tokens, and the given token when it is not among them)."""
+    vids, logits = O.candidate_logits(h, ov.w_perm, ov.vm, probes, ov.specials)
+    if tok not in set(vids.tolist()):
+        vids = np.append(vids, tok)
+        logits = np.append(logits, ov.logit(h, tok))
+    m = logits.max()
+    lp = logits - (m + np.log(np.exp(logits - m).sum()))
+    return dict(zip(vids.tolist(), lp.tolist()))
+
+
+@pytest.mark.parametrize("which,rows", [("llama", 1), ("llama", 6), ("specials", 5)])
+def test_candidate_logprobs_match_the_oracle(llama1b_heads, which, rows):
+    """FlashHead.candidate_logprobs (the sampler hook's logprobs): per row the
+    given token's logprob, the top-k ids and values and the token's rank agree
+    with the oracle's float64 log-softmax over the same candidate set (the
+    kernel's own probes, the special tokens and the token) within 2e-2 (logits
+    rounded to bf16). Even rows ask for the greedy token (rank 1), odd rows
+    for a token of an unprobed cluster."""
+    from flash_head.synthetic import HeadShape, make_head, make_hidden
+    if which == "llama":
+        fh = llama1b_heads["fp8"]
+    else:
+        head = make_head(HeadShape(hidden=256, vocab=4800, n_clusters=300, n_probes=24), seed=4)
+        fh = build_head(head.weight, head.centroids, head.assignments, 24,
+                        specials=[0, 5, 4799], stage1="model")
+    nh = fh.native()
+    ov = OracleView(fh)
+    H = make_hidden(rows, fh._D, seed=1500 + rows, device="cuda")
+    Hn = to_np_f32(H)
+    probes = nh.top_clusters(H).cpu().numpy()
+    greedy = nh.next_token(H).cpu().numpy()
+    toks = []
+    for r in range(rows):
+        if r % 2 == 0:
+            toks.append(int(greedy[r]))
+        else:
+            c = next(c for c in range(ov.K) if c not in set(probes[r].tolist()))
+            toks.append(int(ov.vm[c, 0]))
+    k, tol = 5, 2e-2
+    ids, lps, ranks = fh.candidate_logprobs(H, torch.tensor(toks), k)
+    assert ids.shape == (rows, k + 1) and ids.dtype == torch.int32 and lps.dtype == torch.float32
+    ids, lps, ranks = ids.cpu().numpy(), lps.cpu().numpy(), ranks.cpu().numpy()
+    for r in range(rows):
+        want = _oracle_candidate_logprobs(ov, Hn[r], probes[r], toks[r])
+        assert ids[r, 0] == toks[r] and abs(lps[r, 0] - want[toks[r]]) <= tol, r
+        best = sorted(want.values(), reverse=True)
+        assert list(lps[r, 1:]) == sorted(lps[r, 1:], reverse=True), r
+        for j in range(1, k + 1):
+            assert abs(lps[r, j] - want[int(ids[r, j])]) <= tol, (r, j)
+            assert lps[r, j] >= best[j - 1] - tol, (r, j)
+        t = want[toks[r]]
+        lo = sum(v >= t + tol for v in want.values())
+        hi = sum(v >= t - tol for v in want.values())
+        assert lo <= ranks[r] <= hi, (r, ranks[r], lo, hi)
+        if r % 2 == 0 and hi == 1:
+            assert ranks[r] == 1
+
+
 def test_workspace_reuse_across_row_counts(llama1b_heads):
     """One workspace serves calls with any row count: stage 2 alone (which
     relies on the accumulator left zeroed by earlier calls) matches the full

@@ -196,6 +196,22 @@ if after != before:
     print("IDS", ids.dtype, ids.tolist())
     out = Sampler.forward(Sampler.__new__(Sampler), ids, None)
     print("SAMPLED", out.sampled_token_ids.tolist(), out.logprobs_tensors)
+    from types import SimpleNamespace
+    class FakeHeadLogprobs(FakeHead):
+        def candidate_logprobs(self, h, tok, k):
+            n = h.shape[0]
+            print("ASKED", tok.tolist(), k, tuple(h.shape))
+            return (torch.full((n, k + 1), 7, dtype=torch.int32), torch.zeros(n, k + 1),
+                    torch.ones(n, dtype=torch.int64))
+    lp._flash_head = FakeHeadLogprobs()
+    ids = proc.forward(None, torch.zeros(1, 8))
+    md = SimpleNamespace(max_num_logprobs=3, logprob_token_ids=None)
+    t = Sampler.forward(Sampler.__new__(Sampler), ids, md).logprobs_tensors
+    print("LOGPROBS", type(t).__name__, tuple(t.logprob_token_ids.shape), t.logprob_token_ids.dtype,
+          tuple(t.logprobs.shape), t.selected_token_ranks.tolist())
+    for bad in (SimpleNamespace(max_num_logprobs=-1, logprob_token_ids=None),
+                SimpleNamespace(max_num_logprobs=2, logprob_token_ids={{0: [3]}})):
+        print("UNSUPPORTED", Sampler.forward(Sampler.__new__(Sampler), ids, bad).logprobs_tensors)
 """
 
 
@@ -213,5 +229,9 @@ def test_register_and_hooks(enabled):
         assert status.startswith("PATCHED")
         assert "IDS torch.int32 [[5]]" in res.stdout  # ids untouched by soft-cap / scale
         assert "SAMPLED [[5]] None" in res.stdout
+        # logprobs over the step's candidate set when a request asks for k of them
+        assert "ASKED [5] 3 (1, 8)" in res.stdout
+        assert "LOGPROBS LogprobsTensors (1, 4) torch.int32 (1, 4) [1]" in res.stdout
+        assert res.stdout.count("UNSUPPORTED None") == 2
     else:
         assert status.startswith("UNPATCHED")
