@@ -23,6 +23,7 @@
 #include "../../include/flashhead.h"
 #include "fh_batched.cuh"
 #include "fh_dense_tc.cuh"
+#include "fh_spec.cuh"
 
 namespace {
 
@@ -1488,6 +1489,26 @@ FH_API int fh_block_sparse_argmax_atomic(const void *hs, int T, int D, const voi
   }
   FH_CHECK_LAUNCH(launch(fh::k_unpack_ids, dim3((T + 255) / 256), dim3(256), 0, s, false, acc, T),
                   "unpack launch");
+  return FH_OK;
+}
+
+FH_API int fh_spec_accept(const int32_t *draft_ids, const int32_t *target_ids,
+                          const int32_t *bonus_ids, const int32_t *cu_num_draft, int batch,
+                          int max_spec_len, int32_t placeholder, int32_t *out_ids,
+                          fh_stream_t stream) {
+  if (batch < 0) return fail(FH_ERR_INVALID_ARGUMENT, "batch=%d < 0", batch);
+  if (max_spec_len < 0 || max_spec_len > 4096)
+    return fail(FH_ERR_INVALID_ARGUMENT, "max_spec_len=%d outside 0..4096", max_spec_len);
+  if (batch == 0) return FH_OK;
+  if (!bonus_ids || !cu_num_draft || !out_ids ||
+      (max_spec_len > 0 && (!draft_ids || !target_ids)))
+    return fail(FH_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int warps_per_block = 8;
+  FH_CHECK_LAUNCH(launch(fh::k_spec_accept, dim3((batch + warps_per_block - 1) / warps_per_block),
+                         dim3(32 * warps_per_block), 0, s, false, draft_ids, target_ids,
+                         bonus_ids, cu_num_draft, batch, max_spec_len, placeholder, out_ids),
+                  "draft acceptance launch");
   return FH_OK;
 }
 

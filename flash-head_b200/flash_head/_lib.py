@@ -96,6 +96,7 @@ SIGNATURES = {
     "fh_tp_local_candidates": (_I, [_P, _P, _I, _I, _F, _U64, _U64, _P, _P, _SZ, _P]),
     "fh_tp_select_and_score": (_I, [_P, _P, _I, _I, _P, _I, _F, _U64, _U64, _P, _P, _SZ, _P]),
     "fh_tp_finalize": (_I, [_P, _I, _P, _P]),
+    "fh_spec_accept": (_I, [_P, _P, _P, _P, _I, _I, ctypes.c_int32, _P, _P]),
 }
 
 _lib = None

@@ -9,6 +9,10 @@
    (reference patches/llm.py)
 5. AsyncLLM.__init__ - write the head metadata (``vllm serve``)
    (reference patches/async_llm.py)
+6. RejectionSampler.forward - verify speculative drafts against FlashHead
+   ids on the device (reference patches/rejection_sampler.py)
+7. EagleProposer._greedy_sample / _sample_from_logits - pass FlashHead ids
+   through as draft tokens (reference patches/eagle.py)
 """
 
 import logging
@@ -22,10 +26,14 @@ def apply_all():
     from flash_head.patches.gpu_model_runner import patch_gpu_model_runner
     from flash_head.patches.llm import patch_llm
     from flash_head.patches.logits_processor import patch_logits_processor
+    from flash_head.patches.eagle import patch_eagle
+    from flash_head.patches.rejection_sampler import patch_rejection_sampler
     from flash_head.patches.sampler import patch_sampler
 
     patch_logits_processor()
     patch_sampler()
+    patch_rejection_sampler()
+    patch_eagle()
     patch_gpu_model_runner()
     patch_llm()
     patch_async_llm()

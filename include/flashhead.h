@@ -289,6 +289,23 @@ FH_API int fh_block_sparse_logits_argmax(const void *hs, int T, int D,
                                          int dtype, void *out_max,
                                          int64_t *out_vocab,
                                          fh_stream_t stream);
+/*
+ * Speculative decoding with FlashHead ids (replaces the per-element host loop
+ * of the reference's RejectionSampler hook, patches/rejection_sampler.py:55-76).
+ * Per request b (batch requests, drafts draft_ids[cu[b-1] .. cu[b]) with
+ * cu = cu_num_draft, an inclusive prefix sum, int32 on the device):
+ * out_ids[b, j] = draft token j while it equals target_ids at the same flat
+ * position; the first mismatch writes the target's token there and ends the
+ * row; when every draft is accepted, bonus_ids[b] goes to position n (also
+ * for n = 0, as vLLM's rejection sampler does; the reference's loop leaves
+ * such rows empty). Other positions hold `placeholder`. out_ids is
+ * [batch, max_spec_len + 1] int32; max_spec_len 0..4096.
+ */
+FH_API int fh_spec_accept(const int32_t *draft_ids, const int32_t *target_ids,
+                          const int32_t *bonus_ids, const int32_t *cu_num_draft, int batch,
+                          int max_spec_len, int32_t placeholder, int32_t *out_ids,
+                          fh_stream_t stream);
+
 /* fused.py:167-188: out [T] int64 next-token ids. */
 FH_API int fh_block_sparse_argmax_atomic(const void *hs, int T, int D,
                                          const void *w_perm, const int64_t *ci,

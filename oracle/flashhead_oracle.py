@@ -371,3 +371,38 @@ def chi2_homogeneity(counts_a: np.ndarray, counts_b: np.ndarray, min_expected: f
     stat = float((((A - EA) ** 2) / EA).sum() + (((B - EB) ** 2) / EB).sum())
     dof = len(A) - 1
     return stat, dof, float(chi2.sf(stat, dof)) if dof > 0 else 1.0
+
+
+# ----------------------------------------------------------------------------
+# Speculative decoding: acceptance of draft tokens against FlashHead ids
+# (patches/rejection_sampler.py:55-76)
+# ----------------------------------------------------------------------------
+
+
+def spec_accept(draft_ids, target_ids, bonus_ids, num_draft, max_spec_len,
+                placeholder: int = -1, bonus_without_drafts: bool = True) -> np.ndarray:
+    """[batch, max_spec_len + 1] int32 output token ids. Per request, drafts
+    are accepted while they equal the target id at the same flat position;
+    the first mismatch takes the target id and ends the row; a fully
+    accepted row gets its bonus id after its drafts. The reference's loop
+    adds the bonus only when the request had drafts
+    (``bonus_without_drafts=False``); vLLM's own rejection sampler, which
+    the library follows, adds it for rows without drafts too."""
+    draft = np.asarray(draft_ids).ravel()
+    target = np.asarray(target_ids).ravel()
+    bonus = np.asarray(bonus_ids).ravel()
+    out = np.full((len(num_draft), max_spec_len + 1), placeholder, dtype=np.int32)
+    offset = 0
+    for i, n in enumerate(num_draft):
+        all_ok = True
+        for j in range(n):
+            if draft[offset + j] == target[offset + j]:
+                out[i, j] = draft[offset + j]
+            else:
+                out[i, j] = target[offset + j]
+                all_ok = False
+                break
+        if all_ok and (n > 0 or bonus_without_drafts):
+            out[i, n] = bonus[i]
+        offset += n
+    return out

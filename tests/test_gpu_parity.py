@@ -469,6 +469,34 @@ def test_candidate_logprobs_match_the_oracle(llama1b_heads, which, rows):
             assert ranks[r] == 1
 
 
+@pytest.mark.parametrize("batch,max_spec", [(1, 1), (37, 5), (64, 33), (9, 128)])
+def test_spec_accept_matches_the_oracle(batch, max_spec):
+    """Draft acceptance on the device (fh_spec_accept) equals the oracle's
+    restatement of the reference's loop, bit for bit: random draft counts
+    0..max (rows without drafts included), drafts matching the target with
+    probability 0.9 per position, lengths beyond one warp's 32 lanes."""
+    from flash_head.spec import accept_draft_tokens
+    rng = np.random.default_rng(batch * 1000 + max_spec)
+    num = rng.integers(0, max_spec + 1, size=batch)
+    num[0] = max_spec
+    T = int(num.sum())
+    target = rng.integers(0, 128256, size=T).astype(np.int32)
+    draft = np.where(rng.random(T) < 0.9, target, rng.integers(0, 128256, size=T)).astype(np.int32)
+    bonus = rng.integers(0, 128256, size=batch).astype(np.int32)
+    cu = np.cumsum(num).astype(np.int32)
+    out = accept_draft_tokens(torch.from_numpy(draft).cuda(), torch.from_numpy(target).cuda(),
+                              torch.from_numpy(bonus).cuda(), torch.from_numpy(cu).cuda(),
+                              max_spec)
+    want = O.spec_accept(draft, target, bonus, num.tolist(), max_spec)
+    assert out.dtype == torch.int32 and np.array_equal(out.cpu().numpy(), want)
+    # no drafts at all: every row is its bonus token
+    none = accept_draft_tokens(torch.empty(0, dtype=torch.int32, device="cuda"),
+                               torch.empty(0, dtype=torch.int32, device="cuda"),
+                               torch.from_numpy(bonus).cuda(),
+                               torch.zeros(batch, dtype=torch.int32, device="cuda"), 0)
+    assert none.view(-1).cpu().tolist() == bonus.tolist()
+
+
 def test_workspace_reuse_across_row_counts(llama1b_heads):
     """One workspace serves calls with any row count: stage 2 alone (which
     relies on the accumulator left zeroed by earlier calls) matches the full

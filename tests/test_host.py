@@ -209,6 +209,31 @@ if after != before:
     t = Sampler.forward(Sampler.__new__(Sampler), ids, md).logprobs_tensors
     print("LOGPROBS", type(t).__name__, tuple(t.logprob_token_ids.shape), t.logprob_token_ids.dtype,
           tuple(t.logprobs.shape), t.selected_token_ranks.tolist())
+    # speculative decoding: verification of drafts against FlashHead ids (the
+    # device comparison replaced by the oracle here: no GPU on this path)
+    import numpy as np
+    from oracle import flashhead_oracle as O
+    import flash_head.spec as spec
+    def fake_accept(draft, target, bonus, cu, max_spec_len, placeholder=-1, out=None):
+        cu = cu.tolist()
+        num = [c - (cu[i - 1] if i else 0) for i, c in enumerate(cu)]
+        return torch.from_numpy(O.spec_accept(draft.numpy(), target.numpy(), bonus.numpy(),
+                                              num, max_spec_len, placeholder))
+    spec.accept_draft_tokens = fake_accept
+    from vllm.v1.sample.rejection_sampler import RejectionSampler
+    from vllm.v1.spec_decode.metadata import SpecDecodeMetadata
+    md = SpecDecodeMetadata.make_dummy([[5, 6], [7], []], device="cpu")
+    md.target_logits_indices = torch.tensor([0, 1, 3], dtype=torch.int32)
+    md.bonus_logits_indices = torch.tensor([2, 4, 5], dtype=torch.int32)
+    step_ids = torch.tensor([[5], [6], [30], [8], [31], [32]], dtype=torch.int32)
+    rs = RejectionSampler.__new__(RejectionSampler)
+    print("SPEC", RejectionSampler.forward(rs, md, None, step_ids, None).sampled_token_ids.tolist())
+    from vllm.v1.spec_decode.eagle import EagleProposer
+    prop = EagleProposer.__new__(EagleProposer)
+    prop.use_local_argmax_reduction = False
+    prop.model = SimpleNamespace(compute_logits=lambda h: torch.tensor([[11], [12]], dtype=torch.int32))
+    print("DRAFT", prop._greedy_sample(torch.zeros(2, 8)).tolist(),
+          prop._sample_from_logits(torch.tensor([[3]], dtype=torch.int32), None)[0].tolist())
     for bad in (SimpleNamespace(max_num_logprobs=-1, logprob_token_ids=None),
                 SimpleNamespace(max_num_logprobs=2, logprob_token_ids={{0: [3]}})):
         print("UNSUPPORTED", Sampler.forward(Sampler.__new__(Sampler), ids, bad).logprobs_tensors)
@@ -233,5 +258,8 @@ def test_register_and_hooks(enabled):
         assert "ASKED [5] 3 (1, 8)" in res.stdout
         assert "LOGPROBS LogprobsTensors (1, 4) torch.int32 (1, 4) [1]" in res.stdout
         assert res.stdout.count("UNSUPPORTED None") == 2
+        # drafts [5, 6] vs targets [5, 6] -> bonus 30; [7] vs [8] -> 8; no drafts -> bonus 32
+        assert "SPEC [[5, 6, 30], [8, -1, -1], [32, -1, -1]]" in res.stdout
+        assert "DRAFT [11, 12] [3]" in res.stdout
     else:
         assert status.startswith("UNPATCHED")

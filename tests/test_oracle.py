@@ -267,3 +267,18 @@ def test_fp8_table():
     t = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
     both = ~np.isnan(t)
     assert np.array_equal(t[both], O.FP8_E4M3_VALUES[both])
+
+
+def test_spec_accept_restates_the_reference_loop():
+    """Draft acceptance (patches/rejection_sampler.py:55-76) on hand-made
+    rows: accepted prefix, first mismatch replaced by the target id, bonus
+    after a fully accepted row; a row without drafts gets its bonus only in
+    vLLM's semantics (the library's), not in the reference's literal loop."""
+    draft = [5, 6, 7, 1, 2, 9, 9, 9]
+    target = [5, 6, 7, 1, 3, 9, 8, 9]
+    bonus = [40, 41, 42, 43]
+    num = [3, 2, 0, 3]  # row 0 all accepted, row 1 rejects at 1, row 2 empty, row 3 rejects at 1
+    out = O.spec_accept(draft, target, bonus, num, max_spec_len=3)
+    assert out.tolist() == [[5, 6, 7, 40], [1, 3, -1, -1], [42, -1, -1, -1], [9, 8, -1, -1]]
+    ref = O.spec_accept(draft, target, bonus, num, max_spec_len=3, bonus_without_drafts=False)
+    assert ref[2].tolist() == [-1, -1, -1, -1] and ref[0].tolist() == [5, 6, 7, 40]
