@@ -164,6 +164,17 @@ def test_call_validation_needs_no_gpu(lib):
                                           s) == _lib.FH_ERR_INVALID_ARGUMENT
         assert lib.fh_block_sparse_logits(fake, 1, 64, fake, fake, 8, 8, 16, _lib.FH_FP8_E4M3,
                                           fake, s) == _lib.FH_ERR_INVALID_ARGUMENT
+        # draft acceptance: empty batch, then bad sizes and pointers
+        assert lib.fh_spec_accept(None, None, None, None, 0, 4, -1, None, s) == _lib.FH_OK
+        assert lib.fh_spec_accept(fake, fake, fake, fake, -1, 4, -1, fake, s) == \
+            _lib.FH_ERR_INVALID_ARGUMENT
+        assert lib.fh_spec_accept(fake, fake, fake, fake, 2, 4097, -1, fake, s) == \
+            _lib.FH_ERR_INVALID_ARGUMENT
+        assert "max_spec_len" in _lib.last_error()
+        assert lib.fh_spec_accept(None, fake, fake, fake, 2, 3, -1, fake, s) == \
+            _lib.FH_ERR_INVALID_ARGUMENT
+        assert lib.fh_spec_accept(fake, fake, None, fake, 2, 3, -1, fake, s) == \
+            _lib.FH_ERR_INVALID_ARGUMENT
     finally:
         lib.fh_head_destroy(h)
 
