@@ -158,7 +158,7 @@ __device__ __forceinline__ uint4 ldg_keep(const void *p) {
 // ---------------------------------------------------------------------------
 // Bulk asynchronous copies (TMA engine, no tensor map) into shared memory,
 // completed on an mbarrier. Addresses 16-byte aligned, sizes multiples of 16.
-// Never multicast.
+// Every copy lands in the issuing CTA's own shared memory only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
