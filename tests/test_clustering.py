@@ -65,6 +65,25 @@ def test_deterministic_and_input_checks():
         balanced_clusters(head.weight[0], cap=16)
 
 
+def test_degenerate_heads_stay_balanced():
+    """One cluster, clusters of one token, identical and all-zero rows (ties
+    everywhere), and a bf16 weight: every cluster still gets exactly cap
+    tokens and the centroids are the member means."""
+    from flash_head.clustering import balanced_clusters
+    a, c = balanced_clusters(torch.randn(16, 8), cap=16)
+    assert a.tolist() == [0] * 16 and c.shape == (8, 1)
+    w = torch.randn(10, 4)
+    a, c = balanced_clusters(w, cap=1)
+    assert sorted(a.tolist()) == list(range(10))
+    np.testing.assert_allclose(c.numpy(), w.numpy()[np.argsort(a.numpy())].T, atol=1e-7)
+    w = torch.zeros(64, 8)
+    w[:32] = torch.randn(1, 8)
+    a, c = balanced_clusters(w, cap=16)
+    assert np.all(np.bincount(a.numpy(), minlength=4) == 16)
+    a, c = balanced_clusters(torch.randn(256, 32).to(torch.bfloat16), cap=16)
+    assert np.all(np.bincount(a.numpy(), minlength=16) == 16) and c.dtype == torch.float32
+
+
 def test_learned_clusters_beat_random_ones_on_a_noisy_head():
     """Noise larger than the centre spread (0.03 vs 0.02): the FlashHead step
     (oracle, p = 16 of 256 clusters) on the learned clustering agrees with the
