@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cmath>
@@ -137,23 +138,33 @@ cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream
   // start streaming its stage-1 rows while the previous kernel in the stream
   // drains; it reads the hidden states and the workspace only after
   // griddepcontrol.wait.
-  static int pdl_ok[128];  // 0 unknown, 1 accepted, -1 rejected
+  // 0 unknown, 1 accepted, -1 rejected; shared by the host threads of a process
+  static std::atomic<int> pdl_ok[128];
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  if (pdl_ok[dev] >= 0) {
+  int known = pdl_ok[dev].load(std::memory_order_relaxed);
+  if (known == 0) {
+    // A refused trial launch would invalidate a graph being captured: while
+    // the stream captures and support is still unknown, launch without PDL
+    // and leave the question for an uncaptured call.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+      known = -2;
+  }
+  if (known >= 0) {
     cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e == cudaSuccess) {
-      pdl_ok[dev] = 1;
+      pdl_ok[dev].store(1, std::memory_order_relaxed);
       return e;
     }
-    if (pdl_ok[dev] == 1) return e;
+    if (known == 1) return e;
     (void)cudaGetLastError();  // the pair is not supported here: launch without PDL
-    pdl_ok[dev] = -1;
+    pdl_ok[dev].store(-1, std::memory_order_relaxed);
   }
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, a);

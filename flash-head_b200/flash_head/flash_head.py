@@ -10,9 +10,13 @@ per-step computation runs in ``libflashhead_b200.so``; there is no CPU or
 PyTorch fallback for the step itself.
 
 Differences from the reference, all deliberate:
-  * stage 1 scores the L2-normalised centroids in fp8 e4m3 with a per-row
-    fp32 scale by default (``stage1_dtype="fp8"``; "model" keeps the model
-    dtype, bit-compatible with the reference's bf16 scores);
+  * stage 1 scores the L2-normalised centroids in the model dtype by default
+    (``stage1_dtype="model"``: the reference's bf16 scores, with fp32
+    accumulation), or in fp8 e4m3 with a per-row fp32 scale
+    (``stage1_dtype="fp8"``: half the stage-1 bytes; on N(0, 0.25) hidden
+    states of the Llama-3.2-1B-shaped head it keeps ~97.5 % of the
+    reference's probes and its greedy tokens, but the fp8 score error of
+    ~2 % of the boundary score breaks the 1e-2 probe-set rule on most rows);
   * ties: probe selection prefers the smaller cluster id, the token the
     smaller vocab id, on fp32 logits in every mode (``use_identical_tiebreak``
     is accepted; the reference's tiebreak branch differs only in comparing
@@ -121,7 +125,7 @@ class FlashHead(nn.Module):
     :param n_probes: probes per step (default K / 16).
     :param special_token_ids: tokens always scored, independent of clusters.
     :param stage1_dtype: "fp8" (e4m3 + per-row scale) or "model"; default from
-        the FLASHHEAD_STAGE1_DTYPE environment variable, else "fp8".
+        the FLASHHEAD_STAGE1_DTYPE environment variable, else "model".
     """
 
     def __init__(self, lm_head: nn.Linear, centroids: torch.Tensor,
@@ -136,7 +140,7 @@ class FlashHead(nn.Module):
         self._K, self._cap, self._D = K, cap, D
         self.n_probes = int(n_probes if n_probes is not None
                             else centroids.shape[1] / DEFAULT_CLUSTER_RATIO)
-        stage1_dtype = stage1_dtype or os.environ.get(STAGE1_ENV, "fp8")
+        stage1_dtype = stage1_dtype or os.environ.get(STAGE1_ENV, "model")
         if stage1_dtype not in ("fp8", "model"):
             raise ValueError(f"stage1_dtype must be 'fp8' or 'model', got {stage1_dtype!r}")
         self.stage1_dtype = stage1_dtype

@@ -73,7 +73,7 @@ class ShardedFlashHead:
 
     def __init__(self, w_perm: torch.Tensor, vocab_maps: torch.Tensor, cluster_w: torch.Tensor,
                  centroids: torch.Tensor, n_probes: int, special_ids: Optional[torch.Tensor] = None,
-                 stage1_dtype: str = "fp8", group=None, device: Optional[torch.device] = None):
+                 stage1_dtype: str = "model", group=None, device: Optional[torch.device] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)

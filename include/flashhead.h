@@ -27,6 +27,10 @@
  *     the last failure on the calling thread is available from
  *     fh_last_error(). Launch errors are reported as FH_ERR_CUDA.
  *   - stream is a cudaStream_t (NULL = legacy default stream).
+ *   - Hidden-state pointers (device ones, and page-locked host ones read by
+ *     the kernels directly) must be 16-byte aligned; misaligned ones are
+ *     refused with FH_ERR_INVALID_ARGUMENT by every entry point that takes
+ *     them.
  *   - Ties: probe selection prefers the smaller cluster id, the greedy token
  *     the smaller vocab id (fused.py:161-163).
  */

@@ -167,6 +167,36 @@ def probe_set_within_tolerance(mine: np.ndarray, ref: np.ndarray,
     return all(abs(scores[c] - kth) <= band for c in diff)
 
 
+def probe_rule_vs_reference_list(mine: np.ndarray, ref_probes: np.ndarray, top_vals: np.ndarray,
+                                 top_ids: np.ndarray, rtol: float = 1e-2):
+    """The probe-set rule judged on the reference's own scores.
+
+    top_vals / top_ids: the reference's largest bf16 scores of the row
+    (descending) with their cluster ids, at least p + 1 of them; every cluster
+    not listed scores at most top_vals[-1]. Returns (ok, recall, n_outside):
+    ok when every cluster in exactly one of the two sets scores within rtol of
+    the p-th score (a cluster of `mine` missing from the list counts as
+    outside the band unless the list's last score is still inside it);
+    recall = |mine & ref| / p.
+    """
+    mine = set(int(x) for x in mine)
+    ref = set(int(x) for x in ref_probes)
+    p = len(ref)
+    kth = float(top_vals[p - 1])
+    band = rtol * max(abs(kth), 1e-30)
+    score = {int(c): float(v) for c, v in zip(top_ids, top_vals)}
+    last = float(top_vals[-1])
+    outside = 0
+    for c in mine.symmetric_difference(ref):
+        v = score.get(c)
+        if v is None:
+            outside += not (abs(last - kth) <= band)
+        else:
+            outside += not (abs(v - kth) <= band)
+    recall = len(mine & ref) / p
+    return len(mine) == p and outside == 0, recall, outside
+
+
 # ----------------------------------------------------------------------------
 # Stage 2: block-sparse logits + argmax (fused.py:119-188, flash_head.py:223-261)
 # ----------------------------------------------------------------------------

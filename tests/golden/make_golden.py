@@ -13,6 +13,10 @@ derives the clustering, and the module is cast to bf16 (loading.py:152-164),
 on CPU instead of CUDA.
 
 Usage:  python tests/golden/make_golden.py [--reference-src DIR] [--only NAME]
+
+The reference source tree (the directory holding its ``flash_head`` package)
+comes from ``--reference-src`` or the ``FLASHHEAD_REFERENCE_SRC`` environment
+variable.
 """
 
 from __future__ import annotations
@@ -45,7 +49,8 @@ def _load_synthetic():
 
 
 _syn = _load_synthetic()
-HeadShape, LLAMA32_1B, QWEN25_15B = _syn.HeadShape, _syn.LLAMA32_1B, _syn.QWEN25_15B
+HeadShape, LLAMA32_1B, LLAMA31_8B, QWEN25_15B = (_syn.HeadShape, _syn.LLAMA32_1B,
+                                                 _syn.LLAMA31_8B, _syn.QWEN25_15B)
 head_checksum, make_head, make_hidden, save_assets = (
     _syn.head_checksum, _syn.make_head, _syn.make_hidden, _syn.save_assets)
 
@@ -163,6 +168,55 @@ def config_a(ref_fh, ref_loading, out, rows=8):
                    "checksum": head_checksum(head)}, f, indent=1)
 
 
+def _top_list(sims_bf16: torch.Tensor, n: int):
+    """The n largest bf16 scores of one row (largest first, ties to the smaller
+    cluster id) as (uint16 bits, uint16 ids)."""
+    v = sims_bf16.float().numpy().astype(np.float64)
+    order = np.lexsort((np.arange(v.size), -v))[:n]
+    return _bits(sims_bf16[torch.from_numpy(order)]), order.astype(np.uint16)
+
+
+def batch_reference(ref_fh, ref_loading, out, name, shape, head_seed, hidden_seed, rows=256,
+                    extra=64):
+    """The reference's stage-1 and greedy outputs on `rows` N(0, 0.25) hidden
+    states: probe sets, the top p + extra bf16 scores with their ids (enough
+    to judge every cluster within 1e-2 of the p-th score), greedy tokens. The
+    hidden states are regenerated from their seed by the tests, so only a
+    checksum of them is stored."""
+    head = make_head(shape, seed=head_seed)
+    h = make_hidden(rows, shape.hidden, seed=hidden_seed)
+    fh = _reference_head(ref_fh, ref_loading, head, shape.n_probes, None)
+    top_bits, top_ids, probes, toks = [], [], [], []
+    t0 = time.time()
+    with torch.no_grad():
+        for r in range(rows):
+            x = h[r].view(1, 1, -1)
+            b, i = _top_list(fh.cluster_linear(x).view(-1), shape.n_probes + extra)
+            top_bits.append(b)
+            top_ids.append(i)
+            probes.append(np.sort(fh._get_top_clusters(x).view(-1).numpy()).astype(np.uint16))
+            toks.append(_reference_greedy(fh, x))
+    print(f"{name}: {rows} reference rows in {time.time() - t0:.0f}s", flush=True)
+    np.savez_compressed(os.path.join(out, name + ".npz"), ref_top_bits=np.stack(top_bits),
+                        ref_top_ids=np.stack(top_ids), ref_probes=np.stack(probes),
+                        ref_tok_greedy=np.array(toks, dtype=np.int64))
+    hsum = h.float()
+    with open(os.path.join(out, name + ".json"), "w") as f:
+        json.dump({"shape": shape.__dict__, "head_seed": head_seed, "hidden_seed": hidden_seed,
+                   "rows": rows, "checksum": head_checksum(head),
+                   "hidden_checksum": [float(hsum.sum()), float(hsum.abs().sum())]}, f, indent=1)
+
+
+def config_b_batch(ref_fh, ref_loading, out):
+    """Llama-3.2-1B-shaped head of configs A/B (head seed 0), 256 rows."""
+    batch_reference(ref_fh, ref_loading, out, "config_b_batch", LLAMA32_1B, 0, 21)
+
+
+def config_c_batch(ref_fh, ref_loading, out):
+    """Llama-3.1-8B-shaped head of config C (D=4096, head seed 5), 256 rows."""
+    batch_reference(ref_fh, ref_loading, out, "config_c_batch", LLAMA31_8B, 5, 22)
+
+
 def config_d_sample(ref_fh, ref_loading, out, draws_per_row=50000, temperature=0.8):
     """Qwen2.5-1.5B-shaped head, sampling at T=0.8: 2 rows x 50k draws = 1e5."""
     shape = QWEN25_15B
@@ -192,13 +246,16 @@ def config_d_sample(ref_fh, ref_loading, out, draws_per_row=50000, temperature=0
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default="/root/reference/src")
+    ap.add_argument("--reference-src", default=os.environ.get("FLASHHEAD_REFERENCE_SRC"))
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.reference_src:
+        raise SystemExit("give --reference-src or set FLASHHEAD_REFERENCE_SRC")
     ref_fh, ref_loading = _import_reference(args.reference_src)
     torch.set_num_threads(os.cpu_count())
     jobs = {"small_greedy": small_greedy, "small_sample": small_sample,
-            "config_a": config_a, "config_d_sample": config_d_sample}
+            "config_a": config_a, "config_d_sample": config_d_sample,
+            "config_b_batch": config_b_batch, "config_c_batch": config_c_batch}
     for name, fn in jobs.items():
         if args.only and name != args.only:
             continue

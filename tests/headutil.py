@@ -43,8 +43,10 @@ class OracleView:
         self.K, self.cap, self.D = fh._K, fh._cap, fh._D
         self.vm = fh.vocab_maps.cpu().numpy()
         self.w_perm = to_np_f32(fh.w_perm)
-        self.W = np.empty((self.K * self.cap, self.D), dtype=np.float32)
-        self.W[self.vm.reshape(-1)] = self.w_perm.reshape(-1, self.D)
+        flat = self.vm.reshape(-1)
+        self.slot = np.empty(flat.size, dtype=np.int64)  # vocab id -> w_perm row
+        self.slot[flat] = np.arange(flat.size)
+        self._W = None
         self.cw, self.cscale = self._matrix(b["cluster_w"], b["cluster_scale"])
         self.sw, self.sscale = self._matrix(b["centroid_w"], b["centroid_scale"])
         self.specials = fh.special_token_ids_tensor.cpu().numpy()
@@ -56,6 +58,13 @@ class OracleView:
             return q, scale.cpu().numpy().astype(np.float64)
         return to_np_f32(w), None
 
+    @property
+    def W(self) -> np.ndarray:
+        """[V, D] rows in vocab order (built on first use: large heads)."""
+        if self._W is None:
+            self._W = self.w_perm.reshape(-1, self.D)[self.slot]
+        return self._W
+
     def scores(self, H: np.ndarray) -> np.ndarray:
         return O.cluster_scores(H, self.cw, self.cscale)
 
@@ -63,7 +72,8 @@ class OracleView:
         return O.cluster_scores(H, self.sw, self.sscale)
 
     def logit(self, h: np.ndarray, v: int) -> float:
-        return float(self.W[v].astype(np.float64) @ h.astype(np.float64))
+        row = self.w_perm.reshape(-1, self.D)[self.slot[v]]
+        return float(row.astype(np.float64) @ h.astype(np.float64))
 
     def greedy_given_probes(self, h, probes):
         vids, logits = O.candidate_logits(h, self.w_perm, self.vm, probes, self.specials)

@@ -8,7 +8,9 @@ point runs the same kernels on a fixed scratch array that the library owns.
 
 Checked here through the C ABI: two calls in a row give the ids of the
 workspace entry point (identical to its three-kernel path; within the tests'
-1e-5 logit tolerance of its default one-kernel path), zero rows is a no-op,
+1e-5 logit tolerance of its default one-kernel path) and the oracle's greedy
+token on the same fp8 stage-1 matrix (probe sets and the token within the
+tests' 1e-4 score / 1e-5 logit tolerances), zero rows is a no-op,
 and sizes beyond the fixed limits are refused with FH_ERR_UNSUPPORTED. The
 file is named to be collected last and needs no other test to run first.
 """
@@ -19,7 +21,7 @@ import numpy as np
 import pytest
 import torch
 
-from headutil import OracleView, build_head, to_np_f32
+from headutil import OracleView, build_head, check_greedy_rows, to_np_f32
 from oracle import flashhead_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -58,6 +60,13 @@ def test_noalloc_matches_the_workspace_entry_point(head):
         Hn = to_np_f32(H)
         for r, tok in enumerate(got.cpu().numpy()):
             assert O.token_within_tolerance(tok, default[r], lambda v: ov.logit(Hn[r], v), 1e-5)
+        # directly against the oracle: the token is the argmax of the oracle's
+        # candidates for the kernels' probe set, which is the oracle's top-p
+        check_greedy_rows(head, H, got.cpu().numpy(), nh.top_clusters(H).cpu().numpy())
+        for r in range(rows):
+            want, _, _ = ov.greedy(Hn[r])
+            assert O.token_within_tolerance(int(got[r]), want, lambda v: ov.logit(Hn[r], v),
+                                            1e-5), (r, int(got[r]), want)
 
 
 def test_noalloc_limits(head):
