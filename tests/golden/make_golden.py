@@ -200,11 +200,13 @@ def batch_reference(ref_fh, ref_loading, out, name, shape, head_seed, hidden_see
     np.savez_compressed(os.path.join(out, name + ".npz"), ref_top_bits=np.stack(top_bits),
                         ref_top_ids=np.stack(top_ids), ref_probes=np.stack(probes),
                         ref_tok_greedy=np.array(toks, dtype=np.int64))
-    hsum = h.float()
+    b = h.view(torch.int16).to(torch.int64)  # exact: integer sums of the bf16 bits
+    idx = torch.arange(b.numel(), dtype=torch.int64).view_as(b)
     with open(os.path.join(out, name + ".json"), "w") as f:
         json.dump({"shape": shape.__dict__, "head_seed": head_seed, "hidden_seed": hidden_seed,
                    "rows": rows, "checksum": head_checksum(head),
-                   "hidden_checksum": [float(hsum.sum()), float(hsum.abs().sum())]}, f, indent=1)
+                   "hidden_checksum": [int(b.sum()), int((b * (idx % 65521)).sum())]}, f,
+                  indent=1)
 
 
 def config_b_batch(ref_fh, ref_loading, out):
