@@ -25,12 +25,6 @@ LIB_PATH = os.path.join(PKG_ROOT, "flash_head", "libflashhead_b200.so")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
-def cuda_lib_dir() -> str:
-    """Directory of the toolkit's libcublasLt (stage-1 GEMM of batched steps)."""
-    root = os.path.dirname(os.path.dirname(os.path.realpath(nvcc_path())))
-    return os.path.join(root, "lib64")
-
-
 def nvcc_path() -> str:
     cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     if not os.path.exists(cand):
@@ -57,7 +51,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     cmd = [nvcc_path(), "-O3", "-std=c++17", *ARCH_FLAGS, "-lineinfo",
            "-Xcompiler", "-fPIC,-fvisibility=hidden,-O3", "-shared", "-cudart", "static",
            "-I", INCLUDE, "-o", tmp, os.path.join(CSRC, "flashhead.cu"), "-lrt", "-ldl",
-           "-lpthread", "-lcublasLt", "-Xlinker", "-rpath=" + cuda_lib_dir()]
+           "-lpthread"]
     if ptxas_info:
         cmd.insert(1, "-Xptxas=-v")
     if verbose:

@@ -1,11 +1,10 @@
 // Batched decode steps (rows >= kBatchMinRows): the kernels around the
-// stage-1 GEMM, which is a plain library GEMM (cuBLASLt, tensor cores) at
-// these batch sizes.
+// tensor-core stage 1 (fh_s1_tc.cuh).
 //
-//   k_score_epilogue  scores[r][k] = raw * scale[k] (fp8 rows), and in
-//                     sampling mode / T + Gumbel(stage 1, r, k): the same
-//                     keys the one-kernel and three-kernel paths compute.
-//   k_select          (fh_kernels.cuh) top-p clusters per row.
+//   k_select_hist     per row: the stage-1 keys from the split partials
+//                     (sum, fp8 row scale, and in sampling mode / T +
+//                     Gumbel(stage 1, r, k): the keys the one-kernel and
+//                     three-kernel paths compute), then the top-p clusters.
 //   k_inv_*           inverted index: for every probed cluster the rows that
 //                     probed it, cut into items of up to kInvRows rows.
 //   k_stage2_inv      persistent: every item streams its cluster's w_perm rows
@@ -30,8 +29,8 @@ namespace fh {
 // row's clusters with more memory-level parallelism at that size.
 constexpr int kBatchMinRows = 16;
 // From this many rows (below kBatchMinRows) the three-kernel path scores
-// stage 1 with the cuBLASLt GEMM + k_select_hist instead of the CUDA-core
-// k_scores + k_select.
+// stage 1 with the tensor-core kernel k_s1_tc + k_select_hist instead of the
+// CUDA-core k_scores + k_select.
 #ifndef FH_GEMM_S1_MIN_ROWS
 #define FH_GEMM_S1_MIN_ROWS 5
 #endif
@@ -54,27 +53,6 @@ struct InvItem {
   int pad[6];
 };
 static_assert(sizeof(InvItem) == 64, "item descriptor is one 64-byte line");
-
-// ---------------------------------------------------------------------------
-// Stage-1 keys from the GEMM's raw dot products.
-// ---------------------------------------------------------------------------
-// grid (ceil(K / (4 * blockDim)), rows): four clusters per thread.
-__global__ void k_score_epilogue(float *scores, int stride, int rows, int K, const float *scale,
-                                 int do_sample, float temperature, RngKey rng) {
-  const int r = blockIdx.y;
-  const int k0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
-  if (r >= rows || k0 >= K) return;
-  float *p = scores + (size_t)r * stride + k0;
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int k = k0 + u;
-    if (k >= K) break;
-    float v = p[u];
-    if (scale) v *= __ldg(&scale[k]);
-    if (do_sample) v = v / temperature + gumbel(rng, kStageClusters, (uint32_t)r, (uint32_t)k);
-    p[u] = v;
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Top-p clusters of one row per CTA (1024 threads): the same rule as k_select
@@ -104,9 +82,27 @@ __host__ __device__ __forceinline__ size_t hsel_smem_bytes(int K) {
   return hsel_row_bytes(K) + (size_t)kHSelWarps * 256 * sizeof(uint32_t) + sizeof(HSelSmem);
 }
 
-__global__ void __launch_bounds__(kHSelThreads) k_select_hist(const float *scores, int stride, int K,
-                                                               int p, int32_t *probes) {
+struct HSelArgs {
+  const float *part;     // stage-1 partial dot products:
+  size_t split_stride;   //   part[s * split_stride + r * row_stride + k], s < splits,
+  int row_stride;        //   summed in split order
+  int splits;
+  int K;
+  int p;
+  const float *scale;    // [K] fp8 row scale, or null
+  int do_sample;         // keys: score / T + Gumbel(stage 1, row, global cluster id)
+  float temperature;
+  RngKey rng;
+  int cluster_base;      // global id of cluster 0 (noise, candidate words)
+  float *scores_out;     // [rows, out_stride] the keys as ranked, or null
+  int out_stride;
+  int32_t *probes;       // [rows, p] local cluster ids ascending, or null
+  long long *cand_out;   // [rows, p] signed packed (key, global id) words, or null
+};
+
+__global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
   extern __shared__ __align__(16) unsigned char hsm[];
+  const int K = a.K, p = a.p;
   float *sc = reinterpret_cast<float *>(hsm);
   uint32_t *wh = reinterpret_cast<uint32_t *>(hsm + hsel_row_bytes(K));  // [32][256]
   HSelSmem &S = *reinterpret_cast<HSelSmem *>(hsm + hsel_row_bytes(K) +
@@ -115,8 +111,19 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(const float *score
   for (int i = tid; i < kHSelWarps * 256; i += kHSelThreads) wh[i] = 0u;
   if (tid < 256) S.hist[tid] = 0u;
   if (tid == 0) S.n_bkt = 0;
-  const float *row = scores + (size_t)r * stride;
-  for (int k = tid; k < K; k += kHSelThreads) sc[k] = sanitize(__ldcg(&row[k]));
+  grid_dep_wait();  // the partials come from the stage-1 kernel before this one
+  grid_dep_launch();
+  const float *row = a.part + (size_t)r * a.row_stride;
+  for (int k = tid; k < K; k += kHSelThreads) {
+    float v = __ldcg(&row[k]);
+    for (int s = 1; s < a.splits; ++s) v += __ldcg(&row[(size_t)s * a.split_stride + k]);
+    if (a.scale) v *= __ldg(&a.scale[k]);
+    if (a.do_sample)
+      v = v / a.temperature +
+          gumbel(a.rng, kStageClusters, (uint32_t)r, (uint32_t)(a.cluster_base + k));
+    if (a.scores_out) a.scores_out[(size_t)r * a.out_stride + k] = v;
+    sc[k] = sanitize(v);
+  }
   __syncthreads();
   // level 1: coarse bins (key >> 24), one private histogram per warp
   for (int k = tid; k < K; k += kHSelThreads) atomicAdd(&wh[warp * 256 + (mono(sc[k]) >> 24)], 1u);
@@ -210,11 +217,15 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(const float *score
   }
   __syncthreads();
   const unsigned long long T = S.T;
-  int32_t *out = probes + (size_t)r * p;
+  int32_t *out = a.probes ? a.probes + (size_t)r * p : nullptr;
+  long long *cand = a.cand_out ? a.cand_out + (size_t)r * p : nullptr;
   block_ordered_compact(
       K, [&](int k) { return pack(sc[k], (uint32_t)k) >= T; },
       [&](int pos, int k) {
-        if (pos < p) out[pos] = k;
+        if (pos < p) {
+          if (out) out[pos] = k;
+          if (cand) cand[pos] = to_signed(pack(sc[k], (uint32_t)(a.cluster_base + k)));
+        }
       },
       S.warp_counts);
 }
@@ -222,10 +233,13 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(const float *score
 // ---------------------------------------------------------------------------
 // Inverted index.
 // ---------------------------------------------------------------------------
-__global__ void k_inv_count(const int32_t *probes, int rows, int p, int K, int *cnt) {
+// Probe lists hold cluster ids starting at `base` (a tensor-parallel shard's
+// first global id, else 0); ids outside [base, base + K) are not this head's
+// and are skipped.
+__global__ void k_inv_count(const int32_t *probes, int rows, int p, int K, int base, int *cnt) {
   const int n = rows * p;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int c = probes[i];
+    const int c = probes[i] - base;
     if (c >= 0 && c < K) atomicAdd(&cnt[c], 1);
   }
 }
@@ -291,11 +305,11 @@ __global__ void __launch_bounds__(1024) k_inv_build(const int *cnt, int K, int *
   }
 }
 
-__global__ void k_inv_scatter(const int32_t *probes, int rows, int p, int K, const int *off,
-                              int *cursor, int *list) {
+__global__ void k_inv_scatter(const int32_t *probes, int rows, int p, int K, int base,
+                              const int *off, int *cursor, int *list) {
   const int n = rows * p;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int c = probes[i];
+    const int c = probes[i] - base;
     if (c >= 0 && c < K) list[off[c] + atomicAdd(&cursor[c], 1)] = i / p;
   }
 }
@@ -647,10 +661,14 @@ __global__ void k_stage_in(uint4 *dst, const uint4 *src, int n16) {
     dst[i] = src[i];
 }
 
-__global__ void k_inv_finalize(unsigned long long *packed, int rows, int64_t *out_ids) {
+// Publish: ids (out_ids), or for a tensor-parallel shard the signed packed
+// words the ranks max-reduce (out_signed); then packed[] reset.
+__global__ void k_inv_finalize(unsigned long long *packed, int rows, int64_t *out_ids,
+                               long long *out_signed) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) {
     const unsigned long long w = packed[i];
-    out_ids[i] = w ? (int64_t)packed_id(w) : (int64_t)0xFFFFFFFFll;
+    if (out_signed) out_signed[i] = to_signed(w);
+    else out_ids[i] = w ? (int64_t)packed_id(w) : (int64_t)0xFFFFFFFFll;
     packed[i] = 0ull;
   }
 }

@@ -1,9 +1,11 @@
-// Dense head of a batched greedy call on the 5th-generation tensor cores:
+// Dense head of a batched call on the 5th-generation tensor cores:
 // logits = H (rows x D) . w_perm^T (D x V) by tcgen05.mma, with the argmax
 // (largest logit, then smallest vocab id, as packed words) folded into the
-// epilogue, so the [rows, V] logits never reach HBM. The reference runs this
-// branch above 10 rows as F.linear over w_perm + argmax
-// (src/flash_head/flash_head.py:292-301).
+// epilogue, so the [rows, V] logits never reach HBM. In sampling mode the
+// epilogue ranks logit / T + Gumbel noise instead (Gumbel-max: the argmax of
+// the perturbed keys is a draw from softmax(logit / T)). The reference runs
+// this branch above 10 rows as F.linear over w_perm + argmax or multinomial
+// (src/flash_head/flash_head.py:292-301, :263-275).
 //
 // One persistent CTA per SM, 10 warps:
 //   warp 0  lane 0 issues TMA tensor copies (128-byte swizzle) of the hidden
@@ -65,6 +67,10 @@ struct DenseTcArgs {
   unsigned long long *packed;  // [rows], max-folded
   uint32_t *err;
   uint32_t polls;
+  int do_sample;   // keys logit / T + Gumbel(stage 2, row_base + row, vocab id)
+  float temperature;
+  RngKey rng;
+  int row_base;    // global index of hidden row 0 of this launch (noise stream)
 };
 
 struct DenseTcCtrl {
@@ -150,6 +156,9 @@ __device__ __forceinline__ void mbar_arrive_cta(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// SAMPLE: rank Gumbel-perturbed keys (a.do_sample set) instead of logits; a
+// template parameter so the greedy epilogue carries no noise code.
+template <bool SAMPLE>
 __global__ void __launch_bounds__(kDtThreads, 1)
     k_dense_tc(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_w,
                DenseTcArgs a) {
@@ -313,8 +322,13 @@ __global__ void __launch_bounds__(kDtThreads, 1)
               for (int j = 0; j < 16; ++j) {
                 const int col = 16 * (c + u) + j;
                 if (col < n_valid) {
-                  const unsigned long long w =
-                      pack(sanitize(__uint_as_float(v[u][j])), (uint32_t)vid[col]);
+                  float key = sanitize(__uint_as_float(v[u][j]));
+                  if (SAMPLE)
+                    key = key / a.temperature +
+                          gumbel(a.rng, kStageTokens,
+                                 (uint32_t)(a.row_base + m * kDtMTile + 32 * q + lane),
+                                 (uint32_t)vid[col]);
+                  const unsigned long long w = pack(key, (uint32_t)vid[col]);
                   bst[m][j & 3] = w > bst[m][j & 3] ? w : bst[m][j & 3];
                 }
               }

@@ -6,7 +6,6 @@
 // graph. Kernels after the first of a call are launched with programmatic
 // dependent launch so that their CTAs are resident before their predecessor
 // finishes.
-#include <cublasLt.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
@@ -23,7 +22,7 @@
 
 #include "../../include/flashhead.h"
 #include "fh_batched.cuh"
-#include "fh_dense_tc.cuh"
+#include "fh_s1_tc.cuh"
 #include "fh_spec.cuh"
 
 namespace {
@@ -188,23 +187,13 @@ cudaError_t launch_fused(int hdt, int wdt, const fh::FusedArgs &a, int grid, cud
 
 }  // namespace
 
-// cuBLASLt objects of one GEMM shape: `rows` hidden states against `mat`
-// rows of a [*, D] weight matrix (the centroids, or blocks of w_perm).
-struct LtPlan {
-  int rows = 0, stride = 0, mat = 0;
-  bool sample = false;
-  cublasLtMatmulDesc_t op = nullptr;
-  cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
-  cublasLtMatmulAlgo_t algo;
-};
-
 struct fh_head {
   fh_head_desc d;
-  mutable cublasLtHandle_t lt = nullptr;  // created by the first batched call
-  mutable std::mutex plan_mutex;  // the plan cache fills on first use of a row count
-  mutable std::vector<LtPlan> plans;
+  mutable std::mutex plan_mutex;  // guards the tensor maps, encoded on first use
   mutable CUtensorMap tm_w;  // w_perm rows for the dense tensor-core kernel
   mutable int tm_w_tile = 0;  // its box height, 0: not encoded yet
+  mutable CUtensorMap tm_c[2];  // stage-1 matrices (cluster_w, centroid_w) for k_s1_tc
+  mutable bool tm_c_ok[2] = {false, false};
 };
 
 // ---------------------------------------------------------------------------
@@ -212,36 +201,35 @@ struct fh_head {
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr size_t kLtWorkspaceBytes = 8u << 20;  // cuBLASLt scratch of the batched GEMM
-constexpr size_t kDenseScratchBytes = 64u << 20;  // logits of one dense GEMM (rows >= 16)
+// Stage-1 tiling of the tensor-core kernel k_s1_tc: 128-row tiles of the
+// stage-1 matrix, each split over the hidden dimension so that tiles x splits
+// fills the SMs once; the splits' partial scores are summed by the selection.
+int s1_splits(const fh_head_desc &d) {
+  const int m_tiles = (d.n_clusters + fh::kS1MTile - 1) / fh::kS1MTile;
+  const int nk = (d.hidden + fh::kS1KBlock - 1) / fh::kS1KBlock;
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  return std::max(1, std::min(nk, sms / m_tiles));
+}
 
-// Dense head of a batched call: the cap K-row blocks of w_perm are multiplied
-// in GEMMs of `blocks` blocks each (as many as fit kDenseScratchBytes of f32
-// logits, balanced over the GEMMs); `stride` is the logits row pitch.
-struct DenseSplit {
-  int blocks, gemms, stride;
-};
-DenseSplit dense_split(const fh_head_desc &d, int rows) {
-  const size_t per_block = (size_t)rows * d.n_clusters * sizeof(float);
-  int g = (int)std::min<size_t>((size_t)d.cluster_size, std::max<size_t>(1, kDenseScratchBytes / per_block));
-  const int gemms = (d.cluster_size + g - 1) / g;
-  g = (d.cluster_size + gemms - 1) / gemms;
-  return DenseSplit{g, gemms, (int)round_up((size_t)g * d.n_clusters, 64)};
+// An fp8 stage-1 matrix is multiplied in f16: bf16 hidden rows need an f16 copy.
+bool s1_needs_h16(const fh_head_desc &d) {
+  return d.weight_dtype == FH_BF16 &&
+         (d.score_dtype == FH_FP8_E4M3 || (d.centroid_w && d.sample_dtype == FH_FP8_E4M3));
 }
 
 struct Workspace {
-  float *scores;                // [rows, score_stride]
+  float *scores;                // [splits][rows, score_stride]: stage-1 (partial) scores
   int score_stride;
+  int splits;                   // k_s1_tc partials held (1 below kGemmS1MinRows rows)
+  size_t split_stride;          // floats between two splits' partials
   int32_t *probes;              // [rows, p]
   unsigned long long *packed;   // [rows]
   unsigned *counter;            // [1]
   unsigned char *epoch_bufs;    // one-kernel histograms
-  // batched steps (rows >= kBatchMinRows) only, else null; lt_ws from
-  // kGemmS1MinRows rows
+  void *h16;                    // [rows, D] f16 copy of bf16 hidden rows (fp8 stage 1)
+  // batched steps (rows >= kBatchMinRows) only, else null
   int *inv_cnt, *inv_off, *inv_item_off, *inv_cursor, *inv_meta, *inv_list;
   fh::InvItem *inv_items;
-  void *lt_ws;
-  float *dense;                 // [rows, dense stride] logits of the dense GEMMs
   size_t bytes;                 // bytes needed for `rows`
 };
 
@@ -251,59 +239,53 @@ struct Workspace {
 // stage-2 accumulator packed[r].
 // Stage 2 leaves both zeroed when it completes, so a workspace zero-filled
 // once stays clean across calls with any row count. Per-call scratch
-// (probes, scores) is placed from the top of the buffer downwards and never
-// reaches the state of a call whose size check passed.
+// (probes, scores, the f16 hidden copy, the inverted index) is placed from
+// the top of the buffer downwards and never reaches the state of a call
+// whose size check passed.
 Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   Workspace w;
   char *p = reinterpret_cast<char *>(base);
   w.score_stride = (int)round_up((size_t)d.n_clusters, 64);
+  w.splits = rows >= fh::kGemmS1MinRows ? s1_splits(d) : 1;
+  w.split_stride = (size_t)rows * w.score_stride;
   const size_t state =
       256 + fh::kHistBytes + round_up((size_t)rows * sizeof(unsigned long long), 256);
   const size_t probes = round_up((size_t)rows * d.n_probes * sizeof(int32_t), 256);
-  const size_t scores = round_up((size_t)rows * w.score_stride * sizeof(float), 256);
-  // GEMM stage 1 (kGemmS1MinRows+ rows): cuBLASLt scratch; batched steps
-  // (kBatchMinRows+): also the inverted index and dense logits; below the scores
+  const size_t scores = round_up((size_t)w.splits * w.split_stride * sizeof(float), 256);
+  const size_t h16 = rows >= fh::kGemmS1MinRows && s1_needs_h16(d)
+                         ? round_up((size_t)rows * d.hidden * 2, 256)
+                         : 0;
   const bool batched = rows >= fh::kBatchMinRows;
-  const bool gemm = rows >= fh::kGemmS1MinRows;
   const size_t kint = round_up((size_t)d.n_clusters * sizeof(int), 256);
   const size_t n_pairs = (size_t)rows * d.n_probes;
   const size_t max_items = n_pairs / fh::kInvRows + (size_t)d.n_clusters + 1;
-  const size_t dense =
-      batched ? round_up((size_t)rows * dense_split(d, rows).stride * sizeof(float), 256) : 0;
-  const size_t inv = (batched ? 4 * kint + 256 + round_up(n_pairs * sizeof(int), 256) +
-                                    round_up(max_items * sizeof(fh::InvItem), 256) + dense
-                              : 0) +
-                     (gemm ? kLtWorkspaceBytes : 0);
-  w.bytes = state + probes + scores + inv + 256;
+  const size_t inv = batched ? 4 * kint + 256 + round_up(n_pairs * sizeof(int), 256) +
+                                   round_up(max_items * sizeof(fh::InvItem), 256)
+                             : 0;
+  w.bytes = state + probes + scores + h16 + inv + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
   w.epoch_bufs = reinterpret_cast<unsigned char *>(p + 256);
   w.packed = reinterpret_cast<unsigned long long *>(p + 256 + fh::kHistBytes);
   const size_t top = (ws_bytes / 256) * 256;
   const size_t probes_off = top >= probes ? top - probes : 0;
   const size_t scores_off = probes_off >= scores ? probes_off - scores : 0;
+  const size_t h16_off = scores_off >= h16 ? scores_off - h16 : 0;
   w.probes = reinterpret_cast<int32_t *>(p + probes_off);
   w.scores = reinterpret_cast<float *>(p + scores_off);
+  w.h16 = h16 ? p + h16_off : nullptr;
   w.inv_cnt = w.inv_off = w.inv_item_off = w.inv_cursor = w.inv_meta = w.inv_list = nullptr;
   w.inv_items = nullptr;
-  w.lt_ws = nullptr;
-  w.dense = nullptr;
-  if (gemm) {  // (batched implies gemm)
-    size_t q = scores_off >= inv ? scores_off - inv : 0;
-    if (batched) w.dense = reinterpret_cast<float *>(p + q);
-    q += dense;
-    w.lt_ws = p + q;
-    q += kLtWorkspaceBytes;
-    if (batched) {
-      w.inv_items = reinterpret_cast<fh::InvItem *>(p + q);
-      q += round_up(max_items * sizeof(fh::InvItem), 256);
-      w.inv_list = reinterpret_cast<int *>(p + q);
-      q += round_up(n_pairs * sizeof(int), 256);
-      w.inv_cnt = reinterpret_cast<int *>(p + q);
-      w.inv_off = reinterpret_cast<int *>(p + q + kint);
-      w.inv_item_off = reinterpret_cast<int *>(p + q + 2 * kint);
-      w.inv_cursor = reinterpret_cast<int *>(p + q + 3 * kint);
-      w.inv_meta = reinterpret_cast<int *>(p + q + 4 * kint);
-    }
+  if (batched) {
+    size_t q = h16_off >= inv ? h16_off - inv : 0;
+    w.inv_items = reinterpret_cast<fh::InvItem *>(p + q);
+    q += round_up(max_items * sizeof(fh::InvItem), 256);
+    w.inv_list = reinterpret_cast<int *>(p + q);
+    q += round_up(n_pairs * sizeof(int), 256);
+    w.inv_cnt = reinterpret_cast<int *>(p + q);
+    w.inv_off = reinterpret_cast<int *>(p + q + kint);
+    w.inv_item_off = reinterpret_cast<int *>(p + q + 2 * kint);
+    w.inv_cursor = reinterpret_cast<int *>(p + q + 3 * kint);
+    w.inv_meta = reinterpret_cast<int *>(p + q + 4 * kint);
   }
   return w;
 }
@@ -524,110 +506,32 @@ int run_fused(const fh_head *h, const void *hidden, int rows, bool sample, float
 }
 
 // ---------------------------------------------------------------------------
-// Batched steps (rows >= kBatchMinRows): cuBLASLt stage-1 GEMM, the selection
+// Batched steps (rows >= kBatchMinRows): tensor-core stage 1, the selection
 // kernel, the inverted index and the inverted stage 2.
-// ---------------------------------------------------------------------------
 bool batched_ok(const fh_head *h, int rows, bool sample, int min_rows = fh::kBatchMinRows) {
   const fh_head_desc &d = h->d;
   if (rows < min_rows || (d.flags & FH_FLAG_NO_FUSED)) return false;
-  if (!(sample ? d.centroid_w16 : d.cluster_w16) || d.cluster_base != 0) return false;
+  if (sample && !d.centroid_w) return false;
+  if (d.cluster_base != 0) return false;
   if (d.cluster_size > fh::kTileRows || (d.hidden * 2) % 128 != 0) return false;
   return sm_count() > 0;
 }
 
-const char *lt_status_name(cublasStatus_t st) {
-  switch (st) {
-    case CUBLAS_STATUS_NOT_INITIALIZED: return "not initialized";
-    case CUBLAS_STATUS_ALLOC_FAILED: return "allocation failed";
-    case CUBLAS_STATUS_INVALID_VALUE: return "invalid value";
-    case CUBLAS_STATUS_ARCH_MISMATCH: return "arch mismatch";
-    case CUBLAS_STATUS_EXECUTION_FAILED: return "execution failed";
-    case CUBLAS_STATUS_NOT_SUPPORTED: return "not supported";
-    default: return "error";
-  }
+// The inverted stage 2 (any shard): clusters of at most 16 rows of whole
+// 128-byte groups, and the index buffers of a workspace laid out for 16+ rows.
+bool inv_ok(const fh_head_desc &d, int rows) {
+  if (rows < fh::kBatchMinRows || (d.flags & FH_FLAG_NO_FUSED)) return false;
+  if (d.cluster_size > fh::kTileRows || (d.hidden * 2) % 128 != 0) return false;
+  return sm_count() > 0;
 }
 
-#define FH_CHECK_LT(expr, what)                                                           \
-  do {                                                                                    \
-    cublasStatus_t _st = (expr);                                                          \
-    if (_st != CUBLAS_STATUS_SUCCESS)                                                     \
-      return fail(FH_ERR_CUDA, "%s: cuBLASLt %s (%d)", what, lt_status_name(_st), (int)_st); \
-  } while (0)
-
-void destroy_plan(LtPlan &pl) {
-  if (pl.a) cublasLtMatrixLayoutDestroy(pl.a);
-  if (pl.b) cublasLtMatrixLayoutDestroy(pl.b);
-  if (pl.c) cublasLtMatrixLayoutDestroy(pl.c);
-  if (pl.op) cublasLtMatmulDescDestroy(pl.op);
-  pl.a = pl.b = pl.c = nullptr;
-  pl.op = nullptr;
-}
-
-// S^T (K x rows, column-major, ld = score_stride) = Wc (K x D) . H^T (D x rows):
-// the row-major [K, D] matrix is a column-major D x K operand taken transposed.
-int get_plan(const fh_head *h, int rows, bool sample, int stride, int mat, const LtPlan **out) {
-  std::lock_guard<std::mutex> lock(h->plan_mutex);
-  for (const LtPlan &pl : h->plans)
-    if (pl.rows == rows && pl.sample == sample && pl.stride == stride && pl.mat == mat) {
-      *out = &pl;
-      return FH_OK;
-    }
-  const fh_head_desc &d = h->d;
-  if (!h->lt) {
-    const cublasStatus_t ls = cublasLtCreate(&h->lt);
-    if (ls != CUBLAS_STATUS_SUCCESS) {
-      h->lt = nullptr;
-      return fail(FH_ERR_CUDA, "cuBLASLt handle: %s", lt_status_name(ls));
-    }
-  }
-  LtPlan pl;
-  pl.rows = rows;
-  pl.stride = stride;
-  pl.mat = mat;
-  pl.sample = sample;
-  const cudaDataType_t dt = d.weight_dtype == FH_BF16 ? CUDA_R_16BF : CUDA_R_16F;
-  int st = FH_OK;
-  do {
-    if (cublasLtMatmulDescCreate(&pl.op, CUBLAS_COMPUTE_32F, CUDA_R_32F) != CUBLAS_STATUS_SUCCESS) {
-      st = fail(FH_ERR_CUDA, "cuBLASLt matmul descriptor");
-      break;
-    }
-    const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
-    cublasLtMatmulDescSetAttribute(pl.op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta));
-    cublasLtMatmulDescSetAttribute(pl.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb));
-    if (cublasLtMatrixLayoutCreate(&pl.a, dt, d.hidden, mat, d.hidden) != CUBLAS_STATUS_SUCCESS ||
-        cublasLtMatrixLayoutCreate(&pl.b, dt, d.hidden, rows, d.hidden) != CUBLAS_STATUS_SUCCESS ||
-        cublasLtMatrixLayoutCreate(&pl.c, CUDA_R_32F, mat, rows, stride) !=
-            CUBLAS_STATUS_SUCCESS) {
-      st = fail(FH_ERR_CUDA, "cuBLASLt matrix layouts");
-      break;
-    }
-    cublasLtMatmulPreference_t pref = nullptr;
-    if (cublasLtMatmulPreferenceCreate(&pref) != CUBLAS_STATUS_SUCCESS) {
-      st = fail(FH_ERR_CUDA, "cuBLASLt preference");
-      break;
-    }
-    const size_t ws = kLtWorkspaceBytes;
-    cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws,
-                                         sizeof(ws));
-    cublasLtMatmulHeuristicResult_t res;
-    int n = 0;
-    const cublasStatus_t hs = cublasLtMatmulAlgoGetHeuristic(h->lt, pl.op, pl.a, pl.b, pl.c, pl.c,
-                                                             pref, 1, &res, &n);
-    cublasLtMatmulPreferenceDestroy(pref);
-    if (hs != CUBLAS_STATUS_SUCCESS || n < 1) {
-      st = fail(FH_ERR_UNSUPPORTED, "no cuBLASLt algorithm for the %d x %d GEMM", rows, mat);
-      break;
-    }
-    pl.algo = res.algo;
-  } while (false);
-  if (st != FH_OK) {
-    destroy_plan(pl);
-    return st;
-  }
-  h->plans.push_back(pl);
-  *out = &h->plans.back();
-  return FH_OK;
+// Stage 1 on the tensor cores (k_s1_tc) needs only 16-byte row pitches (the
+// tensor maps) and a selection that keeps a row in shared memory.
+bool s1_tc_ok(const fh_head_desc &d, bool sample) {
+  if (d.flags & FH_FLAG_NO_FUSED) return false;
+  if (sample && !d.centroid_w) return false;
+  if (d.n_clusters > fh::kSelMaxItems || d.hidden % 16 != 0) return false;
+  return sm_count() > 0;
 }
 
 cudaError_t prepare_select_hist() {
@@ -688,49 +592,192 @@ cudaError_t launch_stage2_inv(const fh::InvArgs &a, int grid, cudaStream_t s) {
                 a);
 }
 
-// Stage 1 of a batched step: GEMM scores (+ fp8 row scale, + sampling keys),
-// then the top-p clusters of every row into `probes` (if non-null).
-int run_batched_stage1(const fh_head *h, const void *hidden, int rows, bool sample,
-                       float temperature, uint64_t seed, uint64_t offset, const Workspace &w,
-                       float *scores, int stride, int32_t *probes, cudaStream_t s) {
+// cuTensorMapEncodeTiled from the driver, resolved once through the runtime
+// (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D map of a row-major [n_rows, D] 16-bit matrix: boxes of box_rows rows x
+// one k-block (kDtKBytes bytes) with the swizzle of that width, zero fill
+// outside the matrix.
+bool encode_rows_map(CUtensorMap *tm, const void *base, int dtype, int D, long long n_rows,
+                     int box_rows) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc || !aligned16(base)) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)n_rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)fh::kDtKBlock, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return enc(tm,
+             dtype == FH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+             2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             fh::kDtKBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D map of a row-major [K, D] stage-1 matrix for k_s1_tc: boxes of 128
+// rows x 64 elements; fp8 rows unswizzled (converted in shared memory),
+// 16-bit rows with the 128-byte swizzle the MMA reads; zero fill outside.
+bool encode_s1_map(CUtensorMap *tm, const void *base, int dtype, int D, int K) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc || !aligned16(base)) return false;
+  const bool fp8 = dtype == FH_FP8_E4M3;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)K};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * (fp8 ? 1 : 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)fh::kS1KBlock, (cuuint32_t)fh::kS1MTile};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUtensorMapDataType t = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                : dtype == FH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(tm, t, 2, const_cast<void *>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE,
+             fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t prepare_s1_tc() {
+  static bool done[128];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(fh::k_s1_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fh::kS1SmemMax);
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
+
+// Stage 1 of a call of kGemmS1MinRows+ rows on the tensor cores: partial
+// scores of every (128-cluster tile, hidden split) by k_s1_tc (one launch per
+// 256 hidden rows; bf16 rows against an fp8 matrix first get an f16 copy),
+// then one k_select_hist CTA per row sums the partials into the keys (fp8
+// row scale; sampling: / T + Gumbel), writes them to scores_out (if given,
+// row pitch out_stride) and selects the top-p clusters into probes and/or
+// the signed candidate words (global ids) into cand_out.
+int run_s1_tc(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+              uint64_t seed, uint64_t offset, const Workspace &w, float *scores_out,
+              int out_stride, int32_t *probes, long long *cand_out, cudaStream_t s) {
   const fh_head_desc &d = h->d;
-  const LtPlan *pl = nullptr;
-  int st = get_plan(h, rows, sample, stride, h->d.n_clusters, &pl);
-  if (st != FH_OK) return st;
-  const float alpha = 1.f, beta = 0.f;
-  FH_CHECK_LT(cublasLtMatmul(h->lt, pl->op, &alpha, sample ? d.centroid_w16 : d.cluster_w16,
-                             pl->a, hidden, pl->b, &beta, scores, pl->c, scores, pl->c, &pl->algo,
-                             w.lt_ws, kLtWorkspaceBytes, s),
-              "stage-1 GEMM");
-  const float *scale = sample ? d.centroid_scale : d.cluster_scale;
-  const int K = d.n_clusters;
-  if (scale || sample)
-    FH_CHECK_LAUNCH(launch(fh::k_score_epilogue, dim3((K + 1023) / 1024, rows), dim3(256), 0, s,
-                           false, scores, stride, rows, K, scale, sample ? 1 : 0, temperature,
-                           rng_key(seed, offset)),
-                    "stage-1 epilogue launch");
-  if (!probes) return FH_OK;
+  const int which = sample ? 1 : 0;
+  const int cdt = sample ? d.sample_dtype : d.score_dtype;
+  const void *cmat = sample ? d.centroid_w : d.cluster_w;
+  const bool fp8 = cdt == FH_FP8_E4M3;
+  if (w.splits != s1_splits(d)) return fail(FH_ERR_WORKSPACE, "workspace laid out for another split count");
+  {
+    std::lock_guard<std::mutex> lock(h->plan_mutex);
+    if (!h->tm_c_ok[which]) {
+      if (!encode_s1_map(&h->tm_c[which], cmat, cdt, d.hidden, d.n_clusters))
+        return fail(FH_ERR_UNSUPPORTED, "stage-1 matrix tensor map");
+      h->tm_c_ok[which] = true;
+    }
+  }
+  const CUtensorMap tm_c = h->tm_c[which];
+  // operand type of the MMA: f16 against fp8 rows, else the weight type
+  const bool mma_bf16 = !fp8 && d.weight_dtype == FH_BF16;
+  const void *hop = hidden;
+  bool pdl = false;
+  if (fp8 && d.weight_dtype == FH_BF16) {
+    if (!w.h16) return fail(FH_ERR_WORKSPACE, "no f16 staging for the hidden rows");
+    const int n8 = (int)((size_t)rows * d.hidden / 8);
+    FH_CHECK_LAUNCH(launch(fh::k_hidden_to_f16, dim3(grid_for(n8, 256)), dim3(256), 0, s, false,
+                           reinterpret_cast<const uint4 *>(hidden), reinterpret_cast<uint4 *>(w.h16),
+                           n8),
+                    "hidden f16 copy launch");
+    hop = w.h16;
+    pdl = true;
+  }
+  FH_CHECK_LAUNCH(prepare_s1_tc(), "stage-1 kernel attribute");
+  const int m_tiles = (d.n_clusters + fh::kS1MTile - 1) / fh::kS1MTile;
+  fh::S1TcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.K = d.n_clusters;
+  a.nk = (d.hidden + fh::kS1KBlock - 1) / fh::kS1KBlock;
+  a.splits = w.splits;
+  a.fp8 = fp8 ? 1 : 0;
+  a.split_stride = w.split_stride;
+  a.row_stride = w.score_stride;
+  a.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
+  a.polls = 1u << 22;
+  for (int r0 = 0; r0 < rows; r0 += fh::kS1MaxN) {
+    const int n = std::min(fh::kS1MaxN, rows - r0);
+    a.rows = n;
+    a.n_pad = (n + 15) / 16 * 16;
+    a.tmem_cols = 32;
+    while (a.tmem_cols < a.n_pad) a.tmem_cols *= 2;
+    const size_t sb = fh::s1tc_stage_bytes(a.n_pad, a.fp8);
+    a.stages = (int)std::min<size_t>((size_t)fh::kS1MaxStages,
+                                     ((size_t)fh::kS1SmemMax - 1024 - sizeof(fh::S1TcCtrl)) / sb);
+    if (a.stages < 2) return fail(FH_ERR_UNSUPPORTED, "stage-1 ring does not fit");
+    a.idesc = fh::s1tc_idesc(mma_bf16, a.n_pad);
+    a.part = w.scores + (size_t)r0 * w.score_stride;
+    CUtensorMap tm_h;
+    const char *hrow = reinterpret_cast<const char *>(hop) + (size_t)r0 * d.hidden * 2;
+    if (!encode_rows_map(&tm_h, hrow, mma_bf16 ? FH_BF16 : FH_FP16, d.hidden, n, a.n_pad))
+      return fail(FH_ERR_UNSUPPORTED, "hidden-state tensor map");
+    FH_CHECK_LAUNCH(launch(fh::k_s1_tc, dim3(m_tiles * a.splits), dim3(fh::kS1Threads),
+                           fh::s1tc_smem_bytes(a.n_pad, a.fp8, a.stages), s, pdl, tm_c, tm_h, a),
+                    "stage-1 tensor-core launch");
+    pdl = false;
+  }
+  if (!probes && !cand_out && !scores_out) return FH_OK;
   FH_CHECK_LAUNCH(prepare_select_hist(), "select kernel attribute");
+  fh::HSelArgs se;
+  memset(&se, 0, sizeof(se));
+  se.part = w.scores;
+  se.split_stride = w.split_stride;
+  se.row_stride = w.score_stride;
+  se.splits = w.splits;
+  se.K = d.n_clusters;
+  se.p = d.n_probes;
+  se.scale = sample ? d.centroid_scale : d.cluster_scale;
+  se.do_sample = sample ? 1 : 0;
+  se.temperature = temperature;
+  se.rng = rng_key(seed, offset);
+  se.cluster_base = d.cluster_base;
+  se.scores_out = scores_out;
+  se.out_stride = out_stride;
+  se.probes = probes;
+  se.cand_out = cand_out;
   FH_CHECK_LAUNCH(launch(fh::k_select_hist, dim3(rows), dim3(fh::kHSelThreads),
-                         fh::hsel_smem_bytes(K), s, false, (const float *)scores, stride, K,
-                         d.n_probes, probes),
+                         fh::hsel_smem_bytes(d.n_clusters), s, true, se),
                   "probe selection launch");
   return FH_OK;
 }
 
-int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
-                uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
-                cudaStream_t s) {
+// Stage 2 of a batched step for given probe lists (cluster ids from
+// probe_base): the inverted index (clusters -> the rows that probe them, in
+// items of up to kInvRows rows), the inverted stage 2 over it, the special
+// tokens, and the publish of ids (out_ids) or of signed packed words
+// (out_signed, tensor-parallel shards). packed[] must be zero on entry and is
+// zero again on return.
+int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+                   uint64_t seed, uint64_t offset, const Workspace &w, const int32_t *probes,
+                   int probe_base, int64_t *out_ids, long long *out_signed, cudaStream_t s) {
   const fh_head_desc &d = h->d;
-  int st = run_batched_stage1(h, hidden, rows, sample, temperature, seed, offset, w, w.scores,
-                              w.score_stride, w.probes, s);
-  if (st != FH_OK) return st;
   const fh::RngKey rng = rng_key(seed, offset);
   const int K = d.n_clusters, p = d.n_probes;
   FH_CHECK_LAUNCH(cudaMemsetAsync(w.inv_cnt, 0, (size_t)K * sizeof(int), s), "index reset");
   const long long pairs = (long long)rows * p;
   FH_CHECK_LAUNCH(launch(fh::k_inv_count, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
-                         (const int32_t *)w.probes, rows, p, K, w.inv_cnt),
+                         probes, rows, p, K, probe_base, w.inv_cnt),
                   "index count launch");
   FH_CHECK_LAUNCH(prepare_inv_build(), "index build attribute");
   FH_CHECK_LAUNCH(launch(fh::k_inv_build, dim3(1), dim3(1024), (size_t)K * sizeof(int), s, false,
@@ -738,8 +785,8 @@ int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, flo
                          K, w.inv_off, w.inv_item_off, w.inv_cursor, w.inv_meta),
                   "index build launch");
   FH_CHECK_LAUNCH(launch(fh::k_inv_scatter, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
-                         (const int32_t *)w.probes, rows, p, K, (const int *)w.inv_off,
-                         w.inv_cursor, w.inv_list),
+                         probes, rows, p, K, probe_base, (const int *)w.inv_off, w.inv_cursor,
+                         w.inv_list),
                   "index scatter launch");
   FH_CHECK_LAUNCH(launch(fh::k_inv_items, dim3(grid_for(K, 256)), dim3(256), 0, s, false,
                          (const int *)w.inv_cnt, (const int *)w.inv_off,
@@ -784,46 +831,21 @@ int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, flo
                       "special-token launch");
   }
   FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
-                         w.packed, rows, out_ids),
+                         w.packed, rows, out_ids, out_signed),
                   "finalize launch");
   return FH_OK;
 }
 
-// cuTensorMapEncodeTiled from the driver, resolved once through the runtime
-// (no link-time dependency on libcuda).
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static bool tried = false;
-  std::lock_guard<std::mutex> lock(g_attr_mutex);
-  if (!tried) {
-    tried = true;
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// 2-D map of a row-major [n_rows, D] 16-bit matrix: boxes of box_rows rows x
-// one k-block (kDtKBytes bytes) with the swizzle of that width, zero fill
-// outside the matrix.
-bool encode_rows_map(CUtensorMap *tm, const void *base, int dtype, int D, long long n_rows,
-                     int box_rows) {
-  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-  if (!enc || !aligned16(base)) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)n_rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)fh::kDtKBlock, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1u, 1u};
-  return enc(tm,
-             dtype == FH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-             2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             fh::kDtKBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+// Batched step (rows >= kBatchMinRows): tensor-core stage 1 + selection,
+// then the inverted stage 2.
+int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+                uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
+                cudaStream_t s) {
+  const int st = run_s1_tc(h, hidden, rows, sample, temperature, seed, offset, w, nullptr, 0,
+                           w.probes, nullptr, s);
+  if (st != FH_OK) return st;
+  return run_inv_stage2(h, hidden, rows, sample, temperature, seed, offset, w, w.probes, 0,
+                        out_ids, nullptr, s);
 }
 
 // Tiling of the dense tensor-core kernel: vocab tiles of n_tile slots (a
@@ -869,7 +891,10 @@ cudaError_t prepare_dense_tc() {
   if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_attr_mutex);
   if (!done[dev]) {
-    e = cudaFuncSetAttribute(fh::k_dense_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(fh::k_dense_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fh::kDtSmemMax);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fh::k_dense_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fh::kDtSmemMax);
     if (e != cudaSuccess) return e;
     done[dev] = true;
@@ -877,93 +902,67 @@ cudaError_t prepare_dense_tc() {
   return cudaSuccess;
 }
 
-// Greedy dense head in one tensor-core kernel (logits stay on chip). Returns
+// Dense head in one tensor-core kernel per 256 hidden rows (logits stay on
+// chip; greedy argmax, or Gumbel-max in sampling mode). Returns
 // FH_ERR_UNSUPPORTED without launching anything when the shape or the tensor
-// maps do not fit it; the caller then takes the GEMM + argmax route.
-int run_dense_tc(const fh_head *h, const void *hidden, int rows, int64_t *out_ids,
-                 const Workspace &w, cudaStream_t s) {
+// maps do not fit it; the caller then takes the block-sparse route over every
+// cluster.
+int run_dense_tc(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
+                 uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
+                 cudaStream_t s) {
   const fh_head_desc &d = h->d;
-  DenseTcPlan pl;
-  if ((d.flags & FH_FLAG_NO_FUSED) || d.cluster_base != 0 || !dense_tc_plan(d, rows, &pl))
+  if ((d.flags & FH_FLAG_NO_FUSED) || d.cluster_base != 0 || rows < fh::kBatchMinRows)
     return FH_ERR_UNSUPPORTED;
   const long long V = (long long)d.n_clusters * d.cluster_size;
-  CUtensorMap tm_w, tm_h;
-  {
-    std::lock_guard<std::mutex> lock(h->plan_mutex);
-    if (h->tm_w_tile != pl.n_tile) {
-      if (!encode_rows_map(&h->tm_w, d.w_perm, d.weight_dtype, d.hidden, V, pl.n_tile))
-        return FH_ERR_UNSUPPORTED;
-      h->tm_w_tile = pl.n_tile;
+  for (int r0 = 0; r0 < rows; r0 += fh::kDtMaxRows) {
+    const int n = std::min(fh::kDtMaxRows, rows - r0);
+    DenseTcPlan pl;
+    if (!dense_tc_plan(d, n, &pl)) return FH_ERR_UNSUPPORTED;
+    CUtensorMap tm_w, tm_h;
+    {
+      std::lock_guard<std::mutex> lock(h->plan_mutex);
+      if (h->tm_w_tile != pl.n_tile) {
+        if (!encode_rows_map(&h->tm_w, d.w_perm, d.weight_dtype, d.hidden, V, pl.n_tile))
+          return FH_ERR_UNSUPPORTED;
+        h->tm_w_tile = pl.n_tile;
+      }
+      tm_w = h->tm_w;
     }
-    tm_w = h->tm_w;
-  }
-  if (!encode_rows_map(&tm_h, hidden, d.weight_dtype, d.hidden, rows, fh::kDtMTile))
-    return FH_ERR_UNSUPPORTED;
-  FH_CHECK_LAUNCH(prepare_dense_tc(), "dense tensor-core kernel attribute");
-  fh::DenseTcArgs a;
-  a.rows = rows;
-  a.V = (int)V;
-  a.n_tile = pl.n_tile;
-  a.n_tiles = pl.n_tiles;
-  a.mt = pl.mt;
-  a.stages = pl.stages;
-  a.n_acc = pl.n_acc;
-  a.acc_stride = pl.acc_stride;
-  a.nk = (d.hidden + fh::kDtKBlock - 1) / fh::kDtKBlock;
-  a.idesc = fh::dense_tc_idesc(d.weight_dtype == FH_BF16, pl.n_tile);
-  a.vocab_map = d.vocab_map;
-  a.packed = w.packed;
-  a.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
-  a.polls = 1u << 22;
-  FH_CHECK_LAUNCH(launch(fh::k_dense_tc, dim3(pl.grid), dim3(fh::kDtThreads), pl.smem, s, false,
-                         tm_h, tm_w, a),
-                  "dense tensor-core launch");
-  FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
-                         w.packed, rows, out_ids),
-                  "finalize launch");
-  return FH_OK;
-}
-
-// Dense head for batched calls: GEMMs of the hidden rows against groups of
-// K-row blocks of w_perm into f32 logits, each folded into packed[] by
-// k_dense_block_argmax (the smallest-id tie rule of the packed words), then the
-// ids. The logits are exact f32 dot products of the 16-bit operands.
-bool dense_gemm_ok(const fh_head *h, int rows) {
-  const fh_head_desc &d = h->d;
-  return rows >= fh::kBatchMinRows && !(d.flags & FH_FLAG_NO_FUSED) && d.cluster_base == 0 &&
-         sm_count() > 0;
-}
-
-int run_dense_gemm(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
-                   uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
-                   cudaStream_t s) {
-  const fh_head_desc &d = h->d;
-  if (!sample) {
-    const int st = run_dense_tc(h, hidden, rows, out_ids, w, s);
-    if (st != FH_ERR_UNSUPPORTED) return st;
-  }
-  const DenseSplit sp = dense_split(d, rows);
-  const int K = d.n_clusters;
-  const size_t block_bytes = (size_t)K * d.hidden * 2;
-  const fh::RngKey rng = rng_key(seed, offset);
-  for (int j0 = 0; j0 < d.cluster_size; j0 += sp.blocks) {
-    const int n = (std::min(d.cluster_size, j0 + sp.blocks) - j0) * K;
-    const LtPlan *pl = nullptr;
-    const int st = get_plan(h, rows, false, sp.stride, n, &pl);
-    if (st != FH_OK) return st;
-    const float alpha = 1.f, beta = 0.f;
-    const void *wj = reinterpret_cast<const char *>(d.w_perm) + (size_t)j0 * block_bytes;
-    FH_CHECK_LT(cublasLtMatmul(h->lt, pl->op, &alpha, wj, pl->a, hidden, pl->b, &beta, w.dense,
-                               pl->c, w.dense, pl->c, &pl->algo, w.lt_ws, kLtWorkspaceBytes, s),
-                "dense GEMM");
-    const int splits = std::max(1, std::min(64, (4 * sm_count() + rows - 1) / rows));
-    FH_CHECK_LAUNCH(launch(fh::k_dense_block_argmax, dim3(rows, splits), dim3(256), 0, s, false,
-                           (const float *)w.dense, sp.stride, rows, n, d.vocab_map, j0 * K,
-                           sample ? 1 : 0, temperature, rng, w.packed),
-                    "dense argmax launch");
+    const char *hrow = reinterpret_cast<const char *>(hidden) + (size_t)r0 * d.hidden * 2;
+    if (!encode_rows_map(&tm_h, hrow, d.weight_dtype, d.hidden, n, fh::kDtMTile))
+      return FH_ERR_UNSUPPORTED;
+    FH_CHECK_LAUNCH(prepare_dense_tc(), "dense tensor-core kernel attribute");
+    fh::DenseTcArgs a;
+    memset(&a, 0, sizeof(a));
+    a.rows = n;
+    a.V = (int)V;
+    a.n_tile = pl.n_tile;
+    a.n_tiles = pl.n_tiles;
+    a.mt = pl.mt;
+    a.stages = pl.stages;
+    a.n_acc = pl.n_acc;
+    a.acc_stride = pl.acc_stride;
+    a.nk = (d.hidden + fh::kDtKBlock - 1) / fh::kDtKBlock;
+    a.idesc = fh::dense_tc_idesc(d.weight_dtype == FH_BF16, pl.n_tile);
+    a.vocab_map = d.vocab_map;
+    a.packed = w.packed + r0;
+    a.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
+    a.polls = 1u << 22;
+    a.do_sample = sample ? 1 : 0;
+    a.temperature = temperature;
+    a.rng = rng_key(seed, offset);
+    a.row_base = r0;
+    if (sample)
+      FH_CHECK_LAUNCH(launch(fh::k_dense_tc<true>, dim3(pl.grid), dim3(fh::kDtThreads), pl.smem,
+                             s, false, tm_h, tm_w, a),
+                      "dense tensor-core launch");
+    else
+      FH_CHECK_LAUNCH(launch(fh::k_dense_tc<false>, dim3(pl.grid), dim3(fh::kDtThreads), pl.smem,
+                             s, false, tm_h, tm_w, a),
+                      "dense tensor-core launch");
   }
   FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
-                         w.packed, rows, out_ids),
+                         w.packed, rows, out_ids, (long long *)nullptr),
                   "finalize launch");
   return FH_OK;
 }
@@ -998,8 +997,6 @@ int validate_desc(const fh_head_desc *d) {
   if (d->n_special < 0 || (d->n_special > 0 && !d->special_slots))
     return fail(FH_ERR_INVALID_ARGUMENT, "n_special=%d with null special_slots", d->n_special);
   if (d->cluster_base < 0) return fail(FH_ERR_INVALID_ARGUMENT, "cluster_base < 0");
-  if (!aligned16(d->cluster_w16) || !aligned16(d->centroid_w16))
-    return fail(FH_ERR_INVALID_ARGUMENT, "16-bit stage-1 copies must be 16-byte aligned");
   return FH_OK;
 }
 
@@ -1037,8 +1034,6 @@ FH_API int fh_head_create(const fh_head_desc *desc, fh_head **out) {
 
 FH_API int fh_head_destroy(fh_head *head) {
   if (head) {
-    for (LtPlan &pl : head->plans) destroy_plan(pl);
-    if (head->lt) cublasLtDestroy(head->lt);
   }
   delete head;
   return FH_OK;
@@ -1047,15 +1042,19 @@ FH_API int fh_head_destroy(fh_head *head) {
 FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample) {
   if (!head || rows <= 0) return 0;
   const fh_head_desc &d = head->d;
-  const bool epi = do_sample || (do_sample ? d.centroid_scale : d.cluster_scale);
-  if (batched_ok(head, rows, do_sample != 0)) {
-    // GEMM, [epilogue], select, index reset, count, build, scatter, items,
-    // stage 2, [specials], finalize
-    return 9 + (epi ? 1 : 0) + (d.n_special > 0 ? 1 : 0);
+  const bool sample = do_sample != 0;
+  const int cdt = sample ? d.sample_dtype : d.score_dtype;
+  // tensor-core stage 1: [f16 copy of bf16 rows], one k_s1_tc per 256 rows, select
+  const int s1 = (cdt == FH_FP8_E4M3 && d.weight_dtype == FH_BF16 ? 1 : 0) +
+                 (rows + fh::kS1MaxN - 1) / fh::kS1MaxN + 1;
+  if (batched_ok(head, rows, sample)) {
+    // stage 1, index reset (memset), count, build, scatter, items, stage 2,
+    // [specials], finalize
+    return s1 + 7 + (d.n_special > 0 ? 1 : 0);
   }
-  if (fused_ok(d, rows, do_sample != 0, sm_count())) return 1;
-  // GEMM, [epilogue], select, stage 2; or scores, select, stage 2
-  if (batched_ok(head, rows, do_sample != 0, fh::kGemmS1MinRows)) return 3 + (epi ? 1 : 0);
+  if (fused_ok(d, rows, sample, sm_count())) return 1;
+  // stage 1 + stage 2; or scores, select, stage 2
+  if (rows >= fh::kGemmS1MinRows && s1_tc_ok(d, sample)) return s1 + 1;
   return 3;
 }
 
@@ -1078,9 +1077,8 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
     return run_batched(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, s);
   if (fused_ok(head->d, rows, false, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, false, 1.f, 0, 0, out_ids, w, grid, s);
-  if (batched_ok(head, rows, false, fh::kGemmS1MinRows))
-    st = run_batched_stage1(head, hidden, rows, false, 1.f, 0, 0, w, w.scores, w.score_stride,
-                            w.probes, s);
+  if (rows >= fh::kGemmS1MinRows && s1_tc_ok(head->d, false))
+    st = run_s1_tc(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, 0, w.probes, nullptr, s);
   else
     st = run_stage1(head, hidden, rows, false, 1.f, 0, 0, w, nullptr, w.probes, nullptr, 0, s);
   if (st != FH_OK) return st;
@@ -1185,9 +1183,9 @@ FH_API int fh_get_next_token_sample(const fh_head *head, const void *hidden, int
     return run_batched(head, hidden, rows, true, temperature, seed, offset, out_ids, w, s);
   if (fused_ok(head->d, rows, true, grid) && aligned16(hidden))
     return run_fused(head, hidden, rows, true, temperature, seed, offset, out_ids, w, grid, s);
-  if (batched_ok(head, rows, true, fh::kGemmS1MinRows))
-    st = run_batched_stage1(head, hidden, rows, true, temperature, seed, offset, w, w.scores,
-                            w.score_stride, w.probes, s);
+  if (rows >= fh::kGemmS1MinRows && s1_tc_ok(head->d, true))
+    st = run_s1_tc(head, hidden, rows, true, temperature, seed, offset, w, nullptr, 0, w.probes,
+                   nullptr, s);
   else
     st = run_stage1(head, hidden, rows, true, temperature, seed, offset, w, nullptr, w.probes,
                     nullptr, 0, s);
@@ -1222,10 +1220,9 @@ FH_API int fh_top_clusters(const fh_head *head, const void *hidden, int rows, in
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
   // the stage 1 of the step the library runs for this many rows
-  if (batched_ok(head, rows, do_sample != 0, fh::kGemmS1MinRows))
-    return run_batched_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w,
-                              out_scores ? out_scores : w.scores,
-                              out_scores ? head->d.n_clusters : w.score_stride, out_probes, s);
+  if (rows >= fh::kGemmS1MinRows && s1_tc_ok(head->d, do_sample != 0))
+    return run_s1_tc(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, out_scores,
+                     head->d.n_clusters, out_probes, nullptr, s);
   return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, out_scores,
                     out_probes, nullptr, 0, s);
 }
@@ -1263,6 +1260,11 @@ FH_API int fh_stage2_next_token(const fh_head *head, const void *hidden, int row
   if (do_sample && (!(temperature > 0.f) || !std::isfinite(temperature)))
     return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // the stage 2 fh_get_next_token runs for this many rows
+  if (inv_ok(head->d, rows) && head->d.cluster_base == 0)
+    return run_inv_stage2(head, hidden, rows, do_sample != 0, do_sample ? temperature : 1.f, seed,
+                          offset, w, probes, 0, out_ids, nullptr, s);
   fh::Stage2Args a = stage2_args(head->d, hidden, rows);
   a.probes = probes;
   a.probe_stride = head->d.n_probes;
@@ -1274,7 +1276,6 @@ FH_API int fh_stage2_next_token(const fh_head *head, const void *hidden, int row
   a.temperature = do_sample ? temperature : 1.f;
   a.rng = rng_key(seed, offset);
   const int items = rows * (a.P + a.n_special);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (do_sample)
     FH_CHECK_LAUNCH((launch_stage2<int32_t, fh::kSample>(head->d.weight_dtype, a, items, s, false)),
                     "stage-2 launch");
@@ -1294,9 +1295,8 @@ FH_API int fh_dense_next_token(const fh_head *head, const void *hidden, int rows
     return fail(FH_ERR_INVALID_ARGUMENT, "temperature must be positive and finite");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
-  if (dense_gemm_ok(head, rows))
-    return run_dense_gemm(head, hidden, rows, do_sample != 0, temperature, seed, offset, out_ids, w,
-                          s);
+  st = run_dense_tc(head, hidden, rows, do_sample != 0, temperature, seed, offset, out_ids, w, s);
+  if (st != FH_ERR_UNSUPPORTED) return st;
   FH_CHECK_LAUNCH(launch(fh::k_fill_u64, dim3((rows + 255) / 256), dim3(256), 0, s, false,
                          w.packed, rows, 0ull),
                   "fill launch");
@@ -1388,7 +1388,12 @@ extern "C" FH_API int fh_get_next_token_noalloc(const fh_head *head, const void 
   w.probes = reinterpret_cast<int32_t *>(p + kNoAllocProbesOff);
   w.scores = reinterpret_cast<float *>(p + kNoAllocScoresOff);
   w.score_stride = (int)round_up((size_t)head->d.n_clusters, 64);
+  w.splits = 1;
+  w.split_stride = (size_t)rows * w.score_stride;
   w.epoch_bufs = nullptr;
+  w.h16 = nullptr;
+  w.inv_cnt = w.inv_off = w.inv_item_off = w.inv_cursor = w.inv_meta = w.inv_list = nullptr;
+  w.inv_items = nullptr;
   w.bytes = kNoAllocBytes;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // k_scores zeroes the accumulator and the counter before stage 2 uses them.
@@ -1538,6 +1543,9 @@ FH_API int fh_tp_local_candidates(const fh_head *head, const void *hidden, int r
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Workspace w = layout(head->d, rows, workspace, workspace_bytes);
+  if (rows >= fh::kGemmS1MinRows && s1_tc_ok(head->d, do_sample != 0))
+    return run_s1_tc(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, nullptr, 0,
+                     nullptr, reinterpret_cast<long long *>(cand), s);
   return run_stage1(head, hidden, rows, do_sample != 0, temperature, seed, offset, w, nullptr,
                     nullptr, reinterpret_cast<long long *>(cand), head->d.cluster_base, s);
 }
@@ -1573,6 +1581,10 @@ FH_API int fh_tp_select_and_score(const fh_head *head, const void *hidden, int r
   const size_t smem = (size_t)se.n_items * sizeof(unsigned long long);
   FH_CHECK_LAUNCH(launch(fh::k_select, dim3(rows), dim3(fh::kSelThreads), smem, s, false, se),
                   "global probe selection launch");
+  if (inv_ok(head->d, rows))  // the global probes this shard owns, cluster-major
+    return run_inv_stage2(head, hidden, rows, do_sample != 0, do_sample ? temperature : 1.f, seed,
+                          offset, w, w.probes, head->d.cluster_base, nullptr,
+                          reinterpret_cast<long long *>(best), s);
   fh::Stage2Args a = stage2_args(head->d, hidden, rows);
   a.probes = w.probes;
   a.probe_stride = head->d.n_probes;

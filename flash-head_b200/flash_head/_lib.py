@@ -61,8 +61,6 @@ class HeadDesc(ctypes.Structure):
         ("centroid_w", ctypes.c_void_p),
         ("centroid_scale", ctypes.c_void_p),
         ("special_slots", ctypes.c_void_p),
-        ("cluster_w16", ctypes.c_void_p),
-        ("centroid_w16", ctypes.c_void_p),
     ]
 
 

@@ -33,10 +33,7 @@ def derive_buffers(w_perm: torch.Tensor, vocab_maps: torch.Tensor, cluster_w: to
     w_perm [K, cap, D] (bf16/fp16), vocab_maps [K, cap], cluster_w [K, D]
     normalised centroids, centroids_dk [D, K] raw centroids, special_ids [S].
     Returns w_perm (flat rows), vocab_map int32 [K*cap], cluster_w (+scale),
-    centroid_w (+scale) as [K, D] rows, their copies in the weight dtype with
-    the same values (cluster_w16, centroid_w16: fp8 values are exact in 16
-    bits; the batched steps' tensor-core GEMM reads them), special_slots int32
-    [S].
+    centroid_w (+scale) as [K, D] rows, special_slots int32 [S].
     """
     dev, wdt = w_perm.device, w_perm.dtype
     K, cap, D = w_perm.shape
@@ -49,12 +46,9 @@ def derive_buffers(w_perm: torch.Tensor, vocab_maps: torch.Tensor, cluster_w: to
         if stage1_dtype == "fp8":
             bufs["cluster_w"], bufs["cluster_scale"] = quantize_rows_fp8(cw)
             bufs["centroid_w"], bufs["centroid_scale"] = quantize_rows_fp8(raw)
-            bufs["cluster_w16"] = bufs["cluster_w"].to(wdt).contiguous()
-            bufs["centroid_w16"] = bufs["centroid_w"].to(wdt).contiguous()
         else:
             bufs["cluster_w"], bufs["centroid_w"] = cw, raw
             bufs["cluster_scale"] = bufs["centroid_scale"] = None
-            bufs["cluster_w16"], bufs["centroid_w16"] = cw, raw
         # Slots of the special tokens: the vocab ids need not be a permutation
         # of [0, K*cap) (a tensor-parallel shard holds a subset of the vocab).
         sp = special_ids.to(device=dev, dtype=torch.int64)
@@ -80,8 +74,6 @@ def shard_buffers(bufs: dict, cap: int, lo: int, hi: int) -> dict:
     }
     for k in ("cluster_w", "centroid_w"):
         out[k] = bufs[k][lo:hi].contiguous()
-    for k in ("cluster_w16", "centroid_w16"):
-        out[k] = None if bufs.get(k) is None else bufs[k][lo:hi].contiguous()
     for k in ("cluster_scale", "centroid_scale"):
         out[k] = None if bufs[k] is None else bufs[k][lo:hi].contiguous()
     sp = bufs["special_slots"]
@@ -127,8 +119,6 @@ class NativeHead:
         d.centroid_w = bufs["centroid_w"].data_ptr()
         d.centroid_scale = _ptr(bufs["centroid_scale"])
         d.special_slots = _ptr(sp)
-        d.cluster_w16 = _ptr(bufs.get("cluster_w16"))
-        d.centroid_w16 = _ptr(bufs.get("centroid_w16"))
         self.desc = d
         self.lib = _lib.load_library()
         handle = ctypes.c_void_p()

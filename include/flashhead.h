@@ -102,14 +102,6 @@ typedef struct fh_head_desc {
   const void *centroid_w;
   const float *centroid_scale;
   const int32_t *special_slots;
-  /* Optional copies of cluster_w / centroid_w in weight_dtype with the same
-   * values (fp8 values are exact in 16 bits; the fp8 row scales still apply).
-   * When present, calls with >= 16 rows run stage 1 as a tensor-core GEMM
-   * (cuBLASLt) and stage 2 over an inverted cluster -> rows index. New in this
-   * library; the reference runs its dense head above 10 rows
-   * (flash_head.py:292-301). */
-  const void *cluster_w16;
-  const void *centroid_w16;
 } fh_head_desc;
 
 /* fh_head_desc.flags */
@@ -144,10 +136,12 @@ FH_API size_t fh_workspace_error_offset(void);
 /*
  * Kernel launches one fh_get_next_token / fh_get_next_token_sample call makes
  * for `rows` hidden states on the current device: 1 when the one-kernel step
- * applies (rows <= 4 and supported shapes), 3 for the three stage kernels
- * (5..15 rows, or unsupported shapes), and 10 to 11 for batched steps (16+
- * rows with cluster_w16 / centroid_w16: GEMM, selection, inverted index,
- * inverted stage 2).
+ * applies (rows <= 4 and supported shapes); from 5 rows stage 1 runs on the
+ * tensor cores ([an f16 copy of bf16 rows for an fp8 stage-1 matrix], one
+ * stage-1 kernel per 256 rows, the selection), followed for 5..15 rows by
+ * the block-sparse stage 2 and for 16+ rows by the inverted index (a memset
+ * and 4 kernels), the inverted stage 2, [the special tokens] and the id
+ * publish; 3 for the CUDA-core stage kernels (unsupported shapes).
  */
 FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample);
 
@@ -260,10 +254,10 @@ FH_API int fh_stage2_next_token(const fh_head *head, const void *hidden,
 /*
  * Full-vocabulary next token over w_perm (greedy, or sampled at temperature
  * when do_sample != 0). Replaces the dense branch of get_next_token for
- * hidden_states.shape[0] > 10 (flash_head.py:292-301). Greedy calls of 16..256
- * rows run one tcgen05 GEMM + argmax kernel (the logits stay on chip);
- * sampled calls of 16+ rows run cuBLASLt GEMMs into workspace logits and a
- * Gumbel-max pass; fewer rows run the block-sparse stage 2 over every cluster.
+ * hidden_states.shape[0] > 10 (flash_head.py:292-301). Calls of 16+ rows run
+ * one tcgen05 GEMM kernel per 256 rows with the argmax (or, sampling, the
+ * Gumbel-max) in its epilogue, so the logits stay on chip; fewer rows run the
+ * block-sparse stage 2 over every cluster.
  * Ties go to the smallest vocab id; logits are f32 sums of the 16-bit
  * products, so ids equal the exact argmax up to f32 rounding of near-ties.
  */

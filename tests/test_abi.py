@@ -117,16 +117,20 @@ def test_valid_descriptor_and_workspace_size(lib):
             return (x + 255) // 256 * 256
         for rows in (1, 8, 256):
             hist = 2 * 4 * (256 + 65536) * 4  # two epochs of 4 rows' histograms
-            want = 256 + hist + rnd(rows * 8) + rnd(rows * 256 * 4) + rnd(rows * 8064 * 4) + 256
-            if rows >= 5:  # GEMM stage 1: cuBLASLt scratch
-                want += 8 << 20
-            if rows >= 16:  # batched steps: inverted index, item list, dense logits
-                K, pairs, cap = 8016, rows * 256, 16
-                g = min(cap, max(1, (64 << 20) // (rows * K * 4)))  # w_perm blocks per dense GEMM
-                g = -(-cap // -(-cap // g))
-                dense = rnd(rows * ((g * K + 63) // 64 * 64) * 4)
-                want += (4 * rnd(K * 4) + 256 + rnd(pairs * 4) + rnd((pairs // 8 + K + 1) * 64)
-                         + dense)
+            # tensor-core stage 1 from 5 rows: partial scores of every split of
+            # the hidden dimension (tiles x splits fill the SMs once; no GPU
+            # here, so the library assumes 148), and an f16 copy of the bf16
+            # hidden rows for the fp8 stage-1 matrix
+            splits = 1
+            if rows >= 5:
+                splits = max(1, min(2048 // 64, 148 // ((8016 + 127) // 128)))
+            want = (256 + hist + rnd(rows * 8) + rnd(rows * 256 * 4)
+                    + rnd(splits * rows * 8064 * 4) + 256)
+            if rows >= 5:
+                want += rnd(rows * 2048 * 2)
+            if rows >= 16:  # batched steps: inverted index and item list
+                K, pairs = 8016, rows * 256
+                want += 4 * rnd(K * 4) + 256 + rnd(pairs * 4) + rnd((pairs // 8 + K + 1) * 64)
             assert lib.fh_workspace_bytes(h, rows) == want
         assert lib.fh_workspace_bytes(None, 1) == 0
     finally:

@@ -2,10 +2,11 @@
 
 Each rank keeps only its contiguous cluster range; the step exchanges the
 [rows, p] candidate words with one all-gather and the [rows] packed winners
-with one MAX all-reduce. Both ranks must return the ids of the unsharded head
-(three-kernel path, the same stage kernels as the shards), greedy and
-sampling. Skipped unless two GPUs are visible. The process group has a short
-timeout so a failing peer ends the test with an error instead of a hang.
+with one MAX all-reduce. Both ranks must return the same ids, those of the
+unsharded head up to fp32 near-ties, greedy and sampling, at 6 rows and at
+40 rows (tensor-core stage 1, inverted stage 2). Skipped unless two GPUs are
+visible. The process group has a short timeout so a failing peer ends the
+test with an error instead of a hang.
 """
 
 from __future__ import annotations
@@ -56,13 +57,16 @@ def _worker(rank, world, port, result_q):
                                                  device=torch.device("cuda", rank))
         nh = fh.native()
         twin = NativeHead(nh.bufs, nh.D, nh.cap, nh.p, flags=_lib.FH_FLAG_NO_FUSED)
-        H = make_hidden(6, shape.hidden, seed=72, device="cuda", std=2.0)
         out = {}
-        for do_sample in (False, True):
-            kw = dict(do_sample=do_sample, temperature=0.8, seed=13, offset=4)
-            got = shard.get_next_token_batched(H, **kw)
-            want = twin.next_token(H, **kw)
-            out[do_sample] = (got.tolist(), want.tolist())
+        # 6 rows: three-kernel shard steps; 40 rows: tensor-core stage 1 and
+        # the inverted stage 2 over the owned probes
+        for rows, ref in ((6, twin), (40, nh)):
+            H = make_hidden(rows, shape.hidden, seed=72 + rows, device="cuda", std=2.0)
+            for do_sample in (False, True):
+                kw = dict(do_sample=do_sample, temperature=0.8, seed=13, offset=4)
+                got = shard.get_next_token_batched(H, **kw)
+                want = ref.next_token(H, **kw)
+                out[(rows, do_sample)] = (got.tolist(), want.tolist())
         torch.cuda.synchronize()
         result_q.put((rank, out))
     finally:
@@ -90,5 +94,8 @@ def test_tp_two_gpus_nccl_matches_unsharded():
                 p_.kill()
     assert all(p_.exitcode == 0 for p_ in procs), [p_.exitcode for p_ in procs]
     for rank in (0, 1):
-        for do_sample, (got, want) in results[rank].items():
-            assert got == want, (rank, do_sample)
+        for key, (got, want) in results[rank].items():
+            # the shards' stage 1 sums other splits of the hidden dimension than
+            # the whole head's (fp32 order): at most one near-tie row may differ
+            assert sum(a != b for a, b in zip(got, want)) <= 1, (rank, key, got, want)
+        assert results[rank] == results[1 - rank]  # every rank returns the same ids
