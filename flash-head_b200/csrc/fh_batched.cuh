@@ -1,24 +1,13 @@
 // Batched decode steps (rows >= kBatchMinRows): the kernels around the
-// tensor-core stage 1 (fh_s1_tc.cuh).
+// tensor-core stage 1 (fh_s1_tc.cuh) and stage 2 (fh_stage2_tc.cuh).
 //
 //   k_select_hist     per row: the stage-1 keys from the split partials
 //                     (sum, fp8 row scale, and in sampling mode / T +
 //                     Gumbel(stage 1, r, k): the keys the one-kernel and
 //                     three-kernel paths compute), then the top-p clusters.
-//   k_inv_*           inverted index: for every probed cluster the rows that
-//                     probed it, cut into items of up to kInvRows rows.
-//   k_stage2_inv      persistent: every item streams its cluster's w_perm rows
-//                     (one bulk copy when the cluster fits a slot) and its
-//                     hidden rows into shared memory, scores them on the
-//                     tensor cores (mma.m16n8k16: 16 tokens x 4 rows x 2
-//                     parities per column set, two column sets per item, so
-//                     each row fragment serves 8 rows), and folds each row's
-//                     best (logit or Gumbel key, vocab id) into packed[row].
-//                     A cluster is read from HBM once per step however many
-//                     rows probed it; stage-2 HBM bytes are the distinct
-//                     probed clusters, as the roofline counts them.
 //   k_special_scores  the special tokens of every row into packed[row].
-//   k_inv_finalize    ids from packed[], then packed[] reset.
+//   k_inv_finalize    ids (or signed words of a shard) from packed[], then
+//                     packed[] reset.
 #pragma once
 
 #include "fh_fused.cuh"
@@ -36,23 +25,6 @@ constexpr int kBatchMinRows = 16;
 #endif
 constexpr int kGemmS1MinRows = FH_GEMM_S1_MIN_ROWS;
 static_assert(kGemmS1MinRows <= kBatchMinRows, "GEMM stage 1 covers the batched steps");
-constexpr int kInvRows = 8;          // hidden rows per item (two mma column sets)
-constexpr int kInvThreads = kFThreads;
-constexpr int kInvBlock = kFBlock;   // + producer / reducer warp
-constexpr int kInvSlots = 2;
-constexpr int kInvChunk = 4096;      // max bytes of a row per chunk
-// slot: 16 cluster rows + kInvRows hidden rows of one chunk
-constexpr int kInvSlotBytes = (kTileRows + kInvRows) * kInvChunk;
-constexpr int kInvPrefetch = 32;     // item descriptors fetched per producer round
-constexpr int kInvAhead = 4;         // items ahead whose cluster is prefetched into L2
-
-struct InvItem {
-  int cluster;  // stage-2 cluster id
-  int n;        // rows in this item (1..kInvRows)
-  int rows[kInvRows];
-  int pad[6];
-};
-static_assert(sizeof(InvItem) == 64, "item descriptor is one 64-byte line");
 
 // ---------------------------------------------------------------------------
 // Top-p clusters of one row per CTA (1024 threads): the same rule as k_select
@@ -228,380 +200,6 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
         }
       },
       S.warp_counts);
-}
-
-// ---------------------------------------------------------------------------
-// Inverted index.
-// ---------------------------------------------------------------------------
-// Probe lists hold cluster ids starting at `base` (a tensor-parallel shard's
-// first global id, else 0); ids outside [base, base + K) are not this head's
-// and are skipped.
-__global__ void k_inv_count(const int32_t *probes, int rows, int p, int K, int base, int *cnt) {
-  const int n = rows * p;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int c = probes[i] - base;
-    if (c >= 0 && c < K) atomicAdd(&cnt[c], 1);
-  }
-}
-
-// One CTA of 1024 threads: off[c] = sum of cnt before c, item_off[c] = sum
-// of ceil(cnt / kInvRows) before c, cursor[c] = 0, meta[0] = number of items.
-// Dynamic shared memory: K ints. Thread t scans the contiguous counts
-// [t * per, (t + 1) * per); thread totals meet in a two-level warp scan.
-__global__ void __launch_bounds__(1024) k_inv_build(const int *cnt, int K, int *off, int *item_off,
-                                                    int *cursor, int *meta) {
-  extern __shared__ int s_cnt[];
-  __shared__ int warp_a[32], warp_b[32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int c = tid; c < K; c += blockDim.x) s_cnt[c] = __ldcg(&cnt[c]);
-  __syncthreads();
-  const int per = (K + blockDim.x - 1) / blockDim.x;
-  const int c0 = min(K, tid * per), c1 = min(K, c0 + per);
-  int sa = 0, sb = 0;
-  for (int c = c0; c < c1; ++c) {
-    sa += s_cnt[c];
-    sb += (s_cnt[c] + kInvRows - 1) / kInvRows;
-  }
-  int ia = sa, ib = sb;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int ta = __shfl_up_sync(0xFFFFFFFFu, ia, o), tb = __shfl_up_sync(0xFFFFFFFFu, ib, o);
-    if (lane >= o) {
-      ia += ta;
-      ib += tb;
-    }
-  }
-  if (lane == 31) {
-    warp_a[warp] = ia;
-    warp_b[warp] = ib;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    int wa = lane < nw ? warp_a[lane] : 0, wb = lane < nw ? warp_b[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int ta = __shfl_up_sync(0xFFFFFFFFu, wa, o), tb = __shfl_up_sync(0xFFFFFFFFu, wb, o);
-      if (lane >= o) {
-        wa += ta;
-        wb += tb;
-      }
-    }
-    if (lane < nw) {  // exclusive warp offsets
-      warp_a[lane] = wa - (lane < nw ? warp_a[lane] : 0);
-      warp_b[lane] = wb - (lane < nw ? warp_b[lane] : 0);
-    }
-    if (lane == nw - 1) meta[0] = wb;
-  }
-  __syncthreads();
-  int oa = warp_a[warp] + ia - sa, ob = warp_b[warp] + ib - sb;
-  for (int c = c0; c < c1; ++c) {
-    const int v = s_cnt[c];
-    off[c] = oa;
-    item_off[c] = ob;
-    cursor[c] = 0;
-    oa += v;
-    ob += (v + kInvRows - 1) / kInvRows;
-  }
-}
-
-__global__ void k_inv_scatter(const int32_t *probes, int rows, int p, int K, int base,
-                              const int *off, int *cursor, int *list) {
-  const int n = rows * p;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int c = probes[i] - base;
-    if (c >= 0 && c < K) list[off[c] + atomicAdd(&cursor[c], 1)] = i / p;
-  }
-}
-
-// Item g of cluster c: rows list[off[c] + g * kInvRows ...].
-__global__ void k_inv_items(const int *cnt, const int *off, const int *item_off, const int *list,
-                            int K, InvItem *items) {
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < K; c += gridDim.x * blockDim.x) {
-    const int n = cnt[c];
-    for (int g = 0; g * kInvRows < n; ++g) {
-      InvItem it;
-      it.cluster = c;
-      it.n = min(kInvRows, n - g * kInvRows);
-#pragma unroll
-      for (int j = 0; j < kInvRows; ++j)
-        it.rows[j] = j < it.n ? list[off[c] + g * kInvRows + j] : 0;
-#pragma unroll
-      for (int j = 0; j < 6; ++j) it.pad[j] = 0;
-      items[item_off[c] + g] = it;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Stage 2 over the inverted index.
-// ---------------------------------------------------------------------------
-struct InvArgs {
-  const void *hidden;  // [rows, D]
-  int rows;
-  int D;
-  const void *w_perm;  // [K * cap, D]
-  const int32_t *vocab_map;
-  int K;
-  int cap;
-  const InvItem *items;
-  const int *meta;     // meta[0] = number of items
-  int do_sample;
-  float temperature;
-  RngKey rng;
-  unsigned long long *packed;  // [rows]
-  uint32_t *err;               // error bits (copy timeout)
-  uint32_t copy_polls;
-};
-
-struct InvChunk {
-  int cluster;  // -1: end of work; -2: invalid item (no data, no result)
-  int n;        // hidden rows
-  int rows[kInvRows];
-  int dc;
-  int last;
-  int vid_in_smem;
-};
-
-struct InvSmem {
-  uint64_t mbar[kInvSlots];
-  __align__(16) float part[2][kInvRows][kTileRows][kFWarps];
-  __align__(16) int vid[kInvSlots][kTileRows];
-  InvChunk desc[kInvSlots];
-  __align__(16) InvItem pre[kInvPrefetch];
-  uint32_t s_err;
-};
-
-constexpr size_t kInvSmemBytes = (size_t)kInvSlots * kInvSlotBytes + sizeof(InvSmem);
-
-template <typename HT>
-__global__ void __launch_bounds__(kInvBlock, 1) k_stage2_inv(InvArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char *ring = smem;
-  InvSmem &S = *reinterpret_cast<InvSmem *>(smem + (size_t)kInvSlots * kInvSlotBytes);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool producer = warp == kFWarps;
-  const int gq = lane >> 2, tq = lane & 3, odd = gq & 1;
-  if (tid == 0) {
-    for (int s = 0; s < kInvSlots; ++s) mbar_init(&S.mbar[s], 1);
-    fence_mbar_init();
-    S.s_err = 0u;
-  }
-  __syncthreads();
-
-  const int n_items = __ldg(&a.meta[0]);
-  const int G = gridDim.x, b = blockIdx.x;
-  const int i0 = (int)((long long)b * n_items / G), i1 = (int)((long long)(b + 1) * n_items / G);
-  const int rb = a.D * (int)sizeof(HT);
-  const int cb_max = rb < kInvChunk ? rb : kInvChunk;
-  const int ndc = (rb + cb_max - 1) / cb_max;
-  const int pitch = ndc == 1 ? rb : cb_max;  // cluster rows in a slot
-  const char *wp = reinterpret_cast<const char *>(a.w_perm);
-  const char *hs = reinterpret_cast<const char *>(a.hidden);
-
-  if (producer) {
-    // Warp-uniform producer state; lane 0 issues the copies. Item descriptors
-    // are fetched kInvPrefetch at a time into shared memory by the warp.
-    int item = i0, dc = 0, pre_base = i0 - kInvPrefetch;
-    auto produce = [&](int s) {
-      InvChunk d;
-      d.cluster = -1;
-      d.n = 0;
-      d.dc = 0;
-      d.last = 1;
-      d.vid_in_smem = 0;
-      if (item < i1) {
-        if (item >= pre_base + kInvPrefetch) {  // warp-uniform
-          pre_base = item;
-          __syncwarp();
-          for (int j = lane; j < kInvPrefetch && item + j < i1; j += 32) S.pre[j] = a.items[item + j];
-          __syncwarp();
-        }
-        const InvItem &it = S.pre[item - pre_base];
-        d.cluster = it.cluster;
-        d.n = max(0, min(it.n, kInvRows));
-        for (int j = 0; j < kInvRows; ++j) d.rows[j] = it.rows[j];
-        d.dc = dc;
-        d.last = dc == ndc - 1;
-        if (d.last) {
-          ++item;
-          dc = 0;
-        } else {
-          ++dc;
-        }
-      }
-      const bool valid = d.cluster >= 0 && d.cluster < a.K;
-      if (!valid && d.cluster != -1) {
-        d.cluster = -2;
-        d.n = 0;
-      }
-      if (lane != 0) return;
-      if (valid) {
-        const int cb = min(cb_max, rb - d.dc * cb_max);
-        const int src = d.cluster * a.cap;
-        const int *vsrc = a.vocab_map + src;
-        const bool vid_bulk =
-            d.last && ((reinterpret_cast<uintptr_t>(vsrc) & 15u) == 0) && (a.cap % 4 == 0);
-        d.vid_in_smem = vid_bulk ? 1 : 0;
-        S.desc[s] = d;
-        fence_proxy_async_smem();
-        uint32_t bytes = (uint32_t)(a.cap * cb + d.n * cb) + (vid_bulk ? (uint32_t)(a.cap * 4) : 0u);
-        mbar_expect_tx(&S.mbar[s], bytes);
-        unsigned char *dst = ring + (size_t)s * kInvSlotBytes;
-        const char *wsrc = wp + (size_t)src * rb + (size_t)d.dc * cb_max;
-        if (ndc == 1) {
-          const int per = (a.cap + kS2Pieces - 1) / kS2Pieces;  // rows per bulk copy
-          for (int r0 = 0; r0 < a.cap; r0 += per)
-            bulk_g2s(dst + (size_t)r0 * rb, wsrc + (size_t)r0 * rb,
-                     (uint32_t)(min(per, a.cap - r0) * rb), &S.mbar[s]);
-        } else {
-          for (int r = 0; r < a.cap; ++r)
-            bulk_g2s(dst + (size_t)r * pitch, wsrc + (size_t)r * rb, (uint32_t)cb, &S.mbar[s]);
-        }
-        unsigned char *hdst = dst + (size_t)kTileRows * pitch;
-#pragma unroll
-        for (int j = 0; j < kInvRows; ++j) {
-          if (j < d.n) {
-            const int row = min(max(d.rows[j], 0), a.rows - 1);
-            bulk_g2s(hdst + (size_t)j * cb_max, hs + (size_t)row * rb + (size_t)d.dc * cb_max,
-                     (uint32_t)cb, &S.mbar[s]);
-          }
-        }
-        if (vid_bulk) bulk_g2s(&S.vid[s][0], vsrc, (uint32_t)(a.cap * 4), &S.mbar[s]);
-      } else {
-        S.desc[s] = d;
-        mbar_expect_tx(&S.mbar[s], 0u);  // end of work or invalid item: no data
-      }
-    };
-    int n_prod = 0;
-    while (n_prod < kInvSlots) produce(n_prod++ % kInvSlots);
-    __syncwarp();
-    int tile = 0;
-    for (int c = 0;; ++c) {
-      const int s = c % kInvSlots;
-      const InvChunk d = S.desc[s];
-      if (d.cluster == -1) break;
-      nbar_sync(kBarSlot0 + s, kInvBlock);
-      // lane: hidden row h = lane >> 2, tokens 4 * (lane & 3) .. + 3; their
-      // vocab ids are read before the slot is refilled
-      const int h = lane >> 2, t0 = 4 * (lane & 3);
-      int row_h = 0;  // d.rows[h], selected in registers
-#pragma unroll
-      for (int j = 0; j < kInvRows; ++j) row_h = j == h ? d.rows[j] : row_h;
-      uint32_t vids[4] = {0u, 0u, 0u, 0u};
-      if (d.last && d.cluster >= 0) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (t0 + u < a.cap)
-            vids[u] = (uint32_t)(d.vid_in_smem ? S.vid[s][t0 + u]
-                                               : __ldg(&a.vocab_map[d.cluster * a.cap + t0 + u]));
-      }
-      __syncwarp();
-      // refill the slot first (the reduction below reads only partials), and
-      // pull a later item's cluster into L2 so the refill after it hits L2
-      produce(n_prod++ % kInvSlots);
-      __syncwarp();
-      if (lane == 0 && item + kInvAhead < i1 && item + kInvAhead < pre_base + kInvPrefetch) {
-        const int ahead = S.pre[item + kInvAhead - pre_base].cluster;
-        if (ahead >= 0 && ahead < a.K && ((size_t)a.cap * rb) % 16 == 0)
-          bulk_prefetch_l2(wp + (size_t)ahead * a.cap * rb, (uint32_t)((size_t)a.cap * rb));
-      }
-      if (d.last) {
-        const int par = tile & 1;
-        unsigned long long best = 0ull;
-        if (h < d.n && d.cluster >= 0) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int tok = t0 + u;
-            const float4 *pp = reinterpret_cast<const float4 *>(&S.part[par][h][tok][0]);
-            const float4 x0 = pp[0], x1 = pp[1], x2 = pp[2], x3 = pp[3];
-            const float v = ((x0.x + x0.y) + (x0.z + x0.w)) + ((x1.x + x1.y) + (x1.z + x1.w)) +
-                            (((x2.x + x2.y) + (x2.z + x2.w)) + ((x3.x + x3.y) + (x3.z + x3.w)));
-            if (tok < a.cap) {
-              const uint32_t vid = vids[u];
-              float key = v;
-              if (a.do_sample)
-                key = v / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)row_h, vid);
-              const unsigned long long w = pack(key, vid);
-              best = w > best ? w : best;
-            }
-          }
-        }
-#pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) {
-          const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-          best = other > best ? other : best;
-        }
-        if ((lane & 3) == 0 && h < d.n && row_h >= 0 && row_h < a.rows)
-          atomicMax(&a.packed[row_h], best);
-        __syncwarp();
-        nbar_arrive(kBarPart0 + par, kInvBlock);
-        ++tile;
-      }
-    }
-  } else {
-    float acc[2][2][4];
-#pragma unroll
-    for (int cs = 0; cs < 2; ++cs)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) acc[cs][0][u] = acc[cs][1][u] = 0.f;
-    uint32_t phase = 0u;
-    int tile = 0;
-    for (int c = 0;; ++c) {
-      const int s = c % kInvSlots;
-      if (!mbar_wait(&S.mbar[s], (phase >> s) & 1u, a.copy_polls) && lane == 0)
-        atomicOr(&S.s_err, kErrCopyTimeout);
-      phase ^= 1u << s;
-      const InvChunk d = S.desc[s];
-      if (d.cluster == -1) break;
-      const int cb = d.cluster >= 0 ? min(cb_max, rb - d.dc * cb_max) : 0;  // invalid: no groups
-      const unsigned char *slot = ring + (size_t)s * kInvSlotBytes;
-      const unsigned char *hrows = slot + (size_t)kTileRows * pitch;
-      // column set cs: hidden row 4 * cs + (gq >> 1) of the item, parity odd
-      const int h0 = gq >> 1, h1 = 4 + (gq >> 1);
-      const bool v0 = h0 < d.n, v1 = h1 < d.n;
-      const int ng = cb / 64;
-      for (int grp = warp; grp < ng; grp += kFWarps) {
-        const int q = grp ^ odd;
-        const unsigned char *ra = slot + (size_t)gq * pitch + q * 64 + tq * 16;
-        const uint4 a0 = lds128(ra), b0 = lds128(ra + 8 * pitch);
-        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-        const uint4 x0 = v0 ? lds128(hrows + (size_t)h0 * cb_max + q * 64 + tq * 16) : z;
-        const uint4 x1 = v1 ? lds128(hrows + (size_t)h1 * cb_max + q * 64 + tq * 16) : z;
-        const uint32_t A0[4] = {a0.x, b0.x, a0.y, b0.y}, A1[4] = {a0.z, b0.z, a0.w, b0.w};
-        {
-          const uint32_t B0[2] = {x0.x, x0.y}, B1[2] = {x0.z, x0.w};
-          mma16816<HT>(acc[0][0], A0, B0);
-          mma16816<HT>(acc[0][1], A1, B1);
-        }
-        {
-          const uint32_t B0[2] = {x1.x, x1.y}, B1[2] = {x1.z, x1.w};
-          mma16816<HT>(acc[1][0], A0, B0);
-          mma16816<HT>(acc[1][1], A1, B1);
-        }
-      }
-      if (d.last) {
-        const int par = tile & 1;
-        if (tile >= 2) nbar_sync(kBarPart0 + par, kInvBlock);
-        // lane (g, t): token g (g + 8) against item row 4 * cs + t in c[odd] (c[2 + odd])
-#pragma unroll
-        for (int cs = 0; cs < 2; ++cs) {
-          const int h = 4 * cs + tq;
-          S.part[par][h][gq][warp] = acc[cs][0][odd] + acc[cs][1][odd];
-          S.part[par][h][gq + 8][warp] = acc[cs][0][2 + odd] + acc[cs][1][2 + odd];
-        }
-#pragma unroll
-        for (int cs = 0; cs < 2; ++cs)
-#pragma unroll
-          for (int u = 0; u < 4; ++u) acc[cs][0][u] = acc[cs][1][u] = 0.f;
-        ++tile;
-      }
-      nbar_arrive(kBarSlot0 + s, kInvBlock);
-    }
-    for (int t = max(tile - 2, 0); t < tile; ++t) nbar_sync(kBarPart0 + (t & 1), kInvBlock);
-  }
-  __syncthreads();
-  if (tid == 0 && S.s_err) atomicOr(a.err, S.s_err);
 }
 
 // ---------------------------------------------------------------------------

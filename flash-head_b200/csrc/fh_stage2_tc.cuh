@@ -1,0 +1,473 @@
+// Stage 2 of a batched decode step on the 5th-generation tensor cores,
+// cluster-major: every probed cluster's w_perm rows cross HBM once per step,
+// however many hidden rows probed it. The reference scores each (row, probe)
+// pair separately (src/flash_head/fused.py:119-164, grid (T, P)); the
+// packed (logit, vocab id) words and their max reduction follow it
+// (fused.py:148-163).
+//
+//   k_s2_fill      probe lists -> per cluster the hidden rows that probe it
+//                  (counts and row lists, by atomics).
+//   k_s2_tiles     probed clusters -> tiles of up to 8 clusters (128 w_perm
+//                  rows, the MMA's M); per tile the union of the clusters'
+//                  rows (the MMA's N, at most 256) and, per cluster, a bit mask
+//                  over the union positions of the rows that probed it.
+//   k_s2_tc        persistent, 10 warps:
+//     warp 0     lane 0 issues the TMA copies of each k-block (64 elements)
+//                of the tile's clusters (one 16-row box per cluster, 128-byte
+//                swizzle);
+//     warp 1     allocates 512 TMEM columns (two accumulators of 256), lane 0
+//                issues tcgen05.mma.kind::f16 (M = 128, N = the tile's padded
+//                union, K = 16) per k-block and commits stages and finished
+//                accumulators;
+//     warps 2-5  gather the union's hidden rows of each k-block with
+//                cp.async into the 128-byte-swizzled B operand, a few stages
+//                ahead, then make them visible to the tensor core (proxy
+//                fence) and arrive on the stage's barrier;
+//     warps 6-9  epilogue: thread = one w_perm row (TMEM lane); per union
+//                column whose row probed this thread's cluster, the logit (or
+//                the Gumbel key in sampling mode) packed with the vocab id,
+//                the max over the cluster's 16 rows by shuffles, and one
+//                atomicMax per (row, cluster) into packed[row]. Accumulators
+//                are double-buffered, so the epilogue of tile i overlaps the
+//                MMAs of tile i + 1.
+// The ring's depth follows the largest union of the step (read from the tile
+// builder's meta words), so typical steps keep many stages in flight. Every
+// wait is bounded; on a timeout the kernel records kErrCopyTimeout, drains its
+// own copies and MMAs (bounded) and frees TMEM before it returns.
+#pragma once
+
+#include "fh_s1_tc.cuh"
+
+namespace fh {
+
+constexpr int kS2Threads = 320;
+constexpr int kS2Loaders = 128;    // warps 2..5
+constexpr int kS2EpiThreads = 128; // warps 6..9
+constexpr int kS2Clusters = 8;     // clusters per tile (16 rows each: M = 128)
+constexpr int kS2MaxRows = 256;    // hidden rows per launch (union N <= 256)
+constexpr int kS2ATile = 128 * 128;  // bytes of the w_perm tile of one k-block
+constexpr int kS2MaxStages = 12;
+constexpr int kS2Lag = 3;          // k-blocks of hidden-row copies in flight per loader
+constexpr int kS2SmemMax = 227 * 1024;
+constexpr int kS2TileClusters = 1024;  // clusters per k_s2_tiles CTA
+
+struct S2Tile {
+  int n_cl;                        // clusters in the tile (1..8)
+  int n;                           // union rows
+  int cl[kS2Clusters];             // local cluster ids
+  uint32_t mask[kS2Clusters][8];   // bit u: union row u probed cluster j
+  unsigned char rows[kS2MaxRows];  // union rows (hidden row within the launch), ascending
+  int pad[22];
+};
+static_assert(sizeof(S2Tile) % 64 == 0, "tile descriptors are whole 64-byte lines");
+
+// meta words: [0] tiles, [1] largest union of any tile
+struct S2Meta {
+  int n_tiles;
+  int n_max;
+  int pad[62];
+};
+
+// ---------------------------------------------------------------------------
+// Index: per cluster the rows that probe it.
+// ---------------------------------------------------------------------------
+__global__ void k_s2_fill(const int32_t *probes, int rows, int p, int K, int base, int *cnt,
+                          unsigned char *list) {
+  const int n = rows * p;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int c = probes[i] - base;
+    if (c >= 0 && c < K) {
+      const int slot = atomicAdd(&cnt[c], 1);
+      if (slot < kS2MaxRows) list[(size_t)c * kS2MaxRows + slot] = (unsigned char)(i / p);
+    }
+  }
+}
+
+// One CTA of 256 threads per kS2TileClusters clusters: the CTA's probed
+// clusters (ascending id) are cut into tiles of kS2Clusters; each warp builds
+// whole tiles. Tile indices come from one atomic per CTA (order across CTAs is
+// irrelevant: the tiles partition the probed clusters and their results meet
+// in a max). meta must be zero on entry.
+__global__ void __launch_bounds__(256) k_s2_tiles(const int *cnt, const unsigned char *list, int K,
+                                                  S2Tile *tiles, S2Meta *meta) {
+  __shared__ int ids[kS2TileClusters];
+  __shared__ int scan_scratch[33];
+  __shared__ int s_base;
+  __shared__ uint32_t w_union[8][8];
+  __shared__ uint32_t w_rowmask[8][kS2Clusters][8];
+  __shared__ uint32_t w_posmask[8][kS2Clusters][8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c0 = blockIdx.x * kS2TileClusters;
+  // 4 consecutive clusters per thread
+  int f[4], nf = 0;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = c0 + 4 * tid + u;
+    f[u] = c < K && __ldcg(&cnt[c]) > 0;
+    nf += f[u];
+  }
+  int total;
+  int pos = block_exclusive_scan(nf, scan_scratch, &total);
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    if (f[u]) ids[pos++] = c0 + 4 * tid + u;
+  const int n_tiles = (total + kS2Clusters - 1) / kS2Clusters;
+  if (tid == 0) s_base = n_tiles ? atomicAdd(&meta->n_tiles, n_tiles) : 0;
+  __syncthreads();
+  const int base = s_base;
+  uint32_t *un = w_union[warp];
+  uint32_t(*rm)[8] = w_rowmask[warp];
+  uint32_t(*pm)[8] = w_posmask[warp];
+  for (int t = warp; t < n_tiles; t += 8) {
+    const int j0 = t * kS2Clusters, ncl = min(kS2Clusters, total - j0);
+    for (int i = lane; i < 8 + 2 * kS2Clusters * 8; i += 32) {
+      if (i < 8) un[i] = 0u;
+      else if (i < 8 + kS2Clusters * 8) (&rm[0][0])[i - 8] = 0u;
+      else (&pm[0][0])[i - 8 - kS2Clusters * 8] = 0u;
+    }
+    __syncwarp();
+    // rows of every cluster into the union and per-cluster row bitmaps
+    for (int j = 0; j < ncl; ++j) {
+      const int c = ids[j0 + j];
+      const int n = min(__ldcg(&cnt[c]), kS2MaxRows);
+      for (int s = lane; s < n; s += 32) {
+        const int r = list[(size_t)c * kS2MaxRows + s];
+        atomicOr(&un[r >> 5], 1u << (r & 31));
+        atomicOr(&rm[j][r >> 5], 1u << (r & 31));
+      }
+    }
+    __syncwarp();
+    // union positions: prefix popcounts of the union words
+    uint32_t word = lane < 8 ? un[lane] : 0u;
+    int pc = __popc(word), incl = pc;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const int x = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += x;
+    }
+    const int before = incl - pc;  // union rows in words below this lane's word
+    const int N = __shfl_sync(0xFFFFFFFFu, incl, 7);
+    S2Tile &T = tiles[base + t];
+    if (lane < 8) {
+      // rows of this word, ascending, at their union positions
+      int q = before;
+      for (uint32_t m = word; m; m &= m - 1u) T.rows[q++] = (unsigned char)(lane * 32 + __ffs(m) - 1);
+      // per cluster: each row of this word that probed cluster j sets its position bit
+      for (int j = 0; j < ncl; ++j) {
+        int q2 = before;
+        for (uint32_t m = word; m; m &= m - 1u, ++q2) {
+          const int b = __ffs(m) - 1;
+          if (rm[j][lane] & (1u << b)) atomicOr(&pm[j][q2 >> 5], 1u << (q2 & 31));
+        }
+      }
+    }
+    __syncwarp();
+    for (int i = lane; i < kS2Clusters * 8; i += 32) {
+      const int j = i >> 3;
+      T.mask[j][i & 7] = j < ncl ? pm[j][i & 7] : 0u;
+    }
+    if (lane < kS2Clusters) T.cl[lane] = lane < ncl ? ids[j0 + lane] : -1;
+    if (lane == 0) {
+      T.n_cl = ncl;
+      T.n = N;
+      atomicMax(&meta->n_max, N);
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The tensor-core stage 2.
+// ---------------------------------------------------------------------------
+struct S2TcArgs {
+  const void *hidden;      // [rows, D] (this launch's rows)
+  int rows;
+  int D;
+  int nk;                  // D / 64
+  int cap;                 // w_perm rows per cluster (<= 16)
+  uint32_t idesc0;         // kind::f16 descriptor without N
+  const int32_t *vocab_map;
+  const S2Tile *tiles;
+  const S2Meta *meta;
+  int do_sample;
+  float temperature;
+  RngKey rng;
+  int row_base;            // global row of hidden row 0 (noise stream)
+  unsigned long long *packed;  // [rows] (this launch's rows)
+  uint32_t *err;
+  uint32_t polls;
+};
+
+struct S2TcCtrl {
+  uint64_t full_a[kS2MaxStages];
+  uint64_t full_b[kS2MaxStages];
+  uint64_t empty[kS2MaxStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t s_err;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool SAMPLE>
+__global__ void __launch_bounds__(kS2Threads, 1)
+    k_s2_tc(const __grid_constant__ CUtensorMap tm_w, S2TcArgs a) {
+  extern __shared__ __align__(1024) unsigned char dsm[];
+  const uint32_t raw = smem_u32(dsm);
+  unsigned char *ring = dsm + (((raw + 1023u) & ~1023u) - raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  grid_dep_wait();  // the tile list comes from the kernel before this one
+  const int n_tiles = __ldcg(&a.meta->n_tiles);
+  const int n_max = max(16, (__ldcg(&a.meta->n_max) + 15) & ~15);
+  const size_t sb = (size_t)kS2ATile + (size_t)n_max * 128;  // multiple of 2048
+  const int stages = (int)min((size_t)kS2MaxStages,
+                              ((size_t)kS2SmemMax - 1024 - sizeof(S2TcCtrl)) / sb);
+  S2TcCtrl &S = *reinterpret_cast<S2TcCtrl *>(ring + (size_t)stages * sb);
+  const int G = gridDim.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&S.full_a[s], 1);
+      mbar_init(&S.full_b[s], kS2Loaders);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&S.acc_full[j], 1);
+      mbar_init(&S.acc_empty[j], kS2EpiThreads);
+    }
+    mbar_init(&S.drain, 1);
+    S.s_err = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&S.tmem_base)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------ w_perm tiles (TMA)
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0u;
+      int issued[kS2MaxStages];
+      for (int j = 0; j < kS2MaxStages; ++j) issued[j] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += G) {
+        const S2Tile &T = a.tiles[t];
+        const int ncl = min(max(__ldcg(&T.n_cl), 0), kS2Clusters);
+        int cl[kS2Clusters];
+#pragma unroll
+        for (int j = 0; j < kS2Clusters; ++j) cl[j] = __ldcg(&T.cl[j]);
+        for (int kb = 0; kb < a.nk; ++kb) {
+          if (!mbar_wait(&S.empty[s], ph ^ 1u, a.polls)) {
+            atomicOr(&S.s_err, kErrCopyTimeout);
+            ok = false;
+            break;
+          }
+          unsigned char *st = ring + (size_t)s * sb;
+          mbar_expect_tx(&S.full_a[s], (uint32_t)(ncl * 16 * 128));
+#pragma unroll
+          for (int j = 0; j < kS2Clusters; ++j)
+            if (j < ncl)
+              tma_load_2d(st + j * 16 * 128, &tm_w, kb * 64, cl[j] * a.cap, &S.full_a[s]);
+          issued[s] = (int)ph;
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      for (int j = 0; j < stages; ++j)
+        if (issued[j] >= 0 && !mbar_wait(&S.full_a[j], (uint32_t)issued[j], a.polls))
+          atomicOr(&S.s_err, kErrCopyTimeout);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issue
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0u;
+      bool ok = true;
+      int i = 0;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += G, ++i) {
+        const int buf = i & 1, use = i >> 1;
+        const int n_pad = max(16, (min(__ldcg(&a.tiles[t].n), kS2MaxRows) + 15) & ~15);
+        const uint32_t idesc = a.idesc0 | ((uint32_t)(n_pad >> 3) << 17);
+        if (use > 0) {
+          if (!mbar_wait(&S.acc_empty[buf], (uint32_t)((use - 1) & 1), a.polls)) {
+            atomicOr(&S.s_err, kErrCopyTimeout);
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t acc = tmem + (uint32_t)(buf * 256);
+        for (int kb = 0; kb < a.nk; ++kb) {
+          if (!mbar_wait(&S.full_a[s], ph, a.polls) || !mbar_wait(&S.full_b[s], ph, a.polls)) {
+            atomicOr(&S.s_err, kErrCopyTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(ring + (size_t)s * sb);
+          const uint64_t ad = umma_desc_k(st);
+          const uint64_t bd = umma_desc_k(st + (uint32_t)kS2ATile);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc_mma_f16(acc, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          tc_commit(&S.empty[s]);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) tc_commit(&S.acc_full[buf]);
+      }
+      tc_commit(&S.drain);
+      if (!mbar_wait(&S.drain, 0u, a.polls)) atomicOr(&S.s_err, kErrCopyTimeout);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------ hidden rows (cp.async)
+    // k-block g of this CTA's sequence uses stage g % stages; its copies are
+    // committed as one group and announced kS2Lag groups later.
+    const int lt = tid - 64;
+    const char *hs = reinterpret_cast<const char *>(a.hidden);
+    const size_t rb = (size_t)a.D * 2;
+    int s = 0, g = 0;
+    uint32_t ph = 0u;
+    bool ok = true;
+    for (int t = blockIdx.x; t < n_tiles && ok; t += G) {
+      const S2Tile &T = a.tiles[t];
+      const int n = min(max(__ldcg(&T.n), 0), kS2MaxRows);
+      const int n_pad = max(16, (n + 15) & ~15);
+      const int per = n_pad / 16;  // 16-byte chunks per thread and k-block (<= 16)
+      // chunk i of this thread: union row u = (lt + 128 i) / 8, 16-byte chunk c
+      const int c = lt & 7;
+      const char *src[16];
+      uint32_t dst_off[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int u = (lt + kS2Loaders * i) >> 3;
+        const int row = u < n ? min((int)__ldcg(&T.rows[u]), a.rows - 1) : 0;
+        src[i] = hs + (size_t)row * rb + c * 16;
+        dst_off[i] = (uint32_t)(u * 128 + ((c ^ (u & 7)) << 4)) | (u < n ? 0u : 0x80000000u);
+      }
+      for (int kb = 0; kb < a.nk; ++kb, ++g) {
+        if (!mbar_wait(&S.empty[s], ph ^ 1u, a.polls)) {
+          atomicOr(&S.s_err, kErrCopyTimeout);
+          ok = false;
+          break;
+        }
+        const uint32_t bst = smem_u32(ring + (size_t)s * sb + kS2ATile);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < per)
+            cp_async16(bst + (dst_off[i] & 0x7FFFFFFFu), src[i] + (size_t)kb * 128,
+                       (dst_off[i] >> 31) ? 0u : 16u);
+        cp_async_commit();
+        if (g >= kS2Lag) {
+          cp_async_wait<kS2Lag>();
+          fence_proxy_async_smem();
+          mbar_arrive_cta(&S.full_b[(g - kS2Lag) % stages]);
+        }
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    for (int g2 = max(0, g - kS2Lag); g2 < g; ++g2) mbar_arrive_cta(&S.full_b[g2 % stages]);
+  } else {
+    // ------------------------------------------------ epilogue
+    const int q = warp & 3;       // TMEM lane quadrant
+    const int m = 32 * q + lane;  // w_perm row of the tile
+    const int j = m >> 4, tok = m & 15;
+    bool ok = true;
+    int i = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += G, ++i) {
+      const int buf = i & 1, use = i >> 1;
+      const S2Tile &T = a.tiles[t];
+      const int ncl = min(max(__ldcg(&T.n_cl), 0), kS2Clusters);
+      const int n = min(max(__ldcg(&T.n), 0), kS2MaxRows);
+      const int cj = j < ncl ? __ldcg(&T.cl[j]) : -1;
+      const bool valid = cj >= 0 && tok < a.cap;
+      const uint32_t vid = valid ? (uint32_t)__ldg(&a.vocab_map[cj * a.cap + tok]) : 0u;
+      if (ok && !mbar_wait(&S.acc_full[buf], (uint32_t)(use & 1), a.polls)) {
+        atomicOr(&S.s_err, kErrCopyTimeout);
+        ok = false;
+      }
+      __syncwarp();
+      if (ok) {
+        tc_fence_after();
+        const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * 256);
+        for (int w = 0; w * 32 < n; ++w) {
+          // this lane's cluster mask word, and the warp's (both clusters)
+          const uint32_t mine = j < ncl ? __ldcg(&T.mask[j][w]) : 0u;
+          const uint32_t both = mine | __shfl_xor_sync(0xFFFFFFFFu, mine, 16);
+          if (both == 0u) continue;  // warp-uniform
+          uint32_t v[2][16];
+          tc_ld16(base + (uint32_t)(32 * w), v[0]);
+          tc_ld16(base + (uint32_t)(32 * w + 16), v[1]);
+          tc_wait_ld();
+#pragma unroll
+          for (int b = 0; b < 32; ++b) {
+            if (!((both >> b) & 1u)) continue;  // warp-uniform
+            const bool take = valid && ((mine >> b) & 1u);
+            const int row = take ? (int)T.rows[32 * w + b] : 0;
+            unsigned long long key = 0ull;
+            if (take) {
+              float x = sanitize(__uint_as_float(v[b >> 4][b & 15]));
+              if (SAMPLE)
+                x = x / a.temperature +
+                    gumbel(a.rng, kStageTokens, (uint32_t)(a.row_base + row), vid);
+              key = pack(x, vid);
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+              const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, key, o);
+              key = other > key ? other : key;
+            }
+            if ((lane & 15) == 0 && key && ((mine >> b) & 1u)) {
+              const int r2 = T.rows[32 * w + b];
+              atomicMax(&a.packed[r2], key);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cta(&S.acc_empty[buf]);
+    }
+  }
+  grid_dep_launch();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)
+                 : "memory");
+  }
+  if (tid == 0 && S.s_err) atomicOr(a.err, S.s_err);
+}
+
+}  // namespace fh

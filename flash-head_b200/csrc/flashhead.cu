@@ -22,7 +22,7 @@
 
 #include "../../include/flashhead.h"
 #include "fh_batched.cuh"
-#include "fh_s1_tc.cuh"
+#include "fh_stage2_tc.cuh"
 #include "fh_spec.cuh"
 
 namespace {
@@ -194,6 +194,8 @@ struct fh_head {
   mutable int tm_w_tile = 0;  // its box height, 0: not encoded yet
   mutable CUtensorMap tm_c[2];  // stage-1 matrices (cluster_w, centroid_w) for k_s1_tc
   mutable bool tm_c_ok[2] = {false, false};
+  mutable CUtensorMap tm_s2;  // w_perm in 16-row boxes for k_s2_tc
+  mutable bool tm_s2_ok = false;
 };
 
 // ---------------------------------------------------------------------------
@@ -227,9 +229,13 @@ struct Workspace {
   unsigned *counter;            // [1]
   unsigned char *epoch_bufs;    // one-kernel histograms
   void *h16;                    // [rows, D] f16 copy of bf16 hidden rows (fp8 stage 1)
-  // batched steps (rows >= kBatchMinRows) only, else null
-  int *inv_cnt, *inv_off, *inv_item_off, *inv_cursor, *inv_meta, *inv_list;
-  fh::InvItem *inv_items;
+  // batched steps (rows >= kBatchMinRows) only, else null: the cluster-major
+  // stage 2's index of one chunk of up to kS2MaxRows rows
+  int *s2_cnt;                  // [K] rows per cluster, followed by the meta words
+  fh::S2Meta *s2_meta;
+  unsigned char *s2_list;       // [K][kS2MaxRows] rows of every cluster
+  fh::S2Tile *s2_tiles;         // tile descriptors
+  size_t s2_zero_bytes;         // bytes of s2_cnt + s2_meta (zeroed per chunk)
   size_t bytes;                 // bytes needed for `rows`
 };
 
@@ -257,11 +263,12 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
                          : 0;
   const bool batched = rows >= fh::kBatchMinRows;
   const size_t kint = round_up((size_t)d.n_clusters * sizeof(int), 256);
-  const size_t n_pairs = (size_t)rows * d.n_probes;
-  const size_t max_items = n_pairs / fh::kInvRows + (size_t)d.n_clusters + 1;
-  const size_t inv = batched ? 4 * kint + 256 + round_up(n_pairs * sizeof(int), 256) +
-                                   round_up(max_items * sizeof(fh::InvItem), 256)
-                             : 0;
+  const size_t max_tiles = (size_t)(d.n_clusters + fh::kS2Clusters - 1) / fh::kS2Clusters +
+                           (size_t)(d.n_clusters + fh::kS2TileClusters - 1) / fh::kS2TileClusters +
+                           1;
+  const size_t s2_list = round_up((size_t)d.n_clusters * fh::kS2MaxRows, 256);
+  const size_t s2_tiles = round_up(max_tiles * sizeof(fh::S2Tile), 256);
+  const size_t inv = batched ? kint + sizeof(fh::S2Meta) + s2_list + s2_tiles : 0;
   w.bytes = state + probes + scores + h16 + inv + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
   w.epoch_bufs = reinterpret_cast<unsigned char *>(p + 256);
@@ -273,19 +280,19 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   w.probes = reinterpret_cast<int32_t *>(p + probes_off);
   w.scores = reinterpret_cast<float *>(p + scores_off);
   w.h16 = h16 ? p + h16_off : nullptr;
-  w.inv_cnt = w.inv_off = w.inv_item_off = w.inv_cursor = w.inv_meta = w.inv_list = nullptr;
-  w.inv_items = nullptr;
+  w.s2_cnt = nullptr;
+  w.s2_meta = nullptr;
+  w.s2_list = nullptr;
+  w.s2_tiles = nullptr;
+  w.s2_zero_bytes = kint + sizeof(fh::S2Meta);
   if (batched) {
     size_t q = h16_off >= inv ? h16_off - inv : 0;
-    w.inv_items = reinterpret_cast<fh::InvItem *>(p + q);
-    q += round_up(max_items * sizeof(fh::InvItem), 256);
-    w.inv_list = reinterpret_cast<int *>(p + q);
-    q += round_up(n_pairs * sizeof(int), 256);
-    w.inv_cnt = reinterpret_cast<int *>(p + q);
-    w.inv_off = reinterpret_cast<int *>(p + q + kint);
-    w.inv_item_off = reinterpret_cast<int *>(p + q + 2 * kint);
-    w.inv_cursor = reinterpret_cast<int *>(p + q + 3 * kint);
-    w.inv_meta = reinterpret_cast<int *>(p + q + 4 * kint);
+    w.s2_tiles = reinterpret_cast<fh::S2Tile *>(p + q);
+    q += s2_tiles;
+    w.s2_list = reinterpret_cast<unsigned char *>(p + q);
+    q += s2_list;
+    w.s2_cnt = reinterpret_cast<int *>(p + q);
+    w.s2_meta = reinterpret_cast<fh::S2Meta *>(p + q + kint);
   }
   return w;
 }
@@ -550,46 +557,10 @@ cudaError_t prepare_select_hist() {
   return cudaSuccess;
 }
 
-cudaError_t prepare_inv_build() {
-  static bool done[128];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_attr_mutex);
-  if (!done[dev]) {
-    e = cudaFuncSetAttribute(fh::k_inv_build, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(fh::kSelMaxItems * sizeof(int)));
-    if (e != cudaSuccess) return e;
-    done[dev] = true;
-  }
-  return cudaSuccess;
-}
-
 int grid_for(long long n, int block) {
   long long g = (n + block - 1) / block;
   const int cap = 4 * (sm_count() > 0 ? sm_count() : 148);
   return (int)(g < 1 ? 1 : g > cap ? cap : g);
-}
-
-template <typename HT>
-cudaError_t launch_stage2_inv(const fh::InvArgs &a, int grid, cudaStream_t s) {
-  static bool attr_done[128];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (!attr_done[dev]) {
-      e = cudaFuncSetAttribute(fh::k_stage2_inv<HT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fh::kInvSmemBytes);
-      if (e != cudaSuccess) return e;
-      attr_done[dev] = true;
-    }
-  }
-  return launch(fh::k_stage2_inv<HT>, dim3(grid), dim3(fh::kInvBlock), fh::kInvSmemBytes, s, false,
-                a);
 }
 
 // cuTensorMapEncodeTiled from the driver, resolved once through the runtime
@@ -762,10 +733,30 @@ int run_s1_tc(const fh_head *h, const void *hidden, int rows, bool sample, float
   return FH_OK;
 }
 
+cudaError_t prepare_s2_tc() {
+  static bool done[128];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (!done[dev]) {
+    e = cudaFuncSetAttribute(fh::k_s2_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fh::kS2SmemMax);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fh::k_s2_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fh::kS2SmemMax);
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
+
 // Stage 2 of a batched step for given probe lists (cluster ids from
-// probe_base): the inverted index (clusters -> the rows that probe them, in
-// items of up to kInvRows rows), the inverted stage 2 over it, the special
-// tokens, and the publish of ids (out_ids) or of signed packed words
+// probe_base), per chunk of up to kS2MaxRows rows: the index (the rows of
+// every probed cluster), the tiles of 8 probed clusters with the union of
+// their rows, and the cluster-major tensor-core stage 2 (k_s2_tc); then the
+// special tokens and the publish of ids (out_ids) or of signed packed words
 // (out_signed, tensor-parallel shards). packed[] must be zero on entry and is
 // zero again on return.
 int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
@@ -774,46 +765,58 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
   const fh_head_desc &d = h->d;
   const fh::RngKey rng = rng_key(seed, offset);
   const int K = d.n_clusters, p = d.n_probes;
-  FH_CHECK_LAUNCH(cudaMemsetAsync(w.inv_cnt, 0, (size_t)K * sizeof(int), s), "index reset");
-  const long long pairs = (long long)rows * p;
-  FH_CHECK_LAUNCH(launch(fh::k_inv_count, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
-                         probes, rows, p, K, probe_base, w.inv_cnt),
-                  "index count launch");
-  FH_CHECK_LAUNCH(prepare_inv_build(), "index build attribute");
-  FH_CHECK_LAUNCH(launch(fh::k_inv_build, dim3(1), dim3(1024), (size_t)K * sizeof(int), s, false,
-                         (const int *)w.inv_cnt,
-                         K, w.inv_off, w.inv_item_off, w.inv_cursor, w.inv_meta),
-                  "index build launch");
-  FH_CHECK_LAUNCH(launch(fh::k_inv_scatter, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
-                         probes, rows, p, K, probe_base, (const int *)w.inv_off, w.inv_cursor,
-                         w.inv_list),
-                  "index scatter launch");
-  FH_CHECK_LAUNCH(launch(fh::k_inv_items, dim3(grid_for(K, 256)), dim3(256), 0, s, false,
-                         (const int *)w.inv_cnt, (const int *)w.inv_off,
-                         (const int *)w.inv_item_off, (const int *)w.inv_list, K, w.inv_items),
-                  "index items launch");
-  fh::InvArgs ia;
-  memset(&ia, 0, sizeof(ia));
-  ia.hidden = hidden;
-  ia.rows = rows;
-  ia.D = d.hidden;
-  ia.w_perm = d.w_perm;
-  ia.vocab_map = d.vocab_map;
-  ia.K = K;
-  ia.cap = d.cluster_size;
-  ia.items = w.inv_items;
-  ia.meta = w.inv_meta;
-  ia.do_sample = sample ? 1 : 0;
-  ia.temperature = temperature;
-  ia.rng = rng;
-  ia.packed = w.packed;
-  ia.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
-  ia.copy_polls = 1u << 22;
-  const int grid = sm_count();
-  if (d.weight_dtype == FH_BF16)
-    FH_CHECK_LAUNCH(launch_stage2_inv<__nv_bfloat16>(ia, grid, s), "inverted stage-2 launch");
-  else
-    FH_CHECK_LAUNCH(launch_stage2_inv<__half>(ia, grid, s), "inverted stage-2 launch");
+  if (!w.s2_cnt) return fail(FH_ERR_WORKSPACE, "workspace laid out without the stage-2 index");
+  const long long V = (long long)K * d.cluster_size;
+  CUtensorMap tm_w;
+  {
+    std::lock_guard<std::mutex> lock(h->plan_mutex);
+    if (!h->tm_s2_ok) {
+      if (!encode_rows_map(&h->tm_s2, d.w_perm, d.weight_dtype, d.hidden, V, 16))
+        return fail(FH_ERR_UNSUPPORTED, "w_perm tensor map");
+      h->tm_s2_ok = true;
+    }
+    tm_w = h->tm_s2;
+  }
+  FH_CHECK_LAUNCH(prepare_s2_tc(), "stage-2 kernel attribute");
+  const int tile_ctas = (K + fh::kS2TileClusters - 1) / fh::kS2TileClusters;
+  for (int r0 = 0; r0 < rows; r0 += fh::kS2MaxRows) {
+    const int n = std::min(fh::kS2MaxRows, rows - r0);
+    FH_CHECK_LAUNCH(cudaMemsetAsync(w.s2_cnt, 0, w.s2_zero_bytes, s), "index reset");
+    const long long pairs = (long long)n * p;
+    FH_CHECK_LAUNCH(launch(fh::k_s2_fill, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
+                           probes + (size_t)r0 * p, n, p, K, probe_base, w.s2_cnt, w.s2_list),
+                    "index fill launch");
+    FH_CHECK_LAUNCH(launch(fh::k_s2_tiles, dim3(tile_ctas), dim3(256), 0, s, false,
+                           (const int *)w.s2_cnt, (const unsigned char *)w.s2_list, K, w.s2_tiles,
+                           w.s2_meta),
+                    "tile build launch");
+    fh::S2TcArgs a;
+    memset(&a, 0, sizeof(a));
+    a.hidden = reinterpret_cast<const char *>(hidden) + (size_t)r0 * d.hidden * 2;
+    a.rows = n;
+    a.D = d.hidden;
+    a.nk = d.hidden / 64;
+    a.cap = d.cluster_size;
+    a.idesc0 = fh::s1tc_idesc(d.weight_dtype == FH_BF16, 0) & ~(0x3Fu << 17);
+    a.vocab_map = d.vocab_map;
+    a.tiles = w.s2_tiles;
+    a.meta = w.s2_meta;
+    a.do_sample = sample ? 1 : 0;
+    a.temperature = temperature;
+    a.rng = rng;
+    a.row_base = r0;
+    a.packed = w.packed + r0;
+    a.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
+    a.polls = 1u << 22;
+    if (sample)
+      FH_CHECK_LAUNCH(launch(fh::k_s2_tc<true>, dim3(sm_count()), dim3(fh::kS2Threads),
+                             (size_t)fh::kS2SmemMax, s, true, tm_w, a),
+                      "stage-2 tensor-core launch");
+    else
+      FH_CHECK_LAUNCH(launch(fh::k_s2_tc<false>, dim3(sm_count()), dim3(fh::kS2Threads),
+                             (size_t)fh::kS2SmemMax, s, true, tm_w, a),
+                      "stage-2 tensor-core launch");
+  }
   if (d.n_special > 0) {
     const long long warps = (long long)rows * d.n_special;
     const int n_slots = K * d.cluster_size;
@@ -1048,9 +1051,10 @@ FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample) {
   const int s1 = (cdt == FH_FP8_E4M3 && d.weight_dtype == FH_BF16 ? 1 : 0) +
                  (rows + fh::kS1MaxN - 1) / fh::kS1MaxN + 1;
   if (batched_ok(head, rows, sample)) {
-    // stage 1, index reset (memset), count, build, scatter, items, stage 2,
+    // stage 1; per 256 rows: index reset (memset), index fill, tiles, stage 2;
     // [specials], finalize
-    return s1 + 7 + (d.n_special > 0 ? 1 : 0);
+    const int chunks = (rows + fh::kS2MaxRows - 1) / fh::kS2MaxRows;
+    return s1 + 4 * chunks + (d.n_special > 0 ? 1 : 0) + 1;
   }
   if (fused_ok(d, rows, sample, sm_count())) return 1;
   // stage 1 + stage 2; or scores, select, stage 2
@@ -1392,8 +1396,11 @@ extern "C" FH_API int fh_get_next_token_noalloc(const fh_head *head, const void 
   w.split_stride = (size_t)rows * w.score_stride;
   w.epoch_bufs = nullptr;
   w.h16 = nullptr;
-  w.inv_cnt = w.inv_off = w.inv_item_off = w.inv_cursor = w.inv_meta = w.inv_list = nullptr;
-  w.inv_items = nullptr;
+  w.s2_cnt = nullptr;
+  w.s2_meta = nullptr;
+  w.s2_list = nullptr;
+  w.s2_tiles = nullptr;
+  w.s2_zero_bytes = 0;
   w.bytes = kNoAllocBytes;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // k_scores zeroes the accumulator and the counter before stage 2 uses them.

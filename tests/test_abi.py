@@ -128,9 +128,10 @@ def test_valid_descriptor_and_workspace_size(lib):
                     + rnd(splits * rows * 8064 * 4) + 256)
             if rows >= 5:
                 want += rnd(rows * 2048 * 2)
-            if rows >= 16:  # batched steps: inverted index and item list
-                K, pairs = 8016, rows * 256
-                want += 4 * rnd(K * 4) + 256 + rnd(pairs * 4) + rnd((pairs // 8 + K + 1) * 64)
+            if rows >= 16:  # batched steps: stage-2 index (counts + meta, row lists, tiles)
+                K = 8016
+                tiles = -(-K // 8) + -(-K // 1024) + 1
+                want += rnd(K * 4) + 256 + rnd(K * 256) + rnd(tiles * 640)
             assert lib.fh_workspace_bytes(h, rows) == want
         assert lib.fh_workspace_bytes(None, 1) == 0
     finally:

@@ -96,6 +96,7 @@ def test_config_b_256_rows_vs_reference(config_b, stage1):
         assert mean_rec >= 0.95 and min_rec >= 0.90
     # the batched call (256 rows) against the kernels' own oracle
     check_greedy_rows(fh, H, toks, probes)
+    assert fh.native().workspace_error() == 0  # no bounded wait ran out
 
 
 @pytest.mark.parametrize("stage1", ["model", "fp8"])
