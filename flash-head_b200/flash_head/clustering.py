@@ -223,8 +223,8 @@ def build_clustering_cache(model: str, cache_dir: str, cap: int = 16, iters: int
     """Cluster the LM head of checkpoint `model` (a local directory or a hub
     id) and write the cache into `cache_dir`; returns the file path. The
     model's config.json names the directory in ``flash_head_cache_dir``."""
-    from .loading import _load_lm_head_weight
-    w, _ = _load_lm_head_weight(model)
+    from .assets import ModelFiles, lm_head_weight
+    w, _ = lm_head_weight(ModelFiles(model))
     if w.shape[0] < w.shape[1]:
         w = w.t()
     assign, cent = balanced_clusters(w, cap=cap, iters=iters, seed=seed, device=device)

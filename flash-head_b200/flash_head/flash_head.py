@@ -52,41 +52,15 @@ def _get_device():
     return "cpu"
 
 
-def _resolve_asset(model_or_dir: str, relative_path: str) -> str:
-    """Resolve a model asset to a local path, preferring the HF cache
-    (flash_head.py:29-38)."""
-    if os.path.isdir(model_or_dir):
-        p = os.path.join(model_or_dir, relative_path)
-        if not os.path.exists(p):
-            raise FileNotFoundError(f"Missing local asset: {p}")
-        return p
-    from huggingface_hub import hf_hub_download, try_to_load_from_cache
-    cached = try_to_load_from_cache(model_or_dir, relative_path)
-    if isinstance(cached, str):
-        return cached
-    return hf_hub_download(repo_id=model_or_dir, filename=relative_path)
-
-
 def _get_centroids(lm_head: nn.Linear, model_or_dir: str, cache_dir: str):
-    """Read ``<cache_dir>/clustering_cache.safetensors`` (keys ``centroids``,
-    ``cluster_assignments``) as the reference does (flash_head.py:41-78)."""
-    from safetensors.torch import load_file
+    """(centroids [D, K], cluster_assignments [V]) from the model's
+    clustering cache (the reference's reader, flash_head.py:41-78), on the
+    head's device, centroids in its dtype."""
+    from .assets import ModelFiles, clustering
 
-    original_shape = lm_head.weight.shape
-    cache_file = _resolve_asset(model_or_dir, os.path.join(cache_dir, "clustering_cache.safetensors"))
-    try:
-        tensors = load_file(cache_file)
-        if "centroids" not in tensors or "cluster_assignments" not in tensors:
-            raise KeyError(f"Cache missing required tensors. Found keys: {list(tensors.keys())}")
-        centroids = tensors["centroids"]
-        assign = tensors["cluster_assignments"]
-        if assign.ndim != 1 or assign.shape[0] != original_shape[0]:
-            raise ValueError(f"cluster_assignments shape {tuple(assign.shape)}; "
-                             f"expected ({original_shape[0]},)")
-        device, dtype = lm_head.weight.device, lm_head.weight.dtype
-        return centroids.to(device=device, dtype=dtype), assign.to(device=device)
-    except Exception as e:
-        raise ValueError(f"Error loading cache: {e}") from e
+    centroids, assign = clustering(ModelFiles(model_or_dir), cache_dir, lm_head.weight.shape[0])
+    w = lm_head.weight
+    return centroids.to(device=w.device, dtype=w.dtype), assign.to(device=w.device)
 
 
 def vocab_maps_from_assignments(assign: torch.Tensor, n_clusters: int) -> torch.Tensor:

@@ -8,6 +8,7 @@ patched ``forward`` also leaves such ids untouched by the logit soft-cap and
 scale that vLLM applies to real logits.
 """
 
+import contextlib
 import logging
 import os
 
@@ -37,11 +38,27 @@ def _get_flash_head():
 # hidden states of the last step that returned FlashHead ids; the sampler
 # hook reads them when the step's requests ask for logprobs
 _last_hidden = None
+# > 0 while vLLM must see real logits (its sampler warm-up)
+_full_logits_depth = 0
+
+
+@contextlib.contextmanager
+def full_logits():
+    """Within the block, _get_logits returns vLLM's logits for every step."""
+    global _full_logits_depth
+    _full_logits_depth += 1
+    try:
+        yield
+    finally:
+        _full_logits_depth -= 1
 
 
 def flash_head_token_ids(hidden_states: torch.Tensor):
     """Token ids [n, 1] int32 for a decode step, or None if FlashHead does not apply."""
     global _last_hidden
+    if _full_logits_depth > 0:
+        _last_hidden = None
+        return None
     fh = _get_flash_head()
     n = hidden_states.shape[0]
     if fh is None or not (1 <= n <= max_decode_rows()):

@@ -36,7 +36,7 @@ def test_metadata_and_weight_loading(small_assets):
     meta = loading.load_flash_head_from_checkpoint(d)
     assert meta["cache_dir"] == os.path.join(d, "flash_head_assets")
     assert meta["special_token_ids"] == [0, 7, 2047] and meta["n_probes"] == 8
-    w, key = loading._load_lm_head_weight(d)
+    w, key = loading.lm_head_weight(loading.ModelFiles(d))
     assert key == "lm_head.weight" and torch.equal(w, head.weight)
     assert loading.load_flash_head_from_checkpoint(os.path.join(d, "missing")) is None
 
@@ -44,18 +44,21 @@ def test_metadata_and_weight_loading(small_assets):
 def test_sharded_index_and_tied_embedding(tmp_path):
     from safetensors.torch import save_file
 
-    from flash_head import loading
+    from flash_head import assets
     w = torch.randn(32, 8)
     save_file({"model.embed_tokens.weight": w}, str(tmp_path / "shard-1.safetensors"))
     (tmp_path / "model.safetensors.index.json").write_text(json.dumps(
         {"weight_map": {"model.embed_tokens.weight": "shard-1.safetensors",
                         "model.layers.0.w": "shard-2.safetensors"}}))
-    got, key = loading._load_lm_head_weight(str(tmp_path))
+    got, key = assets.lm_head_weight(assets.ModelFiles(str(tmp_path)))
     assert key == "model.embed_tokens.weight" and torch.equal(got, w)
-    assert loading._find_weight_key_in_index({"weight_map": {"x.lm_head.weight": "a"}}) == \
-        "x.lm_head.weight"
-    with pytest.raises(FileNotFoundError):
-        loading._load_lm_head_weight(str(tmp_path / "nothing"))
+    # an index may name the head under any prefix; a single file only by LM_HEAD_KEYS
+    assert assets.pick_lm_head_key(["x.lm_head.weight"], by_suffix=True) == "x.lm_head.weight"
+    assert assets.pick_lm_head_key(["x.lm_head.weight"], by_suffix=False) is None
+    assert assets.pick_lm_head_key(["model.embed_tokens.weight", "lm_head.weight"],
+                                   by_suffix=True) == "lm_head.weight"
+    with pytest.raises(FileNotFoundError, match="No supported weight files"):
+        assets.lm_head_weight(assets.ModelFiles(str(tmp_path / "nothing")))
 
 
 def test_parameters_match_the_reference_layout(small_assets, golden_small):
@@ -177,6 +180,13 @@ os.environ["FLASHHEAD_ENABLED"] = {enabled!r}
 import flash_head
 from vllm.model_executor.layers.logits_processor import LogitsProcessor
 from vllm.v1.sample.sampler import Sampler
+from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+seen = {{}}
+def fake_dummy_sampler_run(self, h):  # stands in for vLLM's warm-up (no GPU here)
+    from flash_head.patches import logits_processor as lp
+    seen["ids_inside"] = lp.flash_head_token_ids(h)
+    return "vllm-warmup"
+GPUModelRunner._dummy_sampler_run = fake_dummy_sampler_run
 before = (LogitsProcessor._get_logits, Sampler.forward)
 flash_head.register(); flash_head.register()
 after = (LogitsProcessor._get_logits, Sampler.forward)
@@ -189,6 +199,24 @@ if after != before:
     class FakeHead:
         def get_next_token_batched(self, h):
             return torch.arange(h.shape[0], dtype=torch.int64) + 5
+    class CountingHead(FakeHead):
+        calls = 0
+        def get_next_token_batched(self, h):
+            CountingHead.calls += 1
+            return super().get_next_token_batched(h)
+    lp._flash_head = CountingHead()
+    r = GPUModelRunner._dummy_sampler_run(None, torch.zeros(3, 8))
+    print("WARMUP", r, seen["ids_inside"], CountingHead.calls)
+    import tempfile
+    from flash_head.synthetic import HeadShape, make_head, save_assets
+    from flash_head.loading import METADATA_PATH
+    from flash_head.patches import engine
+    from vllm.v1.engine.llm_engine import LLMEngine
+    d = tempfile.mkdtemp()
+    save_assets(make_head(HeadShape(hidden=16, vocab=64, n_clusters=4, n_probes=2), seed=1), d)
+    print("ENGINE", hasattr(LLMEngine.from_engine_args, "__wrapped__"),
+          engine.publish_metadata(d), os.path.exists(METADATA_PATH),
+          engine.publish_metadata(tempfile.mkdtemp()), os.path.exists(METADATA_PATH))
     lp._flash_head = FakeHead()
     proc = LogitsProcessor.__new__(LogitsProcessor)
     proc.logits_as_input = False; proc.soft_cap = 30.0; proc.scale = 2.0
@@ -252,6 +280,10 @@ def test_register_and_hooks(enabled):
     assert status.split()[1] == "True"  # architecture aliases registered either way
     if enabled == "1":
         assert status.startswith("PATCHED")
+        # warm-up: one FlashHead step, vLLM's own warm-up on real logits
+        assert "WARMUP vllm-warmup None 1" in res.stdout
+        # engine hooks: metadata published for a FlashHead model, withdrawn for another
+        assert "ENGINE True True True False False" in res.stdout
         assert "IDS torch.int32 [[5]]" in res.stdout  # ids untouched by soft-cap / scale
         assert "SAMPLED [[5]] None" in res.stdout
         # logprobs over the step's candidate set when a request asks for k of them
