@@ -49,7 +49,7 @@ constexpr int kS2ATile = 128 * 128;  // bytes of the w_perm tile of one k-block
 constexpr int kS2MaxStages = 12;
 constexpr int kS2Lag = 3;          // k-blocks of hidden-row copies in flight per loader
 constexpr int kS2SmemMax = 227 * 1024;
-constexpr int kS2TileClusters = 1024;  // clusters per k_s2_tiles CTA
+constexpr int kS2TileClusters = 64;  // clusters per k_s2_tiles CTA: 8 tiles, one per warp
 
 struct S2Tile {
   int n_cl;                        // clusters in the tile (1..8)
@@ -84,33 +84,31 @@ __global__ void k_s2_fill(const int32_t *probes, int rows, int p, int K, int bas
 }
 
 // One CTA of 256 threads per kS2TileClusters clusters: the CTA's probed
-// clusters (ascending id) are cut into tiles of kS2Clusters; each warp builds
-// whole tiles. Tile indices come from one atomic per CTA (order across CTAs is
+// clusters (ascending id) are cut into tiles of kS2Clusters, one per warp.
+// Tile indices come from one atomic per CTA (order across CTAs is
 // irrelevant: the tiles partition the probed clusters and their results meet
 // in a max). meta must be zero on entry.
 __global__ void __launch_bounds__(256) k_s2_tiles(const int *cnt, const unsigned char *list, int K,
                                                   S2Tile *tiles, S2Meta *meta) {
+  static_assert(kS2TileClusters == 64 && kS2TileClusters / kS2Clusters == 8, "one tile per warp");
   __shared__ int ids[kS2TileClusters];
-  __shared__ int scan_scratch[33];
-  __shared__ int s_base;
+  __shared__ int s_base, s_total;
   __shared__ uint32_t w_union[8][8];
   __shared__ uint32_t w_rowmask[8][kS2Clusters][8];
   __shared__ uint32_t w_posmask[8][kS2Clusters][8];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c0 = blockIdx.x * kS2TileClusters;
-  // 4 consecutive clusters per thread
-  int f[4], nf = 0;
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int c = c0 + 4 * tid + u;
-    f[u] = c < K && __ldcg(&cnt[c]) > 0;
-    nf += f[u];
+  if (warp == 0) {  // the 64 clusters' probed flags, compacted in id order by two ballots
+    const int ca = c0 + lane, cb = c0 + 32 + lane;
+    const bool fa = ca < K && __ldcg(&cnt[ca]) > 0, fb = cb < K && __ldcg(&cnt[cb]) > 0;
+    const unsigned ma = __ballot_sync(0xFFFFFFFFu, fa), mb = __ballot_sync(0xFFFFFFFFu, fb);
+    const unsigned below = (1u << lane) - 1u;
+    if (fa) ids[__popc(ma & below)] = ca;
+    if (fb) ids[__popc(ma) + __popc(mb & below)] = cb;
+    if (lane == 0) s_total = __popc(ma) + __popc(mb);
   }
-  int total;
-  int pos = block_exclusive_scan(nf, scan_scratch, &total);
-#pragma unroll
-  for (int u = 0; u < 4; ++u)
-    if (f[u]) ids[pos++] = c0 + 4 * tid + u;
+  __syncthreads();
+  const int total = s_total;
   const int n_tiles = (total + kS2Clusters - 1) / kS2Clusters;
   if (tid == 0) s_base = n_tiles ? atomicAdd(&meta->n_tiles, n_tiles) : 0;
   __syncthreads();
@@ -118,7 +116,7 @@ __global__ void __launch_bounds__(256) k_s2_tiles(const int *cnt, const unsigned
   uint32_t *un = w_union[warp];
   uint32_t(*rm)[8] = w_rowmask[warp];
   uint32_t(*pm)[8] = w_posmask[warp];
-  for (int t = warp; t < n_tiles; t += 8) {
+  for (int t = warp; t < n_tiles; t += 8) {  // at most one pass
     const int j0 = t * kS2Clusters, ncl = min(kS2Clusters, total - j0);
     for (int i = lane; i < 8 + 2 * kS2Clusters * 8; i += 32) {
       if (i < 8) un[i] = 0u;
@@ -199,6 +197,7 @@ struct S2TcArgs {
 };
 
 struct S2TcCtrl {
+  S2Tile tile[2];  // the epilogue's copies of its current and previous tile
   uint64_t full_a[kS2MaxStages];
   uint64_t full_b[kS2MaxStages];
   uint64_t empty[kS2MaxStages];
@@ -308,9 +307,11 @@ __global__ void __launch_bounds__(kS2Threads, 1)
       uint32_t ph = 0u;
       bool ok = true;
       int i = 0;
+      int n_next = blockIdx.x < n_tiles ? __ldcg(&a.tiles[blockIdx.x].n) : 0;
       for (int t = blockIdx.x; t < n_tiles && ok; t += G, ++i) {
         const int buf = i & 1, use = i >> 1;
-        const int n_pad = max(16, (min(__ldcg(&a.tiles[t].n), kS2MaxRows) + 15) & ~15);
+        const int n_pad = max(16, (min(n_next, kS2MaxRows) + 15) & ~15);
+        if (t + G < n_tiles) n_next = __ldcg(&a.tiles[t + G].n);  // in flight during this tile
         const uint32_t idesc = a.idesc0 | ((uint32_t)(n_pad >> 3) << 17);
         if (use > 0) {
           if (!mbar_wait(&S.acc_empty[buf], (uint32_t)((use - 1) & 1), a.polls)) {
@@ -404,12 +405,22 @@ __global__ void __launch_bounds__(kS2Threads, 1)
     const int j = m >> 4, tok = m & 15;
     bool ok = true;
     int i = 0;
+    const int et = tid - 192;  // epilogue thread 0..127
     for (int t = blockIdx.x; t < n_tiles; t += G, ++i) {
       const int buf = i & 1, use = i >> 1;
-      const S2Tile &T = a.tiles[t];
-      const int ncl = min(max(__ldcg(&T.n_cl), 0), kS2Clusters);
-      const int n = min(max(__ldcg(&T.n), 0), kS2MaxRows);
-      const int cj = j < ncl ? __ldcg(&T.cl[j]) : -1;
+      // the tile's descriptor into shared memory in one round trip (the
+      // loop below reads it per column); the barrier also orders this copy
+      // after every epilogue warp finished the tile two back
+      {
+        const uint4 *src = reinterpret_cast<const uint4 *>(&a.tiles[t]);
+        uint4 *dst = reinterpret_cast<uint4 *>(&S.tile[buf]);
+        for (int k = et; k < (int)(sizeof(S2Tile) / 16); k += kS2EpiThreads) dst[k] = __ldcg(src + k);
+        nbar_sync(1, kS2EpiThreads);
+      }
+      const S2Tile &T = S.tile[buf];
+      const int ncl = min(max(T.n_cl, 0), kS2Clusters);
+      const int n = min(max(T.n, 0), kS2MaxRows);
+      const int cj = j < ncl ? T.cl[j] : -1;
       const bool valid = cj >= 0 && tok < a.cap;
       const uint32_t vid = valid ? (uint32_t)__ldg(&a.vocab_map[cj * a.cap + tok]) : 0u;
       if (ok && !mbar_wait(&S.acc_full[buf], (uint32_t)(use & 1), a.polls)) {
@@ -422,7 +433,7 @@ __global__ void __launch_bounds__(kS2Threads, 1)
         const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * 256);
         for (int w = 0; w * 32 < n; ++w) {
           // this lane's cluster mask word, and the warp's (both clusters)
-          const uint32_t mine = j < ncl ? __ldcg(&T.mask[j][w]) : 0u;
+          const uint32_t mine = j < ncl ? T.mask[j][w] : 0u;
           const uint32_t both = mine | __shfl_xor_sync(0xFFFFFFFFu, mine, 16);
           if (both == 0u) continue;  // warp-uniform
           uint32_t v[2][16];

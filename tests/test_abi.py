@@ -130,7 +130,7 @@ def test_valid_descriptor_and_workspace_size(lib):
                 want += rnd(rows * 2048 * 2)
             if rows >= 16:  # batched steps: stage-2 index (counts + meta, row lists, tiles)
                 K = 8016
-                tiles = -(-K // 8) + -(-K // 1024) + 1
+                tiles = -(-K // 8) + -(-K // 64) + 1
                 want += rnd(K * 4) + 256 + rnd(K * 256) + rnd(tiles * 640)
             assert lib.fh_workspace_bytes(h, rows) == want
         assert lib.fh_workspace_bytes(None, 1) == 0
