@@ -85,16 +85,56 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
   if (tid == 0) S.n_bkt = 0;
   grid_dep_wait();  // the partials come from the stage-1 kernel before this one
   grid_dep_launch();
-  const float *row = a.part + (size_t)r * a.row_stride;
-  for (int k = tid; k < K; k += kHSelThreads) {
-    float v = __ldcg(&row[k]);
-    for (int s = 1; s < a.splits; ++s) v += __ldcg(&row[(size_t)s * a.split_stride + k]);
-    if (a.scale) v *= __ldg(&a.scale[k]);
-    if (a.do_sample)
-      v = v / a.temperature +
-          gumbel(a.rng, kStageClusters, (uint32_t)r, (uint32_t)(a.cluster_base + k));
-    if (a.scores_out) a.scores_out[(size_t)r * a.out_stride + k] = v;
-    sc[k] = sanitize(v);
+  // The row's partials as float4 groups (rows are padded to 64 floats and
+  // 16-byte aligned), up to 4 groups per thread, the loads of two splits at a
+  // time issued before they are summed (in split order).
+  const float4 *row4 = reinterpret_cast<const float4 *>(a.part + (size_t)r * a.row_stride);
+  const size_t split4 = a.split_stride / 4;
+  const int G4 = (K + 3) / 4;
+  constexpr int kPer = kSelMaxItems / 4 / kHSelThreads;
+  float4 acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int g = tid + kHSelThreads * i;
+    acc[i] = g < G4 ? __ldcg(row4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int s0 = 1; s0 < a.splits; s0 += 2) {
+    float4 nx[2][kPer];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int g = tid + kHSelThreads * i;
+        nx[u][i] = (s0 + u < a.splits && g < G4) ? __ldcg(row4 + (size_t)(s0 + u) * split4 + g)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        if (s0 + u < a.splits) {
+          acc[i].x += nx[u][i].x;
+          acc[i].y += nx[u][i].y;
+          acc[i].z += nx[u][i].z;
+          acc[i].w += nx[u][i].w;
+        }
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int g = tid + kHSelThreads * i;
+    const float vv[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = 4 * g + u;
+      if (g >= G4 || k >= K) continue;
+      float v = vv[u];
+      if (a.scale) v *= __ldg(&a.scale[k]);
+      if (a.do_sample)
+        v = v / a.temperature +
+            gumbel(a.rng, kStageClusters, (uint32_t)r, (uint32_t)(a.cluster_base + k));
+      if (a.scores_out) a.scores_out[(size_t)r * a.out_stride + k] = v;
+      sc[k] = sanitize(v);
+    }
   }
   __syncthreads();
   // level 1: coarse bins (key >> 24), one private histogram per warp
