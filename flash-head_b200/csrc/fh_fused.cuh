@@ -536,7 +536,9 @@ __device__ __forceinline__ const char *wp_bytes(const FusedArgs &a) {
   return reinterpret_cast<const char *>(a.w_perm);
 }
 
-template <typename HT, typename WT, int R>
+// SAMPLE: draws (the sampling calls) instead of greedy ids; a template
+// parameter so the greedy instance carries no noise code.
+template <typename HT, typename WT, int R, bool SAMPLE>
 __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   using M1 = typename S1Mma<WT>::T;  // stage-1 mma operand type
   constexpr bool kFp8 = sizeof(WT) == 1;
@@ -723,7 +725,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
     }
     const int k = c0 + kk;
     float sc = v * S.scale[kk];
-    if (a.do_sample)
+    if (SAMPLE)
       sc = sc / a.temperature + gumbel(a.rng, kStageClusters, (uint32_t)col, (uint32_t)k);
     S.local[col][kk] = sc;
     a.scores[(size_t)col * a.score_stride + k] = sc;
@@ -773,7 +775,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
       const float z = -normcdfinvf(frac);
       if (lane == 0) S.t_est[r] = mean + z * sd;
       const float t_pf = mean + (z - kPrefetchMargin) * sd;
-      if (!a.do_sample && nc > 1 && cluster_bytes % 16 == 0)
+      if (!SAMPLE && nc > 1 && cluster_bytes % 16 == 0)
         for (int i = lane; i < nc; i += 32)
           if (S.local[r][i] > t_pf)
             bulk_prefetch_l2(wp_bytes(a) + (size_t)(c0 + i) * cluster_bytes, (uint32_t)cluster_bytes);
@@ -1131,7 +1133,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
               const uint32_t vid =
                   (uint32_t)(d.vid_in_smem ? S.vid[s][row] : __ldg(&a.vocab_map[d.src + row]));
               float key = v;
-              if (a.do_sample)
+              if (SAMPLE)
                 key = v / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)d.row, vid);
               best = pack(key, vid);
             }

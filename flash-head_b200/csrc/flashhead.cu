@@ -110,10 +110,10 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
-template <typename HT, typename WT, int R>
+template <typename HT, typename WT, int R, bool SAMPLE>
 cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream) {
   static bool attr_done[128];
-  auto kern = fh::k_fused_step<HT, WT, R>;
+  auto kern = fh::k_fused_step<HT, WT, R, SAMPLE>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -171,9 +171,14 @@ cudaError_t launch_fused_t(const fh::FusedArgs &a, int grid, cudaStream_t stream
 
 template <typename HT, typename WT>
 cudaError_t launch_fused_rows(const fh::FusedArgs &a, int grid, cudaStream_t s) {
-  if (a.rows == 1) return launch_fused_t<HT, WT, 1>(a, grid, s);
-  if (a.rows == 2) return launch_fused_t<HT, WT, 2>(a, grid, s);
-  return launch_fused_t<HT, WT, 4>(a, grid, s);
+  if (a.do_sample) {
+    if (a.rows == 1) return launch_fused_t<HT, WT, 1, true>(a, grid, s);
+    if (a.rows == 2) return launch_fused_t<HT, WT, 2, true>(a, grid, s);
+    return launch_fused_t<HT, WT, 4, true>(a, grid, s);
+  }
+  if (a.rows == 1) return launch_fused_t<HT, WT, 1, false>(a, grid, s);
+  if (a.rows == 2) return launch_fused_t<HT, WT, 2, false>(a, grid, s);
+  return launch_fused_t<HT, WT, 4, false>(a, grid, s);
 }
 
 cudaError_t launch_fused(int hdt, int wdt, const fh::FusedArgs &a, int grid, cudaStream_t s) {
