@@ -27,15 +27,16 @@ constexpr int kGemmS1MinRows = FH_GEMM_S1_MIN_ROWS;
 static_assert(kGemmS1MinRows <= kBatchMinRows, "GEMM stage 1 covers the batched steps");
 
 // ---------------------------------------------------------------------------
-// Top-p clusters of one row per CTA (1024 threads): the same rule as k_select
-// (the p largest (score, -id) keys, ids ascending) found with two 8-bit
-// histogram levels over the monotone key (bf16 resolution), an exact rank of
-// the threshold bucket's few keys (a radix select over the remaining 48 key
-// bits when the bucket is large), and one ordered compaction.
-// Dynamic shared memory: K floats (the row) + 32 warp histograms of 256 bins.
+// Top-p clusters of one row per CTA: the same rule as k_select (the p largest
+// (score, -id) keys, ids ascending) found with two 8-bit histogram levels over
+// the monotone key (bf16 resolution), an exact rank of the threshold bucket's
+// few keys (a radix select over the remaining 48 key bits when the bucket is
+// large), and one ordered compaction.
+// NT = 1024 threads for up to one row per SM; NT = 512 (two CTAs per SM) when
+// there are more rows than SMs, so that every row is selected in one wave.
+// Dynamic shared memory: K floats (the row) + one 256-bin histogram per warp.
 // ---------------------------------------------------------------------------
-constexpr int kHSelThreads = 1024;
-constexpr int kHSelWarps = kHSelThreads / 32;
+constexpr int kHSelMaxWarps = 32;
 constexpr int kHSelBkt = 256;  // bucket keys ranked directly
 
 struct HSelSmem {
@@ -44,14 +45,14 @@ struct HSelSmem {
   int n_bkt;
   int bin, above, cnt;
   unsigned long long T;
-  int warp_counts[kHSelWarps];
+  int warp_counts[kHSelMaxWarps];
 };
 
 __host__ __device__ __forceinline__ size_t hsel_row_bytes(int K) {
   return ((size_t)K * sizeof(float) + 15) / 16 * 16;
 }
-__host__ __device__ __forceinline__ size_t hsel_smem_bytes(int K) {
-  return hsel_row_bytes(K) + (size_t)kHSelWarps * 256 * sizeof(uint32_t) + sizeof(HSelSmem);
+__host__ __device__ __forceinline__ size_t hsel_smem_bytes(int K, int threads) {
+  return hsel_row_bytes(K) + (size_t)(threads / 32) * 256 * sizeof(uint32_t) + sizeof(HSelSmem);
 }
 
 struct HSelArgs {
@@ -72,77 +73,82 @@ struct HSelArgs {
   long long *cand_out;   // [rows, p] signed packed (key, global id) words, or null
 };
 
-__global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
+template <int NT>
+__global__ void __launch_bounds__(NT, 1024 / NT) k_select_hist(HSelArgs a) {
+  constexpr int kWarps = NT / 32;
+  static_assert(kWarps <= kHSelMaxWarps, "one histogram per warp");
   extern __shared__ __align__(16) unsigned char hsm[];
   const int K = a.K, p = a.p;
   float *sc = reinterpret_cast<float *>(hsm);
-  uint32_t *wh = reinterpret_cast<uint32_t *>(hsm + hsel_row_bytes(K));  // [32][256]
+  uint32_t *wh = reinterpret_cast<uint32_t *>(hsm + hsel_row_bytes(K));  // [kWarps][256]
   HSelSmem &S = *reinterpret_cast<HSelSmem *>(hsm + hsel_row_bytes(K) +
-                                              (size_t)kHSelWarps * 256 * sizeof(uint32_t));
+                                              (size_t)kWarps * 256 * sizeof(uint32_t));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
-  for (int i = tid; i < kHSelWarps * 256; i += kHSelThreads) wh[i] = 0u;
+  for (int i = tid; i < kWarps * 256; i += NT) wh[i] = 0u;
   if (tid < 256) S.hist[tid] = 0u;
   if (tid == 0) S.n_bkt = 0;
   grid_dep_wait();  // the partials come from the stage-1 kernel before this one
   grid_dep_launch();
   // The row's partials as float4 groups (rows are padded to 64 floats and
-  // 16-byte aligned), up to 4 groups per thread, the loads of two splits at a
-  // time issued before they are summed (in split order).
+  // 16-byte aligned), 4 groups per thread and pass, the loads of two splits at
+  // a time issued before they are summed (in split order).
   const float4 *row4 = reinterpret_cast<const float4 *>(a.part + (size_t)r * a.row_stride);
   const size_t split4 = a.split_stride / 4;
   const int G4 = (K + 3) / 4;
-  constexpr int kPer = kSelMaxItems / 4 / kHSelThreads;
-  float4 acc[kPer];
+  constexpr int kPer = 4;
+  for (int g0 = 0; g0 < G4; g0 += kPer * NT) {
+    float4 acc[kPer];
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int g = tid + kHSelThreads * i;
-    acc[i] = g < G4 ? __ldcg(row4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  for (int s0 = 1; s0 < a.splits; s0 += 2) {
-    float4 nx[2][kPer];
+    for (int i = 0; i < kPer; ++i) {
+      const int g = g0 + tid + NT * i;
+      acc[i] = g < G4 ? __ldcg(row4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int s0 = 1; s0 < a.splits; s0 += 2) {
+      float4 nx[2][kPer];
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < 2; ++u)
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        const int g = tid + kHSelThreads * i;
-        nx[u][i] = (s0 + u < a.splits && g < G4) ? __ldcg(row4 + (size_t)(s0 + u) * split4 + g)
-                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-    for (int u = 0; u < 2; ++u)
-#pragma unroll
-      for (int i = 0; i < kPer; ++i)
-        if (s0 + u < a.splits) {
-          acc[i].x += nx[u][i].x;
-          acc[i].y += nx[u][i].y;
-          acc[i].z += nx[u][i].z;
-          acc[i].w += nx[u][i].w;
+        for (int i = 0; i < kPer; ++i) {
+          const int g = g0 + tid + NT * i;
+          nx[u][i] = (s0 + u < a.splits && g < G4) ? __ldcg(row4 + (size_t)(s0 + u) * split4 + g)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-  }
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int g = tid + kHSelThreads * i;
-    const float vv[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+      for (int u = 0; u < 2; ++u)
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int k = 4 * g + u;
-      if (g >= G4 || k >= K) continue;
-      float v = vv[u];
-      if (a.scale) v *= __ldg(&a.scale[k]);
-      if (a.do_sample)
-        v = v / a.temperature +
-            gumbel(a.rng, kStageClusters, (uint32_t)r, (uint32_t)(a.cluster_base + k));
-      if (a.scores_out) a.scores_out[(size_t)r * a.out_stride + k] = v;
-      sc[k] = sanitize(v);
+        for (int i = 0; i < kPer; ++i)
+          if (s0 + u < a.splits) {
+            acc[i].x += nx[u][i].x;
+            acc[i].y += nx[u][i].y;
+            acc[i].z += nx[u][i].z;
+            acc[i].w += nx[u][i].w;
+          }
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int g = g0 + tid + NT * i;
+      const float vv[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = 4 * g + u;
+        if (g >= G4 || k >= K) continue;
+        float v = vv[u];
+        if (a.scale) v *= __ldg(&a.scale[k]);
+        if (a.do_sample)
+          v = v / a.temperature +
+              gumbel(a.rng, kStageClusters, (uint32_t)r, (uint32_t)(a.cluster_base + k));
+        if (a.scores_out) a.scores_out[(size_t)r * a.out_stride + k] = v;
+        sc[k] = sanitize(v);
+      }
     }
   }
   __syncthreads();
   // level 1: coarse bins (key >> 24), one private histogram per warp
-  for (int k = tid; k < K; k += kHSelThreads) atomicAdd(&wh[warp * 256 + (mono(sc[k]) >> 24)], 1u);
+  for (int k = tid; k < K; k += NT) atomicAdd(&wh[warp * 256 + (mono(sc[k]) >> 24)], 1u);
   __syncthreads();
   if (tid < 256) {
     uint32_t t = 0;
-    for (int w = 0; w < kHSelWarps; ++w) t += wh[w * 256 + tid];
+    for (int w = 0; w < kWarps; ++w) t += wh[w * 256 + tid];
     S.hist[tid] = t;
   }
   __syncthreads();
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
   if (tid < 256) S.hist[tid] = 0u;
   __syncthreads();
   // level 2: fine bins ((key >> 16) & 255) of the coarse bin
-  for (int k = tid; k < K; k += kHSelThreads) {
+  for (int k = tid; k < K; k += NT) {
     const uint32_t m = mono(sc[k]);
     if ((m >> 24) == cb) atomicAdd(&S.hist[(m >> 16) & 255u], 1u);
   }
@@ -179,7 +185,7 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
   const int need = p - above1 - S.above;
   // bucket keys
   if (need > 0)
-    for (int k = tid; k < K; k += kHSelThreads) {
+    for (int k = tid; k < K; k += NT) {
       const float v = sc[k];
       if ((mono(v) >> 16) == P) {
         const int m = atomicAdd(&S.n_bkt, 1);
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
   } else if (nb <= kHSelBkt) {
     if (tid == 0) S.T = (unsigned long long)P << 48;  // fewer keys than needed: the whole bucket
     __syncthreads();
-    for (int j = tid; j < nb; j += kHSelThreads) {
+    for (int j = tid; j < nb; j += NT) {
       const unsigned long long mine = S.bkt[j];
       int rank = 0;
       for (int m = 0; m < nb; ++m) rank += S.bkt[m] > mine;
@@ -207,7 +213,7 @@ __global__ void __launch_bounds__(kHSelThreads) k_select_hist(HSelArgs a) {
       if (tid < 256) S.hist[tid] = 0u;
       __syncthreads();
       const unsigned long long hi_sel = pre >> (shift + 8);
-      for (int k = tid; k < K; k += kHSelThreads) {
+      for (int k = tid; k < K; k += NT) {
         const unsigned long long key = pack(sc[k], (uint32_t)k);
         if ((key >> (shift + 8)) == hi_sel) atomicAdd(&S.hist[(key >> shift) & 255u], 1u);
       }

@@ -5,8 +5,8 @@
 // packed (logit, vocab id) words and their max reduction follow it
 // (fused.py:148-163).
 //
-//   k_s2_fill      probe lists -> per cluster the hidden rows that probe it
-//                  (counts and row lists, by atomics).
+//   k_s2_fill      probe lists -> per cluster a bit map of the hidden rows
+//                  that probe it (atomicOr).
 //   k_s2_tiles     probed clusters -> tiles of up to 8 clusters (128 w_perm
 //                  rows, the MMA's M); per tile the union of the clusters'
 //                  rows (the MMA's N, at most 256) and, per cluster, a bit mask
@@ -20,9 +20,11 @@
 //                union, K = 16) per k-block and commits stages and finished
 //                accumulators;
 //     warps 2-5  gather the union's hidden rows of each k-block with
-//                cp.async into the 128-byte-swizzled B operand, a few stages
-//                ahead, then make them visible to the tensor core (proxy
-//                fence) and arrive on the stage's barrier;
+//                cp.async into the 128-byte-swizzled B operand; each
+//                thread's copies arrive on the stage's barrier as they
+//                complete (cp.async.mbarrier.arrive), and the MMA issuer
+//                fences the generic-proxy writes before the tensor core
+//                reads them;
 //     warps 6-9  epilogue: thread = one w_perm row (TMEM lane); per union
 //                column whose row probed this thread's cluster, the logit (or
 //                the Gumbel key in sampling mode) packed with the vocab id,
@@ -47,7 +49,6 @@ constexpr int kS2Clusters = 8;     // clusters per tile (16 rows each: M = 128)
 constexpr int kS2MaxRows = 256;    // hidden rows per launch (union N <= 256)
 constexpr int kS2ATile = 128 * 128;  // bytes of the w_perm tile of one k-block
 constexpr int kS2MaxStages = 12;
-constexpr int kS2Lag = 3;          // k-blocks of hidden-row copies in flight per loader
 constexpr int kS2SmemMax = 227 * 1024;
 constexpr int kS2TileClusters = 64;  // clusters per k_s2_tiles CTA: 8 tiles, one per warp
 
@@ -69,42 +70,58 @@ struct S2Meta {
 };
 
 // ---------------------------------------------------------------------------
-// Index: per cluster the rows that probe it.
+// Index: per cluster a bit map of the hidden rows (of this launch) that probe
+// it, 8 words per cluster. Zero on entry (the host clears it per launch).
 // ---------------------------------------------------------------------------
-__global__ void k_s2_fill(const int32_t *probes, int rows, int p, int K, int base, int *cnt,
-                          unsigned char *list) {
+constexpr int kS2MaskWords = kS2MaxRows / 32;
+
+__global__ void k_s2_fill(const int32_t *probes, int rows, int p, int K, int base, uint32_t *bm) {
   const int n = rows * p;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int c = probes[i] - base;
-    if (c >= 0 && c < K) {
-      const int slot = atomicAdd(&cnt[c], 1);
-      if (slot < kS2MaxRows) list[(size_t)c * kS2MaxRows + slot] = (unsigned char)(i / p);
-    }
+    const int r = i / p;
+    if (c >= 0 && c < K && r < kS2MaxRows)
+      atomicOr(&bm[(size_t)c * kS2MaskWords + (r >> 5)], 1u << (r & 31));
   }
 }
 
 // One CTA of 256 threads per kS2TileClusters clusters: the CTA's probed
 // clusters (ascending id) are cut into tiles of kS2Clusters, one per warp.
-// Tile indices come from one atomic per CTA (order across CTAs is
-// irrelevant: the tiles partition the probed clusters and their results meet
-// in a max). meta must be zero on entry.
-__global__ void __launch_bounds__(256) k_s2_tiles(const int *cnt, const unsigned char *list, int K,
-                                                  S2Tile *tiles, S2Meta *meta) {
+// Per tile: the union of the clusters' row maps, its rows in ascending order
+// (their positions are the MMA's N columns), and per cluster a bit mask over
+// those positions, built with ballots (lane = position). Tile indices come
+// from one atomic per CTA (order across CTAs is irrelevant: the tiles
+// partition the probed clusters and their results meet in a max). meta must
+// be zero on entry.
+__global__ void __launch_bounds__(256) k_s2_tiles(const uint32_t *bm, int K, S2Tile *tiles,
+                                                  S2Meta *meta) {
   static_assert(kS2TileClusters == 64 && kS2TileClusters / kS2Clusters == 8, "one tile per warp");
-  __shared__ int ids[kS2TileClusters];
-  __shared__ int s_base, s_total;
-  __shared__ uint32_t w_union[8][8];
-  __shared__ uint32_t w_rowmask[8][kS2Clusters][8];
-  __shared__ uint32_t w_posmask[8][kS2Clusters][8];
+  static_assert(kS2MaskWords == 8, "eight mask words per cluster");
+  __shared__ uint32_t s_bm[kS2TileClusters][kS2MaskWords];
+  __shared__ int ids[kS2TileClusters];  // local index of the j-th probed cluster
+  __shared__ __align__(16) unsigned char s_rows[8][kS2MaxRows];
+  __shared__ int s_base, s_total, s_nmax;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c0 = blockIdx.x * kS2TileClusters;
+  for (int i = tid; i < kS2TileClusters * kS2MaskWords; i += 256) {
+    const int c = c0 + i / kS2MaskWords;
+    (&s_bm[0][0])[i] = c < K ? __ldcg(&bm[(size_t)c0 * kS2MaskWords + i]) : 0u;
+  }
+  if (tid == 0) s_nmax = 0;
+  __syncthreads();
   if (warp == 0) {  // the 64 clusters' probed flags, compacted in id order by two ballots
-    const int ca = c0 + lane, cb = c0 + 32 + lane;
-    const bool fa = ca < K && __ldcg(&cnt[ca]) > 0, fb = cb < K && __ldcg(&cnt[cb]) > 0;
-    const unsigned ma = __ballot_sync(0xFFFFFFFFu, fa), mb = __ballot_sync(0xFFFFFFFFu, fb);
+    bool f[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t any = 0u;
+#pragma unroll
+      for (int w = 0; w < kS2MaskWords; ++w) any |= s_bm[32 * h + lane][w];
+      f[h] = any != 0u;
+    }
+    const unsigned ma = __ballot_sync(0xFFFFFFFFu, f[0]), mb = __ballot_sync(0xFFFFFFFFu, f[1]);
     const unsigned below = (1u << lane) - 1u;
-    if (fa) ids[__popc(ma & below)] = ca;
-    if (fb) ids[__popc(ma) + __popc(mb & below)] = cb;
+    if (f[0]) ids[__popc(ma & below)] = lane;
+    if (f[1]) ids[__popc(ma) + __popc(mb & below)] = 32 + lane;
     if (lane == 0) s_total = __popc(ma) + __popc(mb);
   }
   __syncthreads();
@@ -112,66 +129,59 @@ __global__ void __launch_bounds__(256) k_s2_tiles(const int *cnt, const unsigned
   const int n_tiles = (total + kS2Clusters - 1) / kS2Clusters;
   if (tid == 0) s_base = n_tiles ? atomicAdd(&meta->n_tiles, n_tiles) : 0;
   __syncthreads();
-  const int base = s_base;
-  uint32_t *un = w_union[warp];
-  uint32_t(*rm)[8] = w_rowmask[warp];
-  uint32_t(*pm)[8] = w_posmask[warp];
-  for (int t = warp; t < n_tiles; t += 8) {  // at most one pass
+  const int t = warp;
+  if (t < n_tiles) {
     const int j0 = t * kS2Clusters, ncl = min(kS2Clusters, total - j0);
-    for (int i = lane; i < 8 + 2 * kS2Clusters * 8; i += 32) {
-      if (i < 8) un[i] = 0u;
-      else if (i < 8 + kS2Clusters * 8) (&rm[0][0])[i - 8] = 0u;
-      else (&pm[0][0])[i - 8 - kS2Clusters * 8] = 0u;
-    }
-    __syncwarp();
-    // rows of every cluster into the union and per-cluster row bitmaps
+    const int lj = lane < ncl ? ids[j0 + lane] : 0;  // lane j: local index of cluster j
+    // union word w on lane w, its set bits' positions before it by a scan
+    uint32_t word = 0u;
     for (int j = 0; j < ncl; ++j) {
-      const int c = ids[j0 + j];
-      const int n = min(__ldcg(&cnt[c]), kS2MaxRows);
-      for (int s = lane; s < n; s += 32) {
-        const int r = list[(size_t)c * kS2MaxRows + s];
-        atomicOr(&un[r >> 5], 1u << (r & 31));
-        atomicOr(&rm[j][r >> 5], 1u << (r & 31));
-      }
+      const int cj = __shfl_sync(0xFFFFFFFFu, lj, j);
+      if (lane < kS2MaskWords) word |= s_bm[cj][lane];
     }
-    __syncwarp();
-    // union positions: prefix popcounts of the union words
-    uint32_t word = lane < 8 ? un[lane] : 0u;
-    int pc = __popc(word), incl = pc;
+    const int pc = __popc(word);
+    int incl = pc;
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
       const int x = __shfl_up_sync(0xFFFFFFFFu, incl, o);
       if (lane >= o) incl += x;
     }
-    const int before = incl - pc;  // union rows in words below this lane's word
     const int N = __shfl_sync(0xFFFFFFFFu, incl, 7);
-    S2Tile &T = tiles[base + t];
-    if (lane < 8) {
-      // rows of this word, ascending, at their union positions
-      int q = before;
-      for (uint32_t m = word; m; m &= m - 1u) T.rows[q++] = (unsigned char)(lane * 32 + __ffs(m) - 1);
-      // per cluster: each row of this word that probed cluster j sets its position bit
-      for (int j = 0; j < ncl; ++j) {
-        int q2 = before;
-        for (uint32_t m = word; m; m &= m - 1u, ++q2) {
-          const int b = __ffs(m) - 1;
-          if (rm[j][lane] & (1u << b)) atomicOr(&pm[j][q2 >> 5], 1u << (q2 & 31));
-        }
-      }
+    unsigned char *rows = s_rows[warp];
+    // rows in ascending order: lane b places bit b of every union word
+#pragma unroll
+    for (int w = 0; w < kS2MaskWords; ++w) {
+      const uint32_t uw = __shfl_sync(0xFFFFFFFFu, word, w);
+      const int before = __shfl_sync(0xFFFFFFFFu, incl - pc, w);
+      if ((uw >> lane) & 1u) rows[before + __popc(uw & ((1u << lane) - 1u))] = (unsigned char)(32 * w + lane);
     }
     __syncwarp();
-    for (int i = lane; i < kS2Clusters * 8; i += 32) {
-      const int j = i >> 3;
-      T.mask[j][i & 7] = j < ncl ? pm[j][i & 7] : 0u;
+    S2Tile &T = tiles[s_base + t];
+    // per cluster and 32 positions: ballot of "the position's row probed it"
+#pragma unroll
+    for (int w = 0; w < kS2MaskWords; ++w) {
+      const int q = 32 * w + lane;
+      const int r = q < N ? rows[q] : 0;
+#pragma unroll
+      for (int j = 0; j < kS2Clusters; ++j) {
+        const int cj = __shfl_sync(0xFFFFFFFFu, lj, j);
+        const bool hit = q < N && j < ncl && ((s_bm[cj][r >> 5] >> (r & 31)) & 1u);
+        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, hit);
+        if (lane == j) T.mask[j][w] = bal;
+      }
     }
-    if (lane < kS2Clusters) T.cl[lane] = lane < ncl ? ids[j0 + lane] : -1;
+    const uint32_t *rw = reinterpret_cast<const uint32_t *>(rows);
+    for (int k = lane; k < kS2MaxRows / 4; k += 32)
+      reinterpret_cast<uint32_t *>(T.rows)[k] = 4 * k < N ? rw[k] : 0u;
+    if (lane < kS2Clusters) T.cl[lane] = lane < ncl ? c0 + lj : -1;
     if (lane == 0) {
       T.n_cl = ncl;
       T.n = N;
-      atomicMax(&meta->n_max, N);
+      atomicMax(&s_nmax, N);
     }
-    __syncwarp();
   }
+  __syncthreads();
+  if (tid == 0 && s_nmax > 0) atomicMax(&meta->n_max, s_nmax);
 }
 
 // ---------------------------------------------------------------------------
@@ -197,7 +207,7 @@ struct S2TcArgs {
 };
 
 struct S2TcCtrl {
-  S2Tile tile[2];  // the epilogue's copies of its current and previous tile
+  __align__(16) S2Tile tile[2];  // the epilogue's copies of its current and previous tile (uint4 stores)
   uint64_t full_a[kS2MaxStages];
   uint64_t full_b[kS2MaxStages];
   uint64_t empty[kS2MaxStages];
@@ -207,18 +217,23 @@ struct S2TcCtrl {
   uint32_t tmem_base;
   uint32_t s_err;
 };
+static_assert(offsetof(S2TcCtrl, tile) % 16 == 0 && sizeof(S2Tile) % 16 == 0,
+              "tile copies are 16-byte stores");
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
                "r"(src_bytes)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// One arrival on bar once every cp.async this thread issued so far has
+// completed (the barrier's expected count includes it).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
 }
 
 template <bool SAMPLE>
@@ -327,6 +342,9 @@ __global__ void __launch_bounds__(kS2Threads, 1)
             ok = false;
             break;
           }
+          // the gathered hidden rows were written through the generic proxy
+          // (cp.async); the tensor core reads them through the async proxy
+          fence_proxy_async_smem();
           tc_fence_after();
           const uint32_t st = smem_u32(ring + (size_t)s * sb);
           const uint64_t ad = umma_desc_k(st);
@@ -347,12 +365,13 @@ __global__ void __launch_bounds__(kS2Threads, 1)
     }
   } else if (warp < 6) {
     // ------------------------------------------------ hidden rows (cp.async)
-    // k-block g of this CTA's sequence uses stage g % stages; its copies are
-    // committed as one group and announced kS2Lag groups later.
+    // k-block g of this CTA's sequence uses stage g % stages; each loader's
+    // copies of it arrive on the stage's barrier when they complete, so the
+    // loaders never wait for their own copies.
     const int lt = tid - 64;
     const char *hs = reinterpret_cast<const char *>(a.hidden);
     const size_t rb = (size_t)a.D * 2;
-    int s = 0, g = 0;
+    int s = 0;
     uint32_t ph = 0u;
     bool ok = true;
     for (int t = blockIdx.x; t < n_tiles && ok; t += G) {
@@ -371,7 +390,7 @@ __global__ void __launch_bounds__(kS2Threads, 1)
         src[i] = hs + (size_t)row * rb + c * 16;
         dst_off[i] = (uint32_t)(u * 128 + ((c ^ (u & 7)) << 4)) | (u < n ? 0u : 0x80000000u);
       }
-      for (int kb = 0; kb < a.nk; ++kb, ++g) {
+      for (int kb = 0; kb < a.nk; ++kb) {
         if (!mbar_wait(&S.empty[s], ph ^ 1u, a.polls)) {
           atomicOr(&S.s_err, kErrCopyTimeout);
           ok = false;
@@ -383,21 +402,14 @@ __global__ void __launch_bounds__(kS2Threads, 1)
           if (i < per)
             cp_async16(bst + (dst_off[i] & 0x7FFFFFFFu), src[i] + (size_t)kb * 128,
                        (dst_off[i] >> 31) ? 0u : 16u);
-        cp_async_commit();
-        if (g >= kS2Lag) {
-          cp_async_wait<kS2Lag>();
-          fence_proxy_async_smem();
-          mbar_arrive_cta(&S.full_b[(g - kS2Lag) % stages]);
-        }
+        cp_async_arrive_noinc(&S.full_b[s]);
         if (++s == stages) {
           s = 0;
           ph ^= 1u;
         }
       }
     }
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    for (int g2 = max(0, g - kS2Lag); g2 < g; ++g2) mbar_arrive_cta(&S.full_b[g2 % stages]);
+    cp_async_wait<0>();  // no copy of this thread is in flight when the CTA exits
   } else {
     // ------------------------------------------------ epilogue
     const int q = warp & 3;       // TMEM lane quadrant

@@ -236,11 +236,10 @@ struct Workspace {
   void *h16;                    // [rows, D] f16 copy of bf16 hidden rows (fp8 stage 1)
   // batched steps (rows >= kBatchMinRows) only, else null: the cluster-major
   // stage 2's index of one chunk of up to kS2MaxRows rows
-  int *s2_cnt;                  // [K] rows per cluster, followed by the meta words
-  fh::S2Meta *s2_meta;
-  unsigned char *s2_list;       // [K][kS2MaxRows] rows of every cluster
+  uint32_t *s2_bm;              // [K][kS2MaskWords] row bit map of every cluster,
+  fh::S2Meta *s2_meta;          //   followed by the meta words
   fh::S2Tile *s2_tiles;         // tile descriptors
-  size_t s2_zero_bytes;         // bytes of s2_cnt + s2_meta (zeroed per chunk)
+  size_t s2_zero_bytes;         // bytes of s2_bm + s2_meta (zeroed per chunk)
   size_t bytes;                 // bytes needed for `rows`
 };
 
@@ -267,13 +266,12 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
                          ? round_up((size_t)rows * d.hidden * 2, 256)
                          : 0;
   const bool batched = rows >= fh::kBatchMinRows;
-  const size_t kint = round_up((size_t)d.n_clusters * sizeof(int), 256);
+  const size_t bmb = round_up((size_t)d.n_clusters * fh::kS2MaskWords * sizeof(uint32_t), 256);
   const size_t max_tiles = (size_t)(d.n_clusters + fh::kS2Clusters - 1) / fh::kS2Clusters +
                            (size_t)(d.n_clusters + fh::kS2TileClusters - 1) / fh::kS2TileClusters +
                            1;
-  const size_t s2_list = round_up((size_t)d.n_clusters * fh::kS2MaxRows, 256);
   const size_t s2_tiles = round_up(max_tiles * sizeof(fh::S2Tile), 256);
-  const size_t inv = batched ? kint + sizeof(fh::S2Meta) + s2_list + s2_tiles : 0;
+  const size_t inv = batched ? bmb + sizeof(fh::S2Meta) + s2_tiles : 0;
   w.bytes = state + probes + scores + h16 + inv + 256;
   w.counter = reinterpret_cast<unsigned *>(p);
   w.epoch_bufs = reinterpret_cast<unsigned char *>(p + 256);
@@ -285,19 +283,16 @@ Workspace layout(const fh_head_desc &d, int rows, void *base, size_t ws_bytes) {
   w.probes = reinterpret_cast<int32_t *>(p + probes_off);
   w.scores = reinterpret_cast<float *>(p + scores_off);
   w.h16 = h16 ? p + h16_off : nullptr;
-  w.s2_cnt = nullptr;
+  w.s2_bm = nullptr;
   w.s2_meta = nullptr;
-  w.s2_list = nullptr;
   w.s2_tiles = nullptr;
-  w.s2_zero_bytes = kint + sizeof(fh::S2Meta);
+  w.s2_zero_bytes = bmb + sizeof(fh::S2Meta);
   if (batched) {
     size_t q = h16_off >= inv ? h16_off - inv : 0;
     w.s2_tiles = reinterpret_cast<fh::S2Tile *>(p + q);
     q += s2_tiles;
-    w.s2_list = reinterpret_cast<unsigned char *>(p + q);
-    q += s2_list;
-    w.s2_cnt = reinterpret_cast<int *>(p + q);
-    w.s2_meta = reinterpret_cast<fh::S2Meta *>(p + q + kint);
+    w.s2_bm = reinterpret_cast<uint32_t *>(p + q);
+    w.s2_meta = reinterpret_cast<fh::S2Meta *>(p + q + bmb);
   }
   return w;
 }
@@ -554,8 +549,11 @@ cudaError_t prepare_select_hist() {
   if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_attr_mutex);
   if (!done[dev]) {
-    e = cudaFuncSetAttribute(fh::k_select_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)fh::hsel_smem_bytes(fh::kSelMaxItems));
+    e = cudaFuncSetAttribute(fh::k_select_hist<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)fh::hsel_smem_bytes(fh::kSelMaxItems, 1024));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fh::k_select_hist<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)fh::hsel_smem_bytes(fh::kSelMaxItems, 512));
     if (e != cudaSuccess) return e;
     done[dev] = true;
   }
@@ -732,9 +730,15 @@ int run_s1_tc(const fh_head *h, const void *hidden, int rows, bool sample, float
   se.out_stride = out_stride;
   se.probes = probes;
   se.cand_out = cand_out;
-  FH_CHECK_LAUNCH(launch(fh::k_select_hist, dim3(rows), dim3(fh::kHSelThreads),
-                         fh::hsel_smem_bytes(d.n_clusters), s, true, se),
-                  "probe selection launch");
+  // more rows than SMs: two 512-thread CTAs per SM, so one wave selects every row
+  if (rows > sm_count())
+    FH_CHECK_LAUNCH(launch(fh::k_select_hist<512>, dim3(rows), dim3(512),
+                           fh::hsel_smem_bytes(d.n_clusters, 512), s, true, se),
+                    "probe selection launch");
+  else
+    FH_CHECK_LAUNCH(launch(fh::k_select_hist<1024>, dim3(rows), dim3(1024),
+                           fh::hsel_smem_bytes(d.n_clusters, 1024), s, true, se),
+                    "probe selection launch");
   return FH_OK;
 }
 
@@ -770,7 +774,7 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
   const fh_head_desc &d = h->d;
   const fh::RngKey rng = rng_key(seed, offset);
   const int K = d.n_clusters, p = d.n_probes;
-  if (!w.s2_cnt) return fail(FH_ERR_WORKSPACE, "workspace laid out without the stage-2 index");
+  if (!w.s2_bm) return fail(FH_ERR_WORKSPACE, "workspace laid out without the stage-2 index");
   const long long V = (long long)K * d.cluster_size;
   CUtensorMap tm_w;
   {
@@ -786,14 +790,13 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
   const int tile_ctas = (K + fh::kS2TileClusters - 1) / fh::kS2TileClusters;
   for (int r0 = 0; r0 < rows; r0 += fh::kS2MaxRows) {
     const int n = std::min(fh::kS2MaxRows, rows - r0);
-    FH_CHECK_LAUNCH(cudaMemsetAsync(w.s2_cnt, 0, w.s2_zero_bytes, s), "index reset");
+    FH_CHECK_LAUNCH(cudaMemsetAsync(w.s2_bm, 0, w.s2_zero_bytes, s), "index reset");
     const long long pairs = (long long)n * p;
     FH_CHECK_LAUNCH(launch(fh::k_s2_fill, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
-                           probes + (size_t)r0 * p, n, p, K, probe_base, w.s2_cnt, w.s2_list),
+                           probes + (size_t)r0 * p, n, p, K, probe_base, w.s2_bm),
                     "index fill launch");
     FH_CHECK_LAUNCH(launch(fh::k_s2_tiles, dim3(tile_ctas), dim3(256), 0, s, false,
-                           (const int *)w.s2_cnt, (const unsigned char *)w.s2_list, K, w.s2_tiles,
-                           w.s2_meta),
+                           (const uint32_t *)w.s2_bm, K, w.s2_tiles, w.s2_meta),
                     "tile build launch");
     fh::S2TcArgs a;
     memset(&a, 0, sizeof(a));
@@ -1401,9 +1404,8 @@ extern "C" FH_API int fh_get_next_token_noalloc(const fh_head *head, const void 
   w.split_stride = (size_t)rows * w.score_stride;
   w.epoch_bufs = nullptr;
   w.h16 = nullptr;
-  w.s2_cnt = nullptr;
+  w.s2_bm = nullptr;
   w.s2_meta = nullptr;
-  w.s2_list = nullptr;
   w.s2_tiles = nullptr;
   w.s2_zero_bytes = 0;
   w.bytes = kNoAllocBytes;

@@ -128,10 +128,10 @@ def test_valid_descriptor_and_workspace_size(lib):
                     + rnd(splits * rows * 8064 * 4) + 256)
             if rows >= 5:
                 want += rnd(rows * 2048 * 2)
-            if rows >= 16:  # batched steps: stage-2 index (counts + meta, row lists, tiles)
+            if rows >= 16:  # batched steps: stage-2 index (row bit maps + meta, tiles)
                 K = 8016
                 tiles = -(-K // 8) + -(-K // 64) + 1
-                want += rnd(K * 4) + 256 + rnd(K * 256) + rnd(tiles * 640)
+                want += rnd(K * 32) + 256 + rnd(tiles * 640)
             assert lib.fh_workspace_bytes(h, rows) == want
         assert lib.fh_workspace_bytes(None, 1) == 0
     finally:
