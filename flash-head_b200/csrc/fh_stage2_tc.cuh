@@ -7,14 +7,19 @@
 //
 //   k_s2_fill      probe lists -> per cluster a bit map of the hidden rows
 //                  that probe it (atomicOr).
-//   k_s2_tiles     probed clusters -> tiles of up to 8 clusters (128 w_perm
-//                  rows, the MMA's M); per tile the union of the clusters'
-//                  rows (the MMA's N, at most 256) and, per cluster, a bit mask
-//                  over the union positions of the rows that probed it.
-//   k_s2_tc        persistent, 10 warps:
-//     warp 0     lane 0 issues the TMA copies of each k-block (64 elements)
-//                of the tile's clusters (one 16-row box per cluster, 128-byte
-//                swizzle);
+//   k_s2_tiles     probed clusters -> tiles of 8 clusters (128 w_perm rows,
+//                  the MMA's M): an aligned window of 8 consecutive clusters
+//                  of which at least kS2WindowMin are probed is one tile,
+//                  copied as one 128-row box per k-block; the probed clusters
+//                  of the other windows are packed 8 to a tile, one 16-row box
+//                  each. Per tile the union of the clusters' rows (the MMA's
+//                  N, at most 256) and, per cluster, a bit mask over the union
+//                  positions of the rows that probed it.
+//   k_s2_tc        persistent, 10 warps; a ring stage holds kps k-blocks (64
+//                  elements each; kps = 2 when the ring stays 4 stages deep):
+//     warp 0     lane 0 issues the TMA copies of the tile's w_perm rows
+//                (128-byte swizzle) and prefetches the next tile's
+//                descriptor;
 //     warp 1     allocates 512 TMEM columns (two accumulators of 256), lane 0
 //                issues tcgen05.mma.kind::f16 (M = 128, N = the tile's padded
 //                union, K = 16) per k-block and commits stages and finished
@@ -22,9 +27,9 @@
 //     warps 2-5  gather the union's hidden rows of each k-block with
 //                cp.async into the 128-byte-swizzled B operand; each
 //                thread's copies arrive on the stage's barrier as they
-//                complete (cp.async.mbarrier.arrive), and the MMA issuer
-//                fences the generic-proxy writes before the tensor core
-//                reads them;
+//                complete (cp.async.mbarrier.arrive), the same barrier the
+//                TMA copies complete, and the MMA issuer fences the
+//                generic-proxy writes before the tensor core reads them;
 //     warps 6-9  epilogue: thread = one w_perm row (TMEM lane); per union
 //                column whose row probed this thread's cluster, the logit (or
 //                the Gumbel key in sampling mode) packed with the vocab id,
@@ -51,14 +56,17 @@ constexpr int kS2ATile = 128 * 128;  // bytes of the w_perm tile of one k-block
 constexpr int kS2MaxStages = 12;
 constexpr int kS2SmemMax = 227 * 1024;
 constexpr int kS2TileClusters = 64;  // clusters per k_s2_tiles CTA: 8 tiles, one per warp
+constexpr int kS2WindowMin = 7;      // probed clusters of 8 that make a window tile
+constexpr int kS2MinDeepStages = 4;  // two k-blocks per stage only if the ring keeps this many
 
 struct S2Tile {
-  int n_cl;                        // clusters in the tile (1..8)
+  int n_cl;                        // cluster slots in the tile (1..8)
   int n;                           // union rows
-  int cl[kS2Clusters];             // local cluster ids
+  int cl[kS2Clusters];             // local cluster id of slot j, or -1 (unprobed window slot)
   uint32_t mask[kS2Clusters][8];   // bit u: union row u probed cluster j
   unsigned char rows[kS2MaxRows];  // union rows (hidden row within the launch), ascending
-  int pad[22];
+  int win;                         // window tile: local id of its first cluster, else -1
+  int pad[21];
 };
 static_assert(sizeof(S2Tile) % 64 == 0, "tile descriptors are whole 64-byte lines");
 
@@ -85,22 +93,24 @@ __global__ void k_s2_fill(const int32_t *probes, int rows, int p, int K, int bas
   }
 }
 
-// One CTA of 256 threads per kS2TileClusters clusters: the CTA's probed
-// clusters (ascending id) are cut into tiles of kS2Clusters, one per warp.
-// Per tile: the union of the clusters' row maps, its rows in ascending order
-// (their positions are the MMA's N columns), and per cluster a bit mask over
-// those positions, built with ballots (lane = position). Tile indices come
-// from one atomic per CTA (order across CTAs is irrelevant: the tiles
-// partition the probed clusters and their results meet in a max). meta must
-// be zero on entry.
-__global__ void __launch_bounds__(256) k_s2_tiles(const uint32_t *bm, int K, S2Tile *tiles,
-                                                  S2Meta *meta) {
+// One CTA of 256 threads per kS2TileClusters clusters (8 aligned windows of
+// 8): windows with at least window_min probed clusters become window tiles;
+// the probed clusters of the other windows (ascending id) are cut into tiles
+// of kS2Clusters. At most 8 tiles per CTA, one per warp. Per tile: the union
+// of the clusters' row maps, its rows in ascending order (their positions are
+// the MMA's N columns), and per cluster a bit mask over those positions,
+// built with ballots (lane = position). Tile indices come from one atomic per
+// CTA (order across CTAs is irrelevant: the tiles partition the probed
+// clusters and their results meet in a max). meta must be zero on entry.
+__global__ void __launch_bounds__(256) k_s2_tiles(const uint32_t *bm, int K, int window_min,
+                                                  S2Tile *tiles, S2Meta *meta) {
   static_assert(kS2TileClusters == 64 && kS2TileClusters / kS2Clusters == 8, "one tile per warp");
   static_assert(kS2MaskWords == 8, "eight mask words per cluster");
   __shared__ uint32_t s_bm[kS2TileClusters][kS2MaskWords];
-  __shared__ int ids[kS2TileClusters];  // local index of the j-th probed cluster
+  __shared__ int ids[kS2TileClusters];  // local index of the j-th sparse cluster
   __shared__ __align__(16) unsigned char s_rows[8][kS2MaxRows];
-  __shared__ int s_base, s_total, s_nmax;
+  __shared__ int s_base, s_total, s_nmax, s_dense;
+  __shared__ unsigned s_wins;  // bit w: window w is a window tile
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c0 = blockIdx.x * kS2TileClusters;
   for (int i = tid; i < kS2TileClusters * kS2MaskWords; i += 256) {
@@ -109,7 +119,9 @@ __global__ void __launch_bounds__(256) k_s2_tiles(const uint32_t *bm, int K, S2T
   }
   if (tid == 0) s_nmax = 0;
   __syncthreads();
-  if (warp == 0) {  // the 64 clusters' probed flags, compacted in id order by two ballots
+  if (warp == 0) {
+    // the 64 clusters' probed flags; windows with enough of them; the other
+    // windows' probed clusters compacted in id order by two ballots
     bool f[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -119,20 +131,51 @@ __global__ void __launch_bounds__(256) k_s2_tiles(const uint32_t *bm, int K, S2T
       f[h] = any != 0u;
     }
     const unsigned ma = __ballot_sync(0xFFFFFFFFu, f[0]), mb = __ballot_sync(0xFFFFFFFFu, f[1]);
+    const unsigned long long m64 = (unsigned long long)mb << 32 | ma;
+    unsigned wins = 0u;
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+      if (__popcll((m64 >> (8 * w)) & 0xFFull) >= window_min) wins |= 1u << w;
+    unsigned long long keep = 0ull;  // clusters of the other windows
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+      if (!((wins >> w) & 1u)) keep |= 0xFFull << (8 * w);
+    const unsigned sa = ma & (unsigned)keep, sb2 = mb & (unsigned)(keep >> 32);
+    const bool fa = (sa >> lane) & 1u, fb = (sb2 >> lane) & 1u;
     const unsigned below = (1u << lane) - 1u;
-    if (f[0]) ids[__popc(ma & below)] = lane;
-    if (f[1]) ids[__popc(ma) + __popc(mb & below)] = 32 + lane;
-    if (lane == 0) s_total = __popc(ma) + __popc(mb);
+    if (fa) ids[__popc(sa & below)] = lane;
+    if (fb) ids[__popc(sa) + __popc(sb2 & below)] = 32 + lane;
+    if (lane == 0) {
+      s_total = __popc(sa) + __popc(sb2);
+      s_wins = wins;
+      s_dense = __popc(wins);
+    }
   }
   __syncthreads();
-  const int total = s_total;
-  const int n_tiles = (total + kS2Clusters - 1) / kS2Clusters;
+  const int total = s_total, n_dense = s_dense;
+  const unsigned wins = s_wins;
+  const int n_sparse = (total + kS2Clusters - 1) / kS2Clusters;
+  const int n_tiles = n_dense + n_sparse;  // <= 8: see the window rule
   if (tid == 0) s_base = n_tiles ? atomicAdd(&meta->n_tiles, n_tiles) : 0;
   __syncthreads();
   const int t = warp;
   if (t < n_tiles) {
-    const int j0 = t * kS2Clusters, ncl = min(kS2Clusters, total - j0);
-    const int lj = lane < ncl ? ids[j0 + lane] : 0;  // lane j: local index of cluster j
+    // tiles [0, n_dense): the window tiles in window order; then the sparse tiles
+    int win = -1, ncl, lj;
+    if (t < n_dense) {
+      int w = 0;
+      for (int k = 0, seen = 0; k < 8; ++k)
+        if ((wins >> k) & 1u) {
+          if (seen++ == t) w = k;
+        }
+      win = 8 * w;
+      ncl = kS2Clusters;
+      lj = 8 * w + (lane & 7);  // slot j = cluster win + j (probed or not)
+    } else {
+      const int j0 = (t - n_dense) * kS2Clusters;
+      ncl = min(kS2Clusters, total - j0);
+      lj = lane < ncl ? ids[j0 + lane] : 0;  // lane j: local index of cluster j
+    }
     // union word w on lane w, its set bits' positions before it by a scan
     uint32_t word = 0u;
     for (int j = 0; j < ncl; ++j) {
@@ -173,10 +216,21 @@ __global__ void __launch_bounds__(256) k_s2_tiles(const uint32_t *bm, int K, S2T
     const uint32_t *rw = reinterpret_cast<const uint32_t *>(rows);
     for (int k = lane; k < kS2MaxRows / 4; k += 32)
       reinterpret_cast<uint32_t *>(T.rows)[k] = 4 * k < N ? rw[k] : 0u;
-    if (lane < kS2Clusters) T.cl[lane] = lane < ncl ? c0 + lj : -1;
+    if (lane < kS2Clusters) {
+      // a window slot whose cluster is unprobed (or past K) keeps cl = -1
+      bool live = lane < ncl;
+      if (win >= 0) {
+        uint32_t any = 0u;
+#pragma unroll
+        for (int w = 0; w < kS2MaskWords; ++w) any |= s_bm[lj][w];
+        live = any != 0u && c0 + lj < K;
+      }
+      T.cl[lane] = live ? c0 + lj : -1;
+    }
     if (lane == 0) {
       T.n_cl = ncl;
       T.n = N;
+      T.win = win >= 0 ? c0 + win : -1;
       atomicMax(&s_nmax, N);
     }
   }
@@ -208,8 +262,7 @@ struct S2TcArgs {
 
 struct S2TcCtrl {
   __align__(16) S2Tile tile[2];  // the epilogue's copies of its current and previous tile (uint4 stores)
-  uint64_t full_a[kS2MaxStages];
-  uint64_t full_b[kS2MaxStages];
+  uint64_t full[kS2MaxStages];   // TMA bytes + one arrival per loader
   uint64_t empty[kS2MaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
@@ -236,9 +289,11 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
                : "memory");
 }
 
+// tm_w: w_perm in 16-row boxes (one cluster); tm_w8: 128-row boxes (a window).
 template <bool SAMPLE>
 __global__ void __launch_bounds__(kS2Threads, 1)
-    k_s2_tc(const __grid_constant__ CUtensorMap tm_w, S2TcArgs a) {
+    k_s2_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w8,
+            S2TcArgs a) {
   extern __shared__ __align__(1024) unsigned char dsm[];
   const uint32_t raw = smem_u32(dsm);
   unsigned char *ring = dsm + (((raw + 1023u) & ~1023u) - raw);
@@ -246,16 +301,20 @@ __global__ void __launch_bounds__(kS2Threads, 1)
   grid_dep_wait();  // the tile list comes from the kernel before this one
   const int n_tiles = __ldcg(&a.meta->n_tiles);
   const int n_max = max(16, (__ldcg(&a.meta->n_max) + 15) & ~15);
-  const size_t sb = (size_t)kS2ATile + (size_t)n_max * 128;  // multiple of 2048
-  const int stages = (int)min((size_t)kS2MaxStages,
-                              ((size_t)kS2SmemMax - 1024 - sizeof(S2TcCtrl)) / sb);
+  // stage: kps A tiles of 16 KB, then kps B tiles of n_max rows (multiples of 2 KB)
+  const size_t kb_bytes = (size_t)kS2ATile + (size_t)n_max * 128;
+  const size_t room = (size_t)kS2SmemMax - 1024 - sizeof(S2TcCtrl);
+  const int kps = (a.nk % 2 == 0 && room / (2 * kb_bytes) >= kS2MinDeepStages) ? 2 : 1;
+  const size_t sb = kps * kb_bytes;
+  const uint32_t b_off = (uint32_t)(kps * kS2ATile), b_step = (uint32_t)(n_max * 128);
+  const int stages = (int)min((size_t)kS2MaxStages, room / sb);
+  const int n_stages = a.nk / kps;  // stages per tile
   S2TcCtrl &S = *reinterpret_cast<S2TcCtrl *>(ring + (size_t)stages * sb);
   const int G = gridDim.x;
 
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) {
-      mbar_init(&S.full_a[s], 1);
-      mbar_init(&S.full_b[s], kS2Loaders);
+      mbar_init(&S.full[s], 1 + kS2Loaders);
       mbar_init(&S.empty[s], 1);
     }
     for (int j = 0; j < 2; ++j) {
@@ -286,24 +345,44 @@ __global__ void __launch_bounds__(kS2Threads, 1)
       int issued[kS2MaxStages];
       for (int j = 0; j < kS2MaxStages; ++j) issued[j] = -1;
       bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles && ok; t += G) {
+      // descriptor of the tile after the current one, loaded while this one streams
+      int nx_ncl = 0, nx_win = -1, nx_cl[kS2Clusters];
+      auto fetch = [&](int t) {
         const S2Tile &T = a.tiles[t];
-        const int ncl = min(max(__ldcg(&T.n_cl), 0), kS2Clusters);
+        nx_ncl = min(max(__ldcg(&T.n_cl), 0), kS2Clusters);
+        nx_win = __ldcg(&T.win);
+#pragma unroll
+        for (int j = 0; j < kS2Clusters; ++j) nx_cl[j] = __ldcg(&T.cl[j]);
+      };
+      if (blockIdx.x < n_tiles) fetch(blockIdx.x);
+      for (int t = blockIdx.x; t < n_tiles && ok; t += G) {
+        const int ncl = nx_ncl, win = nx_win;
         int cl[kS2Clusters];
 #pragma unroll
-        for (int j = 0; j < kS2Clusters; ++j) cl[j] = __ldcg(&T.cl[j]);
-        for (int kb = 0; kb < a.nk; ++kb) {
+        for (int j = 0; j < kS2Clusters; ++j) cl[j] = nx_cl[j];
+        if (t + G < n_tiles) fetch(t + G);
+        // a window tile is one 128-row box per k-block; otherwise one 16-row
+        // box per probed cluster
+        const uint32_t kb_tx = win >= 0 ? (uint32_t)kS2ATile : (uint32_t)(ncl * 16 * 128);
+        for (int sg = 0; sg < n_stages; ++sg) {
           if (!mbar_wait(&S.empty[s], ph ^ 1u, a.polls)) {
             atomicOr(&S.s_err, kErrCopyTimeout);
             ok = false;
             break;
           }
           unsigned char *st = ring + (size_t)s * sb;
-          mbar_expect_tx(&S.full_a[s], (uint32_t)(ncl * 16 * 128));
+          mbar_expect_tx(&S.full[s], kb_tx * (uint32_t)kps);
+          for (int k = 0; k < kps; ++k) {
+            const int x = (sg * kps + k) * 64;
+            unsigned char *at = st + k * kS2ATile;
+            if (win >= 0) {
+              tma_load_2d(at, &tm_w8, x, win * a.cap, &S.full[s]);
+            } else {
 #pragma unroll
-          for (int j = 0; j < kS2Clusters; ++j)
-            if (j < ncl)
-              tma_load_2d(st + j * 16 * 128, &tm_w, kb * 64, cl[j] * a.cap, &S.full_a[s]);
+              for (int j = 0; j < kS2Clusters; ++j)
+                if (j < ncl) tma_load_2d(at + j * 16 * 128, &tm_w, x, cl[j] * a.cap, &S.full[s]);
+            }
+          }
           issued[s] = (int)ph;
           if (++s == stages) {
             s = 0;
@@ -312,7 +391,7 @@ __global__ void __launch_bounds__(kS2Threads, 1)
         }
       }
       for (int j = 0; j < stages; ++j)
-        if (issued[j] >= 0 && !mbar_wait(&S.full_a[j], (uint32_t)issued[j], a.polls))
+        if (issued[j] >= 0 && !mbar_wait(&S.full[j], (uint32_t)issued[j], a.polls))
           atomicOr(&S.s_err, kErrCopyTimeout);
     }
   } else if (warp == 1) {
@@ -336,8 +415,8 @@ __global__ void __launch_bounds__(kS2Threads, 1)
           tc_fence_after();
         }
         const uint32_t acc = tmem + (uint32_t)(buf * 256);
-        for (int kb = 0; kb < a.nk; ++kb) {
-          if (!mbar_wait(&S.full_a[s], ph, a.polls) || !mbar_wait(&S.full_b[s], ph, a.polls)) {
+        for (int sg = 0; sg < n_stages; ++sg) {
+          if (!mbar_wait(&S.full[s], ph, a.polls)) {
             atomicOr(&S.s_err, kErrCopyTimeout);
             ok = false;
             break;
@@ -347,11 +426,13 @@ __global__ void __launch_bounds__(kS2Threads, 1)
           fence_proxy_async_smem();
           tc_fence_after();
           const uint32_t st = smem_u32(ring + (size_t)s * sb);
-          const uint64_t ad = umma_desc_k(st);
-          const uint64_t bd = umma_desc_k(st + (uint32_t)kS2ATile);
+          for (int k = 0; k < kps; ++k) {
+            const uint64_t ad = umma_desc_k(st + (uint32_t)(k * kS2ATile));
+            const uint64_t bd = umma_desc_k(st + b_off + (uint32_t)k * b_step);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc_mma_f16(acc, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_f16(acc, ad + 2u * kk, bd + 2u * kk, idesc, (sg | k | kk) != 0 ? 1u : 0u);
+          }
           tc_commit(&S.empty[s]);
           if (++s == stages) {
             s = 0;
@@ -365,8 +446,8 @@ __global__ void __launch_bounds__(kS2Threads, 1)
     }
   } else if (warp < 6) {
     // ------------------------------------------------ hidden rows (cp.async)
-    // k-block g of this CTA's sequence uses stage g % stages; each loader's
-    // copies of it arrive on the stage's barrier when they complete, so the
+    // stage g of this CTA's sequence uses ring slot g % stages; each loader's
+    // copies of it arrive on the slot's barrier when they complete, so the
     // loaders never wait for their own copies.
     const int lt = tid - 64;
     const char *hs = reinterpret_cast<const char *>(a.hidden);
@@ -390,19 +471,22 @@ __global__ void __launch_bounds__(kS2Threads, 1)
         src[i] = hs + (size_t)row * rb + c * 16;
         dst_off[i] = (uint32_t)(u * 128 + ((c ^ (u & 7)) << 4)) | (u < n ? 0u : 0x80000000u);
       }
-      for (int kb = 0; kb < a.nk; ++kb) {
+      for (int sg = 0; sg < n_stages; ++sg) {
         if (!mbar_wait(&S.empty[s], ph ^ 1u, a.polls)) {
           atomicOr(&S.s_err, kErrCopyTimeout);
           ok = false;
           break;
         }
-        const uint32_t bst = smem_u32(ring + (size_t)s * sb + kS2ATile);
+        for (int k = 0; k < kps; ++k) {
+          const uint32_t bst = smem_u32(ring + (size_t)s * sb) + b_off + (uint32_t)k * b_step;
+          const size_t x = (size_t)(sg * kps + k) * 128;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (i < per)
-            cp_async16(bst + (dst_off[i] & 0x7FFFFFFFu), src[i] + (size_t)kb * 128,
-                       (dst_off[i] >> 31) ? 0u : 16u);
-        cp_async_arrive_noinc(&S.full_b[s]);
+          for (int i = 0; i < 16; ++i)
+            if (i < per)
+              cp_async16(bst + (dst_off[i] & 0x7FFFFFFFu), src[i] + x,
+                         (dst_off[i] >> 31) ? 0u : 16u);
+        }
+        cp_async_arrive_noinc(&S.full[s]);
         if (++s == stages) {
           s = 0;
           ph ^= 1u;

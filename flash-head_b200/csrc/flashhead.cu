@@ -199,7 +199,8 @@ struct fh_head {
   mutable int tm_w_tile = 0;  // its box height, 0: not encoded yet
   mutable CUtensorMap tm_c[2];  // stage-1 matrices (cluster_w, centroid_w) for k_s1_tc
   mutable bool tm_c_ok[2] = {false, false};
-  mutable CUtensorMap tm_s2;  // w_perm in 16-row boxes for k_s2_tc
+  mutable CUtensorMap tm_s2;   // w_perm in 16-row boxes for k_s2_tc (one cluster)
+  mutable CUtensorMap tm_s2w;  // w_perm in 128-row boxes (a window of 8 clusters)
   mutable bool tm_s2_ok = false;
 };
 
@@ -776,16 +777,21 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
   const int K = d.n_clusters, p = d.n_probes;
   if (!w.s2_bm) return fail(FH_ERR_WORKSPACE, "workspace laid out without the stage-2 index");
   const long long V = (long long)K * d.cluster_size;
-  CUtensorMap tm_w;
+  CUtensorMap tm_w, tm_w8;
   {
     std::lock_guard<std::mutex> lock(h->plan_mutex);
     if (!h->tm_s2_ok) {
-      if (!encode_rows_map(&h->tm_s2, d.w_perm, d.weight_dtype, d.hidden, V, 16))
+      if (!encode_rows_map(&h->tm_s2, d.w_perm, d.weight_dtype, d.hidden, V, 16) ||
+          !encode_rows_map(&h->tm_s2w, d.w_perm, d.weight_dtype, d.hidden, V,
+                           fh::kS2Clusters * 16))
         return fail(FH_ERR_UNSUPPORTED, "w_perm tensor map");
       h->tm_s2_ok = true;
     }
     tm_w = h->tm_s2;
+    tm_w8 = h->tm_s2w;
   }
+  // window tiles need 16-row clusters (8 of them fill the MMA's 128 rows)
+  const int window_min = d.cluster_size == 16 ? fh::kS2WindowMin : fh::kS2Clusters + 1;
   FH_CHECK_LAUNCH(prepare_s2_tc(), "stage-2 kernel attribute");
   const int tile_ctas = (K + fh::kS2TileClusters - 1) / fh::kS2TileClusters;
   for (int r0 = 0; r0 < rows; r0 += fh::kS2MaxRows) {
@@ -796,7 +802,7 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
                            probes + (size_t)r0 * p, n, p, K, probe_base, w.s2_bm),
                     "index fill launch");
     FH_CHECK_LAUNCH(launch(fh::k_s2_tiles, dim3(tile_ctas), dim3(256), 0, s, false,
-                           (const uint32_t *)w.s2_bm, K, w.s2_tiles, w.s2_meta),
+                           (const uint32_t *)w.s2_bm, K, window_min, w.s2_tiles, w.s2_meta),
                     "tile build launch");
     fh::S2TcArgs a;
     memset(&a, 0, sizeof(a));
@@ -818,11 +824,11 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
     a.polls = 1u << 22;
     if (sample)
       FH_CHECK_LAUNCH(launch(fh::k_s2_tc<true>, dim3(sm_count()), dim3(fh::kS2Threads),
-                             (size_t)fh::kS2SmemMax, s, true, tm_w, a),
+                             (size_t)fh::kS2SmemMax, s, true, tm_w, tm_w8, a),
                       "stage-2 tensor-core launch");
     else
       FH_CHECK_LAUNCH(launch(fh::k_s2_tc<false>, dim3(sm_count()), dim3(fh::kS2Threads),
-                             (size_t)fh::kS2SmemMax, s, true, tm_w, a),
+                             (size_t)fh::kS2SmemMax, s, true, tm_w, tm_w8, a),
                       "stage-2 tensor-core launch");
   }
   if (d.n_special > 0) {
