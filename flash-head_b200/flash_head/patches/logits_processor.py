@@ -80,6 +80,58 @@ def step_candidate_logprobs(token_ids: torch.Tensor, num_logprobs: int):
     return fh.candidate_logprobs(_last_hidden, token_ids, num_logprobs)
 
 
+# below this temperature a request is greedy (vLLM's sampler uses the same bound)
+_SAMPLING_EPS = 1e-5
+_warned = set()
+
+
+def _warn_once(key, msg):
+    if key not in _warned:
+        _warned.add(key)
+        logger.warning(msg)
+
+
+def _row_seed(rows, generators):
+    """A Philox seed for a group of rows: drawn from the first seeded row's
+    generator (so seeded requests repeat), else from torch's default one."""
+    for r in rows:
+        g = generators.get(int(r)) if generators else None
+        if g is not None:
+            return int(torch.randint(0, 2**62, (1,), generator=g, device=g.device).item())
+    return int(torch.randint(0, 2**62, (1,)).item())
+
+
+def step_sampled_ids(greedy_ids: torch.Tensor, sampling_metadata):
+    """The last FlashHead step's ids with each non-greedy request sampled at its
+    own temperature (FlashHead.get_next_token_batched(do_sample=True), one call
+    per distinct temperature); greedy rows keep greedy_ids. Where the reference
+    hook decodes every request greedily (patches/logits_processor.py:38), this
+    routes vLLM's per-request temperature to the sampling kernels. top-k / top-p
+    / min-p are not applied on this path (a warning says so once)."""
+    md = sampling_metadata
+    if md is None or getattr(md, "all_greedy", True) or getattr(md, "temperature", None) is None:
+        return greedy_ids
+    fh = _flash_head
+    h = _last_hidden
+    n = greedy_ids.numel()
+    if fh is _FLASH_HEAD_NOT_LOADED or fh is None or h is None or h.shape[0] != n:
+        return greedy_ids
+    if getattr(md, "top_k", None) is not None or getattr(md, "top_p", None) is not None:
+        _warn_once("topkp", "[FlashHead] top-k / top-p are not applied on the FlashHead "
+                            "path: requests sample from the candidate set at their temperature")
+    temps = md.temperature.detach().float().view(-1)[:n].cpu()
+    out = greedy_ids.clone()
+    random_rows = torch.nonzero(temps >= _SAMPLING_EPS).view(-1)
+    for t in torch.unique(temps[random_rows]).tolist():
+        rows = random_rows[temps[random_rows] == t]
+        idx = rows.to(h.device)
+        ids = fh.get_next_token_batched(h.index_select(0, idx), do_sample=True, temperature=float(t),
+                                        seed=_row_seed(rows.tolist(), getattr(md, "generators", None)),
+                                        offset=0)
+        out.view(-1).index_copy_(0, idx.to(out.device), ids.to(out.dtype).view(-1))
+    return out
+
+
 def patch_logits_processor():
     from vllm.model_executor.layers.logits_processor import LogitsProcessor
 

@@ -1,6 +1,9 @@
 """Hook vLLM's Sampler to pass FlashHead token ids through (reference
 patches/sampler.py:16-29): 1-D or [N, 1] input is treated as sampled ids and
-returned as ``SamplerOutput(sampled_token_ids=[N, 1] int32, ...)``.
+returned as ``SamplerOutput(sampled_token_ids=[N, 1] int32, ...)``. Requests
+with a temperature are sampled by FlashHead's sampling kernels at that
+temperature (``logits_processor.step_sampled_ids``) instead of decoded
+greedily.
 
 Where the reference always returns ``logprobs_tensors=None``, requests that
 ask for k logprobs get them over the step's candidate set
@@ -50,7 +53,8 @@ def patch_sampler():
     def _patched_forward(self, logits, sampling_metadata, predict_bonus_token=False,
                          logprobs_mode_override=None):
         if logits.ndim == 1 or (logits.ndim == 2 and logits.shape[-1] == 1):
-            sampled = logits.view(-1).to(torch.int32)
+            from flash_head.patches.logits_processor import step_sampled_ids
+            sampled = step_sampled_ids(logits.view(-1).to(torch.int32), sampling_metadata)
             lp = flash_head_logprobs(sampled.to(torch.int64), sampling_metadata)
             return SamplerOutput(sampled_token_ids=sampled.unsqueeze(-1), logprobs_tensors=lp)
         return _original_forward(self, logits, sampling_metadata,

@@ -21,7 +21,9 @@ Checked:
   * with FLASHHEAD_MAX_DECODE_ROWS=4, three concurrent requests decode
     through FlashHead's batched step with the same per-token check;
   * a request for logprobs gets FlashHead's candidate-set logprobs, with the
-    sampled token's among them.
+    sampled token's among them;
+  * a request with a temperature and a seed is sampled by FlashHead's
+    sampling kernels, reproducibly.
 """
 
 from __future__ import annotations
@@ -89,6 +91,7 @@ _DRIVER = r"""
 import json, os, sys
 from vllm import LLM, SamplingParams
 model, prompts, max_tokens, logprobs = sys.argv[1], json.loads(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4])
+temperature, seed = float(sys.argv[5]), int(sys.argv[6])
 llm = LLM(model=model, skip_tokenizer_init=True, enforce_eager=True, dtype="bfloat16",
           gpu_memory_utilization=0.25, max_model_len=256, max_num_seqs=8, seed=0)
 from flash_head.patches import logits_processor as lp
@@ -99,23 +102,31 @@ def counted(h):
     steps.append((int(h.shape[0]), ids is not None))
     return ids
 lp.flash_head_token_ids = counted
-sp = SamplingParams(max_tokens=max_tokens, temperature=0.0, logprobs=logprobs or None,
-                    ignore_eos=True, detokenize=False)
+sampled = []
+inner_s = lp.step_sampled_ids
+def counted_s(ids, md):
+    out = inner_s(ids, md)
+    sampled.append(int(md is not None and not md.all_greedy))
+    return out
+lp.step_sampled_ids = counted_s
+sp = SamplingParams(max_tokens=max_tokens, temperature=temperature, logprobs=logprobs or None,
+                    ignore_eos=True, detokenize=False, seed=seed if seed >= 0 else None)
 outs = llm.generate([{"prompt_token_ids": p} for p in prompts], sp)
-res = {"tokens": [list(o.outputs[0].token_ids) for o in outs], "steps": steps,
+res = {"tokens": [list(o.outputs[0].token_ids) for o in outs], "steps": steps, "sampled": sampled,
        "logprobs": [[{str(k): float(v.logprob) for k, v in pos.items()} for pos in (o.outputs[0].logprobs or [])]
                     for o in outs]}
 print("RESULT " + json.dumps(res), flush=True)
 """
 
 
-def _run_vllm(model_dir, site, prompts, max_tokens, logprobs=0, max_rows=1):
+def _run_vllm(model_dir, site, prompts, max_tokens, logprobs=0, max_rows=1, temperature=0.0,
+              seed=-1):
     env = dict(os.environ)
     env.update(PYTHONPATH=os.pathsep.join([site, PKG, REPO, env.get("PYTHONPATH", "")]),
                VLLM_ENABLE_V1_MULTIPROCESSING="0",
                FLASHHEAD_MAX_DECODE_ROWS=str(max_rows), TOKENIZERS_PARALLELISM="false")
     res = subprocess.run([sys.executable, "-c", _DRIVER, model_dir, json.dumps(prompts),
-                          str(max_tokens), str(logprobs)],
+                          str(max_tokens), str(logprobs), str(temperature), str(seed)],
                          capture_output=True, text=True, timeout=900, env=env, cwd=model_dir)
     line = [ln for ln in res.stdout.splitlines() if ln.startswith("RESULT ")]
     assert res.returncode == 0 and line, (res.stdout[-3000:], res.stderr[-6000:])
@@ -194,3 +205,19 @@ def test_vllm_batched_decode_and_logprobs(served):
             vals = {int(k): v for k, v in pos.items()}
             assert t in vals and all(np.isfinite(v) and v <= 1e-6 for v in vals.values())
             assert vals[t] >= max(vals.values()) - 1e-3  # greedy: the top candidate
+
+
+def test_vllm_temperature_is_sampled_by_flashhead(served):
+    """A request with a temperature and a seed is sampled by FlashHead's
+    sampling kernels (not decoded greedily), and the seed repeats it."""
+    model_dir, site, oracle = served
+    prompts = [[1, 17, 305, 2201, 44]]
+    runs = [_run_vllm(model_dir, site, prompts, max_tokens=16, temperature=1.5, seed=7)
+            for _ in range(2)]
+    for out in runs:
+        assert len(out["tokens"][0]) == 16 and all(0 <= t < V for t in out["tokens"][0])
+        assert out["sampled"] and all(out["sampled"]), out["sampled"]
+        assert all(used for rows, used in out["steps"] if rows == 1)
+    assert runs[0]["tokens"] == runs[1]["tokens"]
+    greedy = _run_vllm(model_dir, site, prompts, max_tokens=16)
+    assert not any(greedy["sampled"])

@@ -265,6 +265,25 @@ if after != before:
     for bad in (SimpleNamespace(max_num_logprobs=-1, logprob_token_ids=None),
                 SimpleNamespace(max_num_logprobs=2, logprob_token_ids={{0: [3]}})):
         print("UNSUPPORTED", Sampler.forward(Sampler.__new__(Sampler), ids, bad).logprobs_tensors)
+    # per-request temperature: greedy rows keep the greedy ids, the others are
+    # sampled once per distinct temperature, seeded from a request's generator
+    calls = []
+    class FakeHeadSample(FakeHead):
+        def get_next_token_batched(self, h, do_sample=False, temperature=1.0, seed=0, offset=0):
+            if not do_sample:
+                return super().get_next_token_batched(h)
+            calls.append((h.shape[0], round(temperature, 3), seed))
+            return torch.full((h.shape[0],), int(round(temperature * 100)), dtype=torch.int64)
+    lp._flash_head = FakeHeadSample()
+    lp.max_decode_rows = lambda: 4
+    ids = proc.forward(None, torch.zeros(4, 8))
+    md = SimpleNamespace(max_num_logprobs=None, logprob_token_ids=None, all_greedy=False,
+                         temperature=torch.tensor([0.0, 0.7, 0.7, 1.3]), top_k=None, top_p=None,
+                         generators={{2: torch.Generator().manual_seed(3)}})
+    out = Sampler.forward(Sampler.__new__(Sampler), ids, md)
+    want_seed = int(torch.randint(0, 2**62, (1,), generator=torch.Generator().manual_seed(3)).item())
+    print("TEMPERATURE", out.sampled_token_ids.view(-1).tolist(), [c[:2] for c in calls],
+          calls[0][2] == want_seed)
 """
 
 
@@ -293,5 +312,6 @@ def test_register_and_hooks(enabled):
         # drafts [5, 6] vs targets [5, 6] -> bonus 30; [7] vs [8] -> 8; no drafts -> bonus 32
         assert "SPEC [[5, 6, 30], [8, -1, -1], [32, -1, -1]]" in res.stdout
         assert "DRAFT [11, 12] [3]" in res.stdout
+        assert "TEMPERATURE [5, 70, 70, 130] [(2, 0.7), (1, 1.3)] True" in res.stdout
     else:
         assert status.startswith("UNPATCHED")
