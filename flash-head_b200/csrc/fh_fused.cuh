@@ -654,7 +654,8 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
   FH_TICK_DECL
   if (!producer) {
     // Compute warps: each chunk (a tile, or a d-range of one) into its own
-    // partial buffer; slots are refilled once per round of n_slots chunks.
+    // partial buffer; a slot is refilled as soon as its chunk is consumed, so
+    // the copies never drain between rounds.
     const int hrow = (gq >> 1) < R ? (gq >> 1) : 0;  // hidden row feeding column gq
     const M1 *hrow1 = hB1 + (size_t)hrow * a.D;
     for (int c = 0; c < n1; ++c) {
@@ -690,14 +691,14 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
         pc[((gq + 8) * R + tq) * kFWarps + warp] = acc0[2 + odd] + acc1[2 + odd];
       }
       FH_TICK(2);
-      if (s == g1.n_slots - 1 && c + 1 < n1) nbar_arrive(kBarSlot0, kFBlock);  // round done
+      if (c + g1.n_slots < n1) nbar_arrive(kBarSlot0 + s, kFBlock);  // slot s free
     }
   } else {
-    // Producer warp: refill the slots after each round of n_slots chunks.
-    for (int c0r = g1.n_slots; c0r < n1; c0r += g1.n_slots) {
-      nbar_sync(kBarSlot0, kFBlock);
-      if (lane == 0)
-        for (int c = c0r; c < min(c0r + g1.n_slots, n1); ++c) issue1(c);
+    // Producer warp: chunk c goes into slot c % n_slots once the chunk before
+    // it in that slot has been consumed.
+    for (int c = g1.n_slots; c < n1; ++c) {
+      nbar_sync(kBarSlot0 + c % g1.n_slots, kFBlock);
+      if (lane == 0) issue1(c);
       __syncwarp();
     }
     // Zero this CTA's share of the histograms the next call will use (32-bit
