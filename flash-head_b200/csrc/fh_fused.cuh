@@ -59,11 +59,12 @@ constexpr float kPrefetchMargin = -1.0f;
 // Bulk copies per stage-2 cluster: four copies of 4 rows complete sooner than
 // one of 16 (measured ~0.4 us per step at batch 1).
 constexpr int kS2Pieces = 4;
-// Bulk copies per stage-1 tile (16 rows): four copies of 4 rows keep more
-// requests in flight than one of 16 rows, and fewer pay less issue cost than
-// one per row (measured: 4 pieces ~0.7 us per step faster than 1, 8 and 16
-// slower than 4).
-constexpr int kS1Pieces = 4;
+// Bytes per stage-1 bulk copy (whole rows, at least one): pieces of about
+// 8 KB keep more requests in flight than one copy per 16-row tile and pay
+// less issue cost than one per row (measured at batch 1: 8 KB pieces beat
+// 16 KB and 4 KB ones by ~0.7 us per step for 4 KB bf16 rows, and beat 4 KB
+// and 16 KB ones for 2 KB fp8 rows).
+constexpr int kS1PieceBytes = 8192;
 constexpr int kRingBytes = 128 * 1024;
 constexpr int kMaxSlots = 4;
 constexpr int kTileRows = 16;
@@ -586,7 +587,7 @@ __global__ void __launch_bounds__(kFBlock, 1) k_fused_step(FusedArgs a) {
     unsigned char *dst = ring + (size_t)s * g1.slot_bytes;
     const char *src = wsrc + (size_t)tile * kTileRows * rb1 + (size_t)dc * g1.cb;
     if (g1.ndc == 1) {
-      const int per = (tr + kS1Pieces - 1) / kS1Pieces;
+      const int per = max(1, kS1PieceBytes / rb1);  // rows per copy
       for (int r0 = 0; r0 < tr; r0 += per)
         bulk_g2s(dst + (size_t)r0 * rb1, src + (size_t)r0 * rb1,
                  (uint32_t)(min(per, tr - r0) * rb1), &S.mbar[s]);
