@@ -71,6 +71,7 @@ struct HSelArgs {
   int out_stride;
   int32_t *probes;       // [rows, p] local cluster ids ascending, or null
   long long *cand_out;   // [rows, p] signed packed (key, global id) words, or null
+  uint32_t *bm;          // [K][8] row bit maps of the stage-2 index (rows <= 256), or null
 };
 
 template <int NT>
@@ -243,6 +244,8 @@ __global__ void __launch_bounds__(NT, 1024 / NT) k_select_hist(HSelArgs a) {
         if (pos < p) {
           if (out) out[pos] = k;
           if (cand) cand[pos] = to_signed(pack(sc[k], (uint32_t)(a.cluster_base + k)));
+          // the stage-2 index directly (8 words of row bits per cluster)
+          if (a.bm) atomicOr(&a.bm[(size_t)k * 8 + (r >> 5)], 1u << (r & 31));
         }
       },
       S.warp_counts);

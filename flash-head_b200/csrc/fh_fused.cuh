@@ -80,6 +80,7 @@ constexpr int kSyncArrive = 1;
 constexpr int kSyncDone = 2;
 constexpr int kSyncError = 3;
 constexpr int kSyncEpoch = 4;
+constexpr int kSyncS2Done = 5;  // CTAs of a batched stage-2 launch that finished
 
 constexpr int kHistCoarse = 256;
 constexpr int kHistWords = kHistCoarse + 65536;

@@ -38,7 +38,8 @@
 //                are double-buffered, so the epilogue of tile i overlaps the
 //                MMAs of tile i + 1.
 // The ring's depth follows the largest union of the step (read from the tile
-// builder's meta words), so typical steps keep many stages in flight. Every
+// builder's meta words), so typical steps keep many stages in flight. The
+// last CTA to finish publishes the launch's ids and resets packed[]. Every
 // wait is bounded; on a timeout the kernel records kErrCopyTimeout, drains its
 // own copies and MMAs (bounded) and frees TMEM before it returns.
 #pragma once
@@ -258,6 +259,9 @@ struct S2TcArgs {
   unsigned long long *packed;  // [rows] (this launch's rows)
   uint32_t *err;
   uint32_t polls;
+  uint32_t *done;          // CTAs finished (zero on entry; the last CTA resets it)
+  int64_t *out_ids;        // [rows] ids, or null
+  long long *out_signed;   // [rows] a shard's signed packed words, or null
 };
 
 struct S2TcCtrl {
@@ -269,6 +273,7 @@ struct S2TcCtrl {
   uint64_t drain;
   uint32_t tmem_base;
   uint32_t s_err;
+  int s_last;
 };
 static_assert(offsetof(S2TcCtrl, tile) % 16 == 0 && sizeof(S2Tile) % 16 == 0,
               "tile copies are 16-byte stores");
@@ -575,6 +580,23 @@ __global__ void __launch_bounds__(kS2Threads, 1)
                  : "memory");
   }
   if (tid == 0 && S.s_err) atomicOr(a.err, S.s_err);
+  // Publish: the last CTA to finish turns packed[] into ids (or a shard's
+  // signed words) and resets it and the counter for the next launch.
+  if (tid == 0) {
+    __threadfence();
+    S.s_last = atomicAdd(a.done, 1u) == (uint32_t)G - 1u;
+  }
+  __syncthreads();
+  if (S.s_last) {
+    __threadfence();
+    for (int i = tid; i < a.rows; i += kS2Threads) {
+      const unsigned long long w = __ldcg(&a.packed[i]);
+      if (a.out_signed) a.out_signed[i] = to_signed(w);
+      else if (a.out_ids) a.out_ids[i] = w ? (int64_t)packed_id(w) : (int64_t)0xFFFFFFFFll;
+      a.packed[i] = 0ull;
+    }
+    if (tid == 0) *a.done = 0u;
+  }
 }
 
 }  // namespace fh

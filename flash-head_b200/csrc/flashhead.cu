@@ -25,6 +25,8 @@
 #include "fh_stage2_tc.cuh"
 #include "fh_spec.cuh"
 
+static_assert(fh::kS2MaskWords == 8, "the selection kernel writes 8 bit-map words per cluster");
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -649,7 +651,8 @@ cudaError_t prepare_s1_tc() {
 // the signed candidate words (global ids) into cand_out.
 int run_s1_tc(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
               uint64_t seed, uint64_t offset, const Workspace &w, float *scores_out,
-              int out_stride, int32_t *probes, long long *cand_out, cudaStream_t s) {
+              int out_stride, int32_t *probes, long long *cand_out, cudaStream_t s,
+              uint32_t *s2_bm = nullptr) {
   const fh_head_desc &d = h->d;
   const int which = sample ? 1 : 0;
   const int cdt = sample ? d.sample_dtype : d.score_dtype;
@@ -731,6 +734,7 @@ int run_s1_tc(const fh_head *h, const void *hidden, int rows, bool sample, float
   se.out_stride = out_stride;
   se.probes = probes;
   se.cand_out = cand_out;
+  se.bm = rows <= fh::kS2MaxRows ? s2_bm : nullptr;
   // more rows than SMs: two 512-thread CTAs per SM, so one wave selects every row
   if (rows > sm_count())
     FH_CHECK_LAUNCH(launch(fh::k_select_hist<512>, dim3(rows), dim3(512),
@@ -771,7 +775,8 @@ cudaError_t prepare_s2_tc() {
 // zero again on return.
 int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
                    uint64_t seed, uint64_t offset, const Workspace &w, const int32_t *probes,
-                   int probe_base, int64_t *out_ids, long long *out_signed, cudaStream_t s) {
+                   int probe_base, int64_t *out_ids, long long *out_signed, cudaStream_t s,
+                   bool index_ready = false) {
   const fh_head_desc &d = h->d;
   const fh::RngKey rng = rng_key(seed, offset);
   const int K = d.n_clusters, p = d.n_probes;
@@ -793,14 +798,35 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
   // window tiles need 16-row clusters (8 of them fill the MMA's 128 rows)
   const int window_min = d.cluster_size == 16 ? fh::kS2WindowMin : fh::kS2Clusters + 1;
   FH_CHECK_LAUNCH(prepare_s2_tc(), "stage-2 kernel attribute");
+  // special tokens first: their words meet the probed ones in packed[], which
+  // each stage-2 launch's last CTA publishes
+  if (d.n_special > 0) {
+    const long long warps = (long long)rows * d.n_special;
+    const int n_slots = K * d.cluster_size;
+    if (d.weight_dtype == FH_BF16)
+      FH_CHECK_LAUNCH(launch(fh::k_special_scores<__nv_bfloat16>, dim3(grid_for(warps * 32, 256)),
+                             dim3(256), 0, s, false, hidden, rows, d.hidden, d.w_perm, d.vocab_map,
+                             d.special_slots, d.n_special, n_slots, sample ? 1 : 0, temperature,
+                             rng, w.packed),
+                      "special-token launch");
+    else
+      FH_CHECK_LAUNCH(launch(fh::k_special_scores<__half>, dim3(grid_for(warps * 32, 256)),
+                             dim3(256), 0, s, false, hidden, rows, d.hidden, d.w_perm, d.vocab_map,
+                             d.special_slots, d.n_special, n_slots, sample ? 1 : 0, temperature,
+                             rng, w.packed),
+                      "special-token launch");
+  }
   const int tile_ctas = (K + fh::kS2TileClusters - 1) / fh::kS2TileClusters;
   for (int r0 = 0; r0 < rows; r0 += fh::kS2MaxRows) {
     const int n = std::min(fh::kS2MaxRows, rows - r0);
-    FH_CHECK_LAUNCH(cudaMemsetAsync(w.s2_bm, 0, w.s2_zero_bytes, s), "index reset");
-    const long long pairs = (long long)n * p;
-    FH_CHECK_LAUNCH(launch(fh::k_s2_fill, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
-                           probes + (size_t)r0 * p, n, p, K, probe_base, w.s2_bm),
-                    "index fill launch");
+    // the selection may have filled the index of a single chunk already
+    if (!(index_ready && rows <= fh::kS2MaxRows)) {
+      FH_CHECK_LAUNCH(cudaMemsetAsync(w.s2_bm, 0, w.s2_zero_bytes, s), "index reset");
+      const long long pairs = (long long)n * p;
+      FH_CHECK_LAUNCH(launch(fh::k_s2_fill, dim3(grid_for(pairs, 256)), dim3(256), 0, s, false,
+                             probes + (size_t)r0 * p, n, p, K, probe_base, w.s2_bm),
+                      "index fill launch");
+    }
     FH_CHECK_LAUNCH(launch(fh::k_s2_tiles, dim3(tile_ctas), dim3(256), 0, s, false,
                            (const uint32_t *)w.s2_bm, K, window_min, w.s2_tiles, w.s2_meta),
                     "tile build launch");
@@ -822,6 +848,9 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
     a.packed = w.packed + r0;
     a.err = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncError;
     a.polls = 1u << 22;
+    a.done = reinterpret_cast<uint32_t *>(w.counter) + fh::kSyncS2Done;
+    a.out_ids = out_ids ? out_ids + r0 : nullptr;
+    a.out_signed = out_signed ? out_signed + r0 : nullptr;
     if (sample)
       FH_CHECK_LAUNCH(launch(fh::k_s2_tc<true>, dim3(sm_count()), dim3(fh::kS2Threads),
                              (size_t)fh::kS2SmemMax, s, true, tm_w, tm_w8, a),
@@ -831,25 +860,6 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
                              (size_t)fh::kS2SmemMax, s, true, tm_w, tm_w8, a),
                       "stage-2 tensor-core launch");
   }
-  if (d.n_special > 0) {
-    const long long warps = (long long)rows * d.n_special;
-    const int n_slots = K * d.cluster_size;
-    if (d.weight_dtype == FH_BF16)
-      FH_CHECK_LAUNCH(launch(fh::k_special_scores<__nv_bfloat16>, dim3(grid_for(warps * 32, 256)),
-                             dim3(256), 0, s, false, hidden, rows, d.hidden, d.w_perm, d.vocab_map,
-                             d.special_slots, d.n_special, n_slots, sample ? 1 : 0, temperature,
-                             rng, w.packed),
-                      "special-token launch");
-    else
-      FH_CHECK_LAUNCH(launch(fh::k_special_scores<__half>, dim3(grid_for(warps * 32, 256)),
-                             dim3(256), 0, s, false, hidden, rows, d.hidden, d.w_perm, d.vocab_map,
-                             d.special_slots, d.n_special, n_slots, sample ? 1 : 0, temperature,
-                             rng, w.packed),
-                      "special-token launch");
-  }
-  FH_CHECK_LAUNCH(launch(fh::k_inv_finalize, dim3(grid_for(rows, 256)), dim3(256), 0, s, false,
-                         w.packed, rows, out_ids, out_signed),
-                  "finalize launch");
   return FH_OK;
 }
 
@@ -858,11 +868,15 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
 int run_batched(const fh_head *h, const void *hidden, int rows, bool sample, float temperature,
                 uint64_t seed, uint64_t offset, int64_t *out_ids, const Workspace &w,
                 cudaStream_t s) {
+  // up to 256 rows the selection writes the stage-2 index itself (cleared first)
+  const bool index_in_select = rows <= fh::kS2MaxRows && w.s2_bm;
+  if (index_in_select)
+    FH_CHECK_LAUNCH(cudaMemsetAsync(w.s2_bm, 0, w.s2_zero_bytes, s), "index reset");
   const int st = run_s1_tc(h, hidden, rows, sample, temperature, seed, offset, w, nullptr, 0,
-                           w.probes, nullptr, s);
+                           w.probes, nullptr, s, index_in_select ? w.s2_bm : nullptr);
   if (st != FH_OK) return st;
   return run_inv_stage2(h, hidden, rows, sample, temperature, seed, offset, w, w.probes, 0,
-                        out_ids, nullptr, s);
+                        out_ids, nullptr, s, index_in_select);
 }
 
 // Tiling of the dense tensor-core kernel: vocab tiles of n_tile slots (a
@@ -1065,10 +1079,10 @@ FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample) {
   const int s1 = (cdt == FH_FP8_E4M3 && d.weight_dtype == FH_BF16 ? 1 : 0) +
                  (rows + fh::kS1MaxN - 1) / fh::kS1MaxN + 1;
   if (batched_ok(head, rows, sample)) {
-    // stage 1; per 256 rows: index reset (memset), index fill, tiles, stage 2;
-    // [specials], finalize
+    // stage 1 (whose selection fills the stage-2 index up to 256 rows);
+    // [specials]; per 256 rows: [index fill], tiles, stage 2 (publishing)
     const int chunks = (rows + fh::kS2MaxRows - 1) / fh::kS2MaxRows;
-    return s1 + 4 * chunks + (d.n_special > 0 ? 1 : 0) + 1;
+    return s1 + (d.n_special > 0 ? 1 : 0) + (chunks > 1 ? 3 : 2) * chunks;
   }
   if (fused_ok(d, rows, sample, sm_count())) return 1;
   // stage 1 + stage 2; or scores, select, stage 2
