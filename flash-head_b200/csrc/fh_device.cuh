@@ -283,8 +283,15 @@ __device__ __forceinline__ void block_ordered_compact(int N, Pred pred, Emit emi
   __syncthreads();  // warp_counts may still be read by a previous use
   if (lane == 0) warp_counts[warp] = cnt;
   __syncthreads();
-  int off = 0;
-  for (int w = 0; w < warp; ++w) off += warp_counts[w];
+  // this warp's first position: exclusive prefix of the warp counts (one scan)
+  const int wc = lane < nw ? warp_counts[lane] : 0;
+  int incl = wc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  int off = __shfl_sync(0xFFFFFFFFu, incl - wc, warp);
   for (int base = lo; base < hi; base += 32) {
     const int i = base + lane;
     const bool f = i < hi && pred(i);

@@ -114,6 +114,8 @@ __global__ void __launch_bounds__(256) k_s2_tiles(const uint32_t *bm, int K, int
   __shared__ unsigned s_wins;  // bit w: window w is a window tile
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c0 = blockIdx.x * kS2TileClusters;
+  grid_dep_wait();    // the bit maps come from the kernel before this one
+  grid_dep_launch();  // stage 2 may set up while the tiles are built (it waits for them)
   for (int i = tid; i < kS2TileClusters * kS2MaskWords; i += 256) {
     const int c = c0 + i / kS2MaskWords;
     (&s_bm[0][0])[i] = c < K ? __ldcg(&bm[(size_t)c0 * kS2MaskWords + i]) : 0u;

@@ -827,7 +827,7 @@ int run_inv_stage2(const fh_head *h, const void *hidden, int rows, bool sample, 
                              probes + (size_t)r0 * p, n, p, K, probe_base, w.s2_bm),
                       "index fill launch");
     }
-    FH_CHECK_LAUNCH(launch(fh::k_s2_tiles, dim3(tile_ctas), dim3(256), 0, s, false,
+    FH_CHECK_LAUNCH(launch(fh::k_s2_tiles, dim3(tile_ctas), dim3(256), 0, s, true,
                            (const uint32_t *)w.s2_bm, K, window_min, w.s2_tiles, w.s2_meta),
                     "tile build launch");
     fh::S2TcArgs a;
