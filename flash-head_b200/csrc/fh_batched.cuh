@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(NT, 1024 / NT) k_select_hist(HSelArgs a) {
   for (int i = tid; i < kWarps * 256; i += NT) wh[i] = 0u;
   if (tid < 256) S.hist[tid] = 0u;
   if (tid == 0) S.n_bkt = 0;
+  __syncthreads();  // the warp histograms are zero before the keys are counted
   grid_dep_wait();  // the partials come from the stage-1 kernel before this one
   grid_dep_launch();
   // The row's partials as float4 groups (rows are padded to 64 floats and
@@ -140,12 +141,11 @@ __global__ void __launch_bounds__(NT, 1024 / NT) k_select_hist(HSelArgs a) {
               gumbel(a.rng, kStageClusters, (uint32_t)r, (uint32_t)(a.cluster_base + k));
         if (a.scores_out) a.scores_out[(size_t)r * a.out_stride + k] = v;
         sc[k] = sanitize(v);
+        // level 1: coarse bins (key >> 24), one private histogram per warp
+        atomicAdd(&wh[warp * 256 + (mono(sc[k]) >> 24)], 1u);
       }
     }
   }
-  __syncthreads();
-  // level 1: coarse bins (key >> 24), one private histogram per warp
-  for (int k = tid; k < K; k += NT) atomicAdd(&wh[warp * 256 + (mono(sc[k]) >> 24)], 1u);
   __syncthreads();
   if (tid < 256) {
     uint32_t t = 0;

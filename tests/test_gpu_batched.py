@@ -93,6 +93,29 @@ def test_batched_special_tokens():
     assert toks[7] == 4095
 
 
+def test_batched_rows_beyond_one_stage2_launch():
+    """300 rows: stage 2 runs as launches of 256 and 44 rows (the index filled
+    by its own kernel, each launch publishing its rows), special tokens scored
+    once for all rows; a second call on the same workspace repeats the ids."""
+    from flash_head.synthetic import make_hidden
+    head = _tiny_head(256, 16, 512, seed=5)
+    fh = build_head(head.weight, head.centroids, head.assignments, 12, specials=[0, 17, 4095],
+                    stage1="model")
+    nh = fh.native()
+    ov = OracleView(fh)
+    H = make_hidden(300, 512, seed=43, device="cuda")
+    H[290] = torch.from_numpy(ov.W[4095] * 50).to("cuda", torch.bfloat16)
+    Hn = to_np_f32(H)
+    probes = nh.top_clusters(H).cpu().numpy()
+    toks = nh.next_token(H).cpu().numpy()
+    for r in range(H.shape[0]):
+        want = ov.greedy_given_probes(Hn[r], probes[r])
+        assert O.token_within_tolerance(toks[r], want, lambda v: ov.logit(Hn[r], v), 1e-5), r
+    assert toks[290] == 4095
+    assert np.array_equal(nh.next_token(H).cpu().numpy(), toks)
+    assert nh.workspace_error() == 0
+
+
 @pytest.mark.parametrize("stage1", ["model", "fp8"])
 def test_batched_sampling_matches_oracle_draw_for_draw(stage1):
     from flash_head.synthetic import make_hidden
