@@ -139,10 +139,12 @@ FH_API size_t fh_workspace_error_offset(void);
  * applies (rows <= 4 and supported shapes); from 5 rows stage 1 runs on the
  * tensor cores ([an f16 copy of bf16 rows for an fp8 stage-1 matrix], one
  * stage-1 kernel per 256 rows, the selection), followed for 5..15 rows by
- * the block-sparse stage 2 and for 16+ rows, per 256 rows, by the
- * cluster-major tensor-core stage 2 (an index reset memset, the index, the
- * tiles, the stage-2 kernel), then [the special tokens] and the id publish;
- * 3 for the CUDA-core stage kernels (unsupported shapes).
+ * the block-sparse stage 2 and for 16+ rows by [the special tokens] and,
+ * per 256 rows, the cluster-major tensor-core stage 2 (up to 256 rows the
+ * selection fills its index, above that an index kernel per 256 rows; the
+ * tile builder; the stage-2 kernel, whose last CTA publishes the ids);
+ * 3 for the CUDA-core stage kernels (unsupported shapes). Memsets are not
+ * counted.
  */
 FH_API int fh_step_kernel_count(const fh_head *head, int rows, int do_sample);
 
