@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cmath>
@@ -1151,6 +1152,10 @@ FH_API size_t fh_workspace_bytes_host(const fh_head *head, int rows) {
   return round_up(layout(head->d, rows, nullptr, 0).bytes, 256) + host_staging_bytes(head, rows);
 }
 
+// Longest host spin on the ids of a host-buffer call before falling back to a
+// stream synchronisation.
+static constexpr int kHostSpinMs = 20;
+
 FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, int rows,
                                   int64_t *out_ids_host, void *workspace, size_t workspace_bytes,
                                   fh_stream_t stream) {
@@ -1179,6 +1184,12 @@ FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, 
   const void *h_mapped = mapped_host(hidden_host);
   if (!(h_mapped && aligned16(h_mapped) && hbytes % 16 == 0)) h_mapped = nullptr;
   int64_t *o_mapped = reinterpret_cast<int64_t *>(mapped_host(out_ids_host));
+  // Ids written over the bus land in the host buffer before the kernel has
+  // finished: mark every row (-1 is never an id) and return once all rows
+  // are overwritten, instead of waiting for the stream to drain.
+  volatile int64_t *watch = o_mapped ? reinterpret_cast<volatile int64_t *>(out_ids_host) : nullptr;
+  if (watch)
+    for (int r = 0; r < rows; ++r) watch[r] = -1;
   if (h_mapped) {
     const int n16 = (int)(hbytes / 16);
     FH_CHECK_LAUNCH(launch(fh::k_stage_in, dim3(grid_for(n16, 256)), dim3(256), 0, s, false,
@@ -1196,6 +1207,23 @@ FH_API int fh_get_next_token_host(const fh_head *head, const void *hidden_host, 
     FH_CHECK_LAUNCH(cudaMemcpyAsync(out_ids_host, dev_out, (size_t)rows * sizeof(int64_t),
                                     cudaMemcpyDeviceToHost, s),
                     "id copy to the host");
+  if (watch) {
+    // bounded spin (then the stream synchronisation below reports any error)
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t it = 0;; ++it) {
+      int r = 0;
+      while (r < rows && watch[r] != -1) ++r;
+      if (r == rows) {
+        std::atomic_thread_fence(std::memory_order_acquire);
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q == cudaSuccess || q == cudaErrorNotReady) return FH_OK;
+        return fail(FH_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
+      }
+      if ((it & 1023u) == 1023u &&
+          std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(kHostSpinMs))
+        break;
+    }
+  }
   FH_CHECK_LAUNCH(cudaStreamSynchronize(s), "stream synchronisation");
   return FH_OK;
 }

@@ -162,10 +162,14 @@ FH_API int fh_get_next_token(const fh_head *head, const void *hidden, int rows,
 /*
  * Greedy next token with HOST buffers: hidden_host [rows, hidden],
  * out_ids_host [rows] int64. The call brings the hidden states to the device,
- * runs fh_get_next_token on the workspace, returns the ids and synchronises
- * `stream` before returning. Page-locked buffers are read and written by the
- * kernels directly (a small copy kernel in, the step's own id stores out);
- * pageable ones go through cudaMemcpyAsync.
+ * runs fh_get_next_token on the workspace and returns once the ids are in
+ * out_ids_host. Page-locked buffers are read and written by the kernels
+ * directly (a small copy kernel in, the step's own id stores out): the call
+ * marks out_ids_host with -1 and returns as soon as every row has been
+ * overwritten, possibly before the kernel's last instructions retire (later
+ * work on `stream` is ordered after it; reuse the workspace on the same
+ * stream); after 20 ms it falls back to synchronising `stream`. Pageable
+ * buffers go through cudaMemcpyAsync and a stream synchronisation.
  * For C and C++ callers that keep the decode state on the host; the
  * reference's get_next_token (flash_head.py:277-334) takes device tensors.
  * The workspace must hold fh_workspace_bytes_host(head, rows) bytes (the
