@@ -603,8 +603,9 @@ def run_single(args, dist):
         "sweep": out_sweep,
         "e2e": {"value": rows / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "us_per_step": e2e_s * 1e6,
-                "path": "C-ABI fh_get_next_token_host: pinned host buffers, copies and stream "
-                        "sync inside the call"},
+                "path": "C-ABI fh_get_next_token_host: pinned host buffers read and written "
+                        "by the kernels over the bus; the call returns once every id is in "
+                        "host memory"},
         "gpu_launches": launches * args.steps,
         "step_kernels": launches,
         "clocks": clocks,
