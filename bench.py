@@ -382,7 +382,8 @@ def measure_library_dense(reps, pool, rows, steps, warmup, dist, sample=False, t
 def measure_e2e(reps, rows, steps, warmup, dist, D):
     """Through the C-ABI call with host buffers (fh_get_next_token_host): per
     step the library brings the pinned host hidden states to the device, runs
-    the step, returns the ids to pinned host memory and synchronises."""
+    the step and returns once the ids are in pinned host memory (the next
+    call is issued only then)."""
     import torch
 
     from flash_head import _lib
