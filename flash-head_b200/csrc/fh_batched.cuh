@@ -320,4 +320,156 @@ __global__ void k_inv_finalize(unsigned long long *packed, int rows, int64_t *ou
   }
 }
 
+// ---------------------------------------------------------------------------
+// Stage 2 of the few-row steps (greedy or sampled), streamed: a persistent
+// grid whose warps each take a contiguous range of w_perm rows to score (the
+// rows of every (row, probe) item in item order, then the special tokens'
+// rows) and keep kS2sSlots whole-row bulk copies in flight into their own
+// shared-memory slots, so an SM has 2-3 rows per warp on the way instead of
+// one register-resident row per warp. A warp keeps the running best packed
+// (key, vocab id) of its current hidden row and folds it into packed[row]
+// with one atomicMax when the row changes; the last CTA publishes (as
+// k_stage2 does). The hidden row is read through L1.
+// ---------------------------------------------------------------------------
+constexpr int kS2sSlots = 3;
+constexpr int kS2sSmemBudget = 192 * 1024;
+
+__host__ __device__ __forceinline__ int s2s_warps(int D) {
+  const int rb = D * 2;
+  const int w = kS2sSmemBudget / (kS2sSlots * rb);
+  return w < 1 ? 1 : (w > 16 ? 16 : w);
+}
+__host__ __device__ __forceinline__ size_t s2s_smem_bytes(int D) {
+  const int nw = s2s_warps(D);
+  return (size_t)nw * kS2sSlots * ((size_t)D * 2) + (size_t)nw * kS2sSlots * (8 + 8) + 128;
+}
+
+template <typename HT, typename IdxT, bool SAMPLE>
+__global__ void __launch_bounds__(512, 1)
+    k_stage2_stream(Stage2Args a, long long items, uint32_t *err, uint32_t polls) {
+  extern __shared__ __align__(128) unsigned char s2s[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const size_t rb = (size_t)a.D * sizeof(HT);
+  unsigned char *ring = s2s + (size_t)warp * kS2sSlots * rb;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(s2s + (size_t)nw * kS2sSlots * rb) +
+                   warp * kS2sSlots;
+  long long *desc = reinterpret_cast<long long *>(
+                        s2s + (size_t)nw * kS2sSlots * rb + (size_t)nw * kS2sSlots * 8) +
+                    warp * kS2sSlots;
+  if (lane == 0) {
+    for (int j = 0; j < kS2sSlots; ++j) mbar_init(&bars[j], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (a.wait_prior) grid_dep_wait();  // the probe lists come from the kernel before
+  const int ipr = a.P + a.n_special;
+  const long long n_units = items * a.cap;
+  const long long W = (long long)gridDim.x * nw, gw = (long long)blockIdx.x * nw + warp;
+  const long long u0 = gw * n_units / W, u1 = (gw + 1) * n_units / W;
+  const int n = (int)(u1 - u0);
+  // w_perm row of unit u, or -1 (an unused slot of a special item, a probe
+  // outside this head's clusters)
+  auto resolve = [&](long long u) -> long long {
+    const long long item = u / a.cap;
+    const int sl = (int)(u - item * a.cap);
+    const int r = (int)(item / ipr), j = (int)(item - (long long)r * ipr);
+    if (j < a.P) {
+      long long cid = a.dense ? (long long)j
+                              : (long long)reinterpret_cast<const IdxT *>(a.probes)[(size_t)r * a.probe_stride + j];
+      cid -= a.cluster_base;
+      return (cid >= 0 && cid < a.K) ? cid * a.cap + sl : -1;
+    }
+    if (sl != 0) return -1;
+    const long long sp = a.special_slots[j - a.P];
+    return (sp >= 0 && sp < (long long)a.K * a.cap) ? sp : -1;
+  };
+  int last_issued[kS2sSlots];  // lane 0: the last unit put in each slot, or -1
+  for (int j = 0; j < kS2sSlots; ++j) last_issued[j] = -1;
+  auto issue = [&](int k) {  // lane 0: unit u0 + k into slot k % kS2sSlots
+    const int s = k % kS2sSlots;
+    const long long row = resolve(u0 + k);
+    desc[s] = row;
+    last_issued[s] = k;
+    if (row >= 0) {
+      fence_proxy_async_smem();
+      mbar_expect_tx(&bars[s], (uint32_t)rb);
+      bulk_g2s(ring + (size_t)s * rb, reinterpret_cast<const char *>(a.w_perm) + (size_t)row * rb,
+               (uint32_t)rb, &bars[s]);
+    } else {
+      mbar_expect_tx(&bars[s], 0u);
+    }
+  };
+  if (lane == 0)
+    for (int k = 0; k < min(n, kS2sSlots); ++k) issue(k);
+  __syncwarp();
+  bool ok = true;
+  int cur_r = -1;
+  unsigned long long best = 0ull;
+  const int nvec = a.D / 8;
+  for (int k = 0; k < n; ++k) {
+    const int s = k % kS2sSlots;
+    if (ok) {
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bars[s], (uint32_t)((k / kS2sSlots) & 1), polls));
+      if (!ok && lane == 0) atomicOr(err, kErrCopyTimeout);
+    }
+    const long long u = u0 + k;
+    const int r = (int)(u / a.cap / ipr);
+    if (r != cur_r) {
+      if (lane == 0 && cur_r >= 0 && best) atomicMax(&a.packed[cur_r], best);
+      best = 0ull;
+      cur_r = r;
+    }
+    const long long row = desc[s];
+    if (ok && row >= 0) {
+      const unsigned char *wr = ring + (size_t)s * rb;
+      const char *hr = reinterpret_cast<const char *>(a.hidden) + (size_t)r * rb;
+      float acc = 0.f;
+#pragma unroll 4
+      for (int v = lane; v < nvec; v += 32) {
+        const uint4 wv = *reinterpret_cast<const uint4 *>(wr + (size_t)v * 16);
+        const uint4 hv = ldg_keep(hr + (size_t)v * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 w2 = pair_to_float2<HT>(wv, q);
+          const float2 h2 = pair_to_float2<HT>(hv, q);
+          acc = fmaf(w2.x, h2.x, acc);
+          acc = fmaf(w2.y, h2.y, acc);
+        }
+      }
+      acc = warp_sum(acc);
+      const uint32_t vid = (uint32_t)reinterpret_cast<const IdxT *>(a.vocab_map)[row];
+      float key = acc;
+      if (SAMPLE) key = acc / a.temperature + gumbel(a.rng, kStageTokens, (uint32_t)(a.row_base + r), vid);
+      const unsigned long long w = pack(key, vid);
+      best = w > best ? w : best;
+    }
+    __syncwarp();  // the slot is read: refill it
+    if (lane == 0 && ok && k + kS2sSlots < n) issue(k + kS2sSlots);
+    __syncwarp();
+  }
+  if (lane == 0 && cur_r >= 0 && best) atomicMax(&a.packed[cur_r], best);
+  if (lane == 0 && !ok)  // after a timeout: no copy of this warp may still be writing
+    for (int j = 0; j < kS2sSlots; ++j)
+      if (last_issued[j] >= 0) mbar_wait(&bars[j], (uint32_t)((last_issued[j] / kS2sSlots) & 1), polls);
+  if (a.counter == nullptr) return;
+  // Last CTA to finish publishes the winners (flag after the descriptors).
+  unsigned *s_last = reinterpret_cast<unsigned *>(
+      s2s + (size_t)nw * kS2sSlots * rb + (size_t)nw * kS2sSlots * 16);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    *s_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (*s_last) {
+    __threadfence();
+    for (int r = threadIdx.x; r < a.rows; r += blockDim.x) {
+      const unsigned long long w = atomicExch(&a.packed[r], 0ull);
+      if (a.out_ids) a.out_ids[r] = w ? (int64_t)packed_id(w) : (int64_t)0xFFFFFFFFll;
+      if (a.out_signed) a.out_signed[r] = to_signed(w);
+    }
+    if (threadIdx.x == 0) *a.counter = 0u;
+  }
+}
+
 }  // namespace fh

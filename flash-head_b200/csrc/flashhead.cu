@@ -356,6 +356,34 @@ cudaError_t launch_scores(int hdt, int wdt, const fh::ScoresArgs &a, cudaStream_
 
 template <typename HT, typename IdxT, int MODE>
 cudaError_t launch_stage2_t(const fh::Stage2Args &a, int items, cudaStream_t s, bool pdl) {
+  // steps of 5+ rows on a workspace (a last-CTA counter to publish with): the
+  // streamed kernel, one persistent CTA per SM (8 rows: 33.8 -> 31.2 us on
+  // the Llama-3.2-1B head); fewer rows and the stateless entry points keep
+  // the one-CTA-per-item kernel, which has less start-up (1 row: 7.0 us
+  // against 9.8 us streamed)
+  if constexpr (MODE == fh::kGreedy || MODE == fh::kSample) {
+    if (a.counter != nullptr && a.rows >= fh::kGemmS1MinRows && (size_t)a.D * sizeof(HT) % 16 == 0 &&
+        fh::s2s_smem_bytes(a.D) <= (size_t)fh::kS2SmemMax && sm_count() > 0) {
+      static size_t attr_bytes[128];  // dynamic shared memory allowed so far
+      auto kern = fh::k_stage2_stream<HT, IdxT, MODE == fh::kSample>;
+      const size_t need = fh::s2s_smem_bytes(a.D);
+      int dev = 0;
+      cudaError_t e = cudaGetDevice(&dev);
+      if (e != cudaSuccess) return e;
+      if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+      {
+        std::lock_guard<std::mutex> lock(g_attr_mutex);
+        if (need > attr_bytes[dev]) {
+          e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need);
+          if (e != cudaSuccess) return e;
+          attr_bytes[dev] = need;
+        }
+      }
+      return launch(kern, dim3(sm_count()), dim3(32 * fh::s2s_warps(a.D)), fh::s2s_smem_bytes(a.D),
+                    s, pdl, a, (long long)items, reinterpret_cast<uint32_t *>(a.counter) + fh::kSyncError,
+                    (uint32_t)(1u << 22));
+    }
+  }
   constexpr int U = 4;
   const int warps = a.cap < 16 ? a.cap : 16;
   return launch(fh::k_stage2<HT, IdxT, MODE, U>, dim3(items), dim3(32 * warps), 0, s, pdl, a);
