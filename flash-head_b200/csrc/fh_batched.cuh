@@ -7,7 +7,9 @@
 //                     three-kernel paths compute), then the top-p clusters.
 //   k_special_scores  the special tokens of every row into packed[row].
 //   k_inv_finalize    ids (or signed words of a shard) from packed[], then
-//                     packed[] reset.
+//                     packed[] reset (after the dense kernel).
+//   k_stage2_stream   stage 2 of the 5..15-row steps: per-warp rings of
+//                     whole-row bulk copies over the probed w_perm rows.
 #pragma once
 
 #include "fh_fused.cuh"
