@@ -351,7 +351,10 @@ def test_sampling_distribution_qwen_1e5(stage1):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("do_sample", [False, True])
-def test_tp_shards_reproduce_unsharded(llama1b_heads, world, do_sample):
+@pytest.mark.parametrize("rows", [6, 16])
+def test_tp_shards_reproduce_unsharded(llama1b_heads, world, do_sample, rows):
+    """6 rows score the owned probes with the streamed few-row stage 2, 16
+    rows with the cluster-major tensor-core stage 2."""
     from flash_head.native import NativeHead, derive_buffers, shard_buffers
     from flash_head.synthetic import make_hidden
     from flash_head.tp import cluster_range
@@ -363,7 +366,7 @@ def test_tp_shards_reproduce_unsharded(llama1b_heads, world, do_sample):
         lo, hi = cluster_range(fh._K, world, r)
         shards.append(NativeHead(shard_buffers(full, fh._cap, lo, hi), fh._D, fh._cap,
                                  fh.n_probes, cluster_base=lo))
-    H = make_hidden(16, fh._D, seed=31, device="cuda")
+    H = make_hidden(rows, fh._D, seed=31, device="cuda")
     kw = dict(do_sample=do_sample, temperature=0.8, seed=99, offset=3)
     cands = torch.stack([sh.tp_local_candidates(H, **kw) for sh in shards])
     bests = torch.stack([sh.tp_select_and_score(H, cands, world, **kw) for sh in shards])
